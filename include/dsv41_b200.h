@@ -1,0 +1,114 @@
+/* C ABI of the DeepSeek-V4.1 decode / verify monokernel backend for B200 (sm_100a).
+ *
+ * Every entry point takes a POD argument struct whose fields are all 64-bit (device
+ * pointers as int64, sizes and flags as int64), plus a cudaStream_t passed as void*, and
+ * returns 0 or a negative DSV41_E* status. Nothing throws across the boundary; nothing
+ * allocates device memory: scratch is caller-owned, sized by the *_scratch_bytes queries.
+ * Launches go on the given stream only, so every call is CUDA-graph capturable.
+ *
+ * The reference (omirosh/sgl-amd-mono) binds the same launches through its FlyDSL JIT
+ * entry points, which take raw int64 device pointers and a stream; each declaration below
+ * names the reference interface it replaces (file:line in the reference).
+ */
+#ifndef DSV41_B200_H
+#define DSV41_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DSV41_OK 0
+#define DSV41_EINVAL (-1)   /* an argument is out of range or misaligned */
+#define DSV41_ELAUNCH (-2)  /* a CUDA launch failed (cudaGetLastError) */
+#define DSV41_ESCRATCH (-3) /* the caller's scratch is smaller than required */
+#define DSV41_EDEVICE (-4)  /* a device-side guard fired (deadline, peer failure) */
+
+/* Library version and the compute capability it was built for (100 for sm_100a). */
+int dsv41_version(void);
+int dsv41_arch(void);
+
+/* ---------------------------------------------------------------- FP8 GEMV
+ * y[m][n] = sum_k x[m][k] * dequant(W)[n][k] in fp32: W e4m3 [N, K] row-major with one
+ * E8M0 code per 128 x 128 block, x bf16 [M, x_ld]. Rows n use x columns
+ * (n / x_group_rows) * K .. + K (a grouped projection, wo_a); x_group_rows = 0: N.
+ * Replaces the GEMV tiles of attention/gemv.py:141-194 (chain_mfmas), stages/gemv.py:182-214. */
+typedef struct {
+  int64_t w, codes, x, y;             /* device pointers */
+  int64_t M, N, K, x_ld, x_group_rows;
+  int64_t scratch, scratch_bytes;     /* caller-owned device scratch */
+} Dsv41GemvArgs;
+int64_t dsv41_gemv_fp8_scratch_bytes(const Dsv41GemvArgs* a);
+int dsv41_gemv_fp8(const Dsv41GemvArgs* a, void* stream);
+
+/* ---------------------------------------------------------------- MXFP4 expert relayout
+ * One-time copy of routed-expert weights from the checkpoint layout -- w [E, N, K/2] E2M1
+ * (even K in the low nibble) with E8M0 codes [E, N, K/32] -- into the kernels' fragment
+ * order (dst [E*N*K/2] bytes, dst_codes [E*N*K/32]). N % 16 == 0, K % 128 == 0.
+ * Replaces the reader of aiter's shuffle_weight / shuffle_scale layout (common/mx.py:35-50,
+ * stages/moe.py:567-607); the runner logs the copy as the reference logs its copies
+ * (deepseek_v41/spec.py:34-41). */
+typedef struct {
+  int64_t src, src_codes, dst, dst_codes;
+  int64_t E, N, K;
+} Dsv41RelayoutArgs;
+int dsv41_relayout_mxfp4(const Dsv41RelayoutArgs* a, void* stream);
+
+/* ---------------------------------------------------------------- K1
+ * The attention seam and front of one layer (gfx950/layer.py:189-468, launch args
+ * layer.py:223-263; host runner.py:512-622): mHC seam, wqkv_a GEMV, q_norm -> MXFP8 q,
+ * kv_norm + RoPE -> the FP8 KV record at the row's slot, the key table for K2, wq_b GEMV +
+ * RoPE -> q. Shapes: hidden % 256 == 0; q_lora in {256, 512, 1024}; nope % 64 == 0,
+ * rope == 64; heads * (nope + rope) % 16 == 0. Inputs and outputs are row-major. */
+typedef struct {
+  int64_t M, hidden, q_lora, nope, rope, heads, swa_width, topk_width;
+  int64_t fold, first, index, build_kt;
+  /* seam */
+  int64_t res_in, x_in, post_in, comb_in, pre_in, hc_fn, hc_scale, hc_base, norm_w;
+  int64_t res_out, post_out, comb_out, pre_out, normed, x8, x8s;
+  /* projections, norms, positions */
+  int64_t wqkv, wqkv_codes, q_norm, kv_norm, cos_sin, pos;
+  /* KV store */
+  int64_t slot, cache, page_stride, blk;
+  /* key table */
+  int64_t swa_idx, swa_lens, topk_idx, topk_lens, kt, klen;
+  /* wq_b and outputs */
+  int64_t wqb, wqb_codes, q, qr, qx8, qx8s, qkv_out;
+  int64_t scratch, scratch_bytes;
+} Dsv41K1Args;
+int64_t dsv41_k1_scratch_bytes(const Dsv41K1Args* a);
+int dsv41_k1(const Dsv41K1Args* a, void* stream);
+
+/* ---------------------------------------------------------------- K2
+ * The attention core, wo_a, wo_b, the attention all-reduce, the FFN seam, the router and
+ * routing, the shared and routed experts and the MoE all-reduce of one layer
+ * (gfx950/layer.py:773-1072, launch args layer.py:802-854; host runner.py:624-728).
+ * route_softmax = 1: softmax top-k routing; 0: sqrtsoftplus + bias, renormalized x 1.5.
+ * tp > 1: peer_parts / peer_moe point at device tables of tp pointers (each rank's
+ * symmetric bf16 [M, hidden] buffer) and the all-reduces go through peer memory. */
+typedef struct {
+  int64_t M, hidden, nope, rope, heads, o_groups, o_rank;
+  int64_t experts, topk, inter, shared_inter, route_softmax, tp, rank, keys_ld;
+  /* attention */
+  int64_t q, kt, klen, swa, swa_stride, swa_blk, comp, comp_stride, comp_blk, sink, cos_sin, pos;
+  int64_t woa, woa_codes, wob, wob_codes;
+  /* FFN seam */
+  int64_t res_in, post_in, comb_in, pre_in, hc_fn, hc_scale, hc_base, norm_w;
+  int64_t res_out, post_out, comb_out, pre_out, normed;
+  /* MoE */
+  int64_t gate_w, bias, w13, w13_codes, w2, w2_codes, sgu, sgu_codes, sw2, sw2_codes;
+  /* outputs (xo, x8b, x8bs, attn_part, attn, logits: optional inspection copies) */
+  int64_t out, ids, wts, xo, x8b, x8bs, attn_part, attn, logits, moe_part;
+  /* tensor parallelism */
+  int64_t peer_attn, peer_moe, peer_flags, epoch, deadline_ns;
+  int64_t scratch, scratch_bytes;
+} Dsv41K2Args;
+int64_t dsv41_k2_scratch_bytes(const Dsv41K2Args* a);
+int dsv41_k2(const Dsv41K2Args* a, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSV41_B200_H */

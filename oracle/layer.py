@@ -110,9 +110,30 @@ def q_path(qkv_q, q_norm_w):
     return ys, q8, q8s
 
 
+def butterfly32(lanes):
+    """The value an xor-butterfly (16, 8, 4, 2, 1) of fp64 lane values [..., 32] leaves."""
+    for d in (16, 8, 4, 2, 1):
+        lanes = lanes[..., :d] + lanes[..., d:2 * d]
+    return lanes[..., 0]
+
+
+def sumsq_fixed(x):
+    """fp64 sum of squares of the rows of x [M, D] (D a multiple of 64) in the kernel's order:
+    lane i of 64 sums x[i + 64 r]^2 over r sequentially; each 32-lane half folds by an
+    xor-butterfly; the two halves add. Exact products, so only the order is pinned."""
+    M, D = x.shape
+    v = x.double().numpy() ** 2
+    v = v.reshape(M, D // 64, 64)
+    acc = np.zeros((M, 64))
+    for r in range(D // 64):
+        acc = acc + v[:, r, :]
+    w = acc.reshape(M, 2, 32)
+    return torch.from_numpy(butterfly32(w[:, 0]) + butterfly32(w[:, 1]))
+
+
 def kv_record(qkv_kv, kv_norm_w, cos, sin, nope):
     """The FP8 KV record of each row (``front.py:246-300``), bit-exact contract:
-    x = bf16(kv); ss = fp32(sum of x^2 accumulated in fp64); ms = fp32(ss / D) + eps;
+    x = bf16(kv); ss = fp32(sum of x^2 in fp64, in ``sumsq_fixed``'s order); ms = fp32(ss / D) + eps;
     r = 1 / sqrt(ms) (IEEE fp32, two roundings); k = (x r) w (fp32, two roundings);
     GPT-J RoPE of the dims past ``nope``: e0 = k0 c - k1 s, e1 = k0 s + k1 c (separate
     fp32 products, then the sum); per 64 nope dims: code = code_ceil(max(amax, 1e-4) / 448),
@@ -120,7 +141,7 @@ def kv_record(qkv_kv, kv_norm_w, cos, sin, nope):
     [M, 2 * rope] u8, codes [M, nope / 64] u8)."""
     x = bf(qkv_kv)
     M, D = x.shape
-    ss = (x.double() ** 2).sum(1).float()
+    ss = sumsq_fixed(x).float()
     ms = ss / torch.tensor(float(D), dtype=torch.float32) + torch.tensor(RMS_EPS, dtype=torch.float32)
     r = torch.tensor(1.0, dtype=torch.float32) / torch.sqrt(ms)
     k = (x * r[:, None]) * f32(kv_norm_w)

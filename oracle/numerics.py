@@ -141,8 +141,8 @@ def mxfp8_dequant(q: torch.Tensor, code: torch.Tensor) -> torch.Tensor:
 # ---------------------------------------------------------------- FP8 block-scaled / MXFP4 weights
 def deq_fp8_block(w8: torch.Tensor, codes: torch.Tensor, rb: int, cb: int) -> torch.Tensor:
     """e4m3 [N, K] with E8M0 codes per (rb x cb) block -> fp32 (``check_ffn.py:118-121``)."""
-    s = pow2(codes.int())
-    return e4m3_decode(w8) * s.repeat_interleave(rb, 0).repeat_interleave(cb, 1)
+    s = pow2(codes.int()).repeat_interleave(rb, 0).repeat_interleave(cb, 1)
+    return e4m3_decode(w8) * s[: w8.shape[0], : w8.shape[1]]
 
 
 def deq_fp4(packed: torch.Tensor, codes: torch.Tensor) -> torch.Tensor:

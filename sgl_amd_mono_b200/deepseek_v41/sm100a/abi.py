@@ -1,0 +1,45 @@
+"""ctypes mirrors of the C-ABI argument structs (``include/dsv41_b200.h``), field for field;
+``tests/test_abi.py`` checks them against the header."""
+
+from __future__ import annotations
+
+from ...common.ext import struct
+
+GemvArgs = struct("Dsv41GemvArgs", [
+    "w", "codes", "x", "y", "M", "N", "K", "x_ld", "x_group_rows", "scratch", "scratch_bytes",
+])
+
+RelayoutArgs = struct("Dsv41RelayoutArgs", ["src", "src_codes", "dst", "dst_codes", "E", "N", "K"])
+
+K1Args = struct("Dsv41K1Args", [
+    "M", "hidden", "q_lora", "nope", "rope", "heads", "swa_width", "topk_width",
+    "fold", "first", "index", "build_kt",
+    "res_in", "x_in", "post_in", "comb_in", "pre_in", "hc_fn", "hc_scale", "hc_base", "norm_w",
+    "res_out", "post_out", "comb_out", "pre_out", "normed", "x8", "x8s",
+    "wqkv", "wqkv_codes", "q_norm", "kv_norm", "cos_sin", "pos",
+    "slot", "cache", "page_stride", "blk",
+    "swa_idx", "swa_lens", "topk_idx", "topk_lens", "kt", "klen",
+    "wqb", "wqb_codes", "q", "qr", "qx8", "qx8s", "qkv_out",
+    "scratch", "scratch_bytes",
+])
+
+K2Args = struct("Dsv41K2Args", [
+    "M", "hidden", "nope", "rope", "heads", "o_groups", "o_rank",
+    "experts", "topk", "inter", "shared_inter", "route_softmax", "tp", "rank", "keys_ld",
+    "q", "kt", "klen", "swa", "swa_stride", "swa_blk", "comp", "comp_stride", "comp_blk", "sink",
+    "cos_sin", "pos",
+    "woa", "woa_codes", "wob", "wob_codes",
+    "res_in", "post_in", "comb_in", "pre_in", "hc_fn", "hc_scale", "hc_base", "norm_w",
+    "res_out", "post_out", "comb_out", "pre_out", "normed",
+    "gate_w", "bias", "w13", "w13_codes", "w2", "w2_codes", "sgu", "sgu_codes", "sw2", "sw2_codes",
+    "out", "ids", "wts", "xo", "x8b", "x8bs", "attn_part", "attn", "logits", "moe_part",
+    "peer_attn", "peer_moe", "peer_flags", "epoch", "deadline_ns",
+    "scratch", "scratch_bytes",
+])
+
+STRUCTS = {
+    "Dsv41GemvArgs": GemvArgs,
+    "Dsv41RelayoutArgs": RelayoutArgs,
+    "Dsv41K1Args": K1Args,
+    "Dsv41K2Args": K2Args,
+}

@@ -1,0 +1,448 @@
+// extern "C" entry points (include/dsv41_b200.h): argument checks, scratch carving, and the
+// launch sequences of K1 and K2. Every launch goes on the caller's stream with programmatic
+// dependent launch, so a kernel's CTAs are resident (and its weight-independent prologue runs)
+// while the previous kernel drains; each kernel waits (griddepcontrol.wait) before reading
+// what the previous one wrote.
+#include <cstdio>
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+
+#include "../../../../include/dsv41_b200.h"
+#include "attention.cuh"
+#include "common.cuh"
+#include "epilogue.cuh"
+#include "front.cuh"
+#include "gemv.cuh"
+#include "moe.cuh"
+#include "seam.cuh"
+
+using namespace dsv41;
+
+namespace {
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cached[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+bool use_pdl() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("DSV41_PDL");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    fprintf(stderr, "dsv41: launch failed: %s\n", cudaGetErrorString(e));
+    return DSV41_ELAUNCH;
+  }
+  return DSV41_OK;
+}
+
+template <typename Kern, typename Args>
+cudaError_t launch(Kern kernel, dim3 grid, dim3 block, int smem, cudaStream_t st, const Args& args) {
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = use_pdl() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args);
+}
+
+// y[m][n] = sum over K slices of partials p[ks][m][n], in slice order.
+__global__ void sum_slices_kernel(const float* __restrict__ p, float* __restrict__ y, int slices,
+                                  int total) {
+  pdl_wait();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    float v = p[i];
+    for (int s = 1; s < slices; ++s) v += p[(size_t)s * total + i];
+    y[i] = v;
+  }
+  pdl_launch();
+}
+
+// Bump allocation over the caller's scratch; with a null base it only measures.
+struct Carver {
+  uint8_t* base;
+  int64_t off = 0;
+  template <class T>
+  T* take(int64_t count) {
+    off = (off + 255) & ~(int64_t)255;
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += count * (int64_t)sizeof(T);
+    return p;
+  }
+};
+
+template <class T>
+T* ptr(int64_t v) {
+  return reinterpret_cast<T*>(v);
+}
+
+int grid_for(int64_t work, int per_block) {
+  int64_t g = (work + per_block - 1) / per_block;
+  if (g < 1) g = 1;
+  if (g > 4 * 148 * 8) g = 4 * 148 * 8;
+  return (int)g;
+}
+
+#define DSV41_TRY(expr)                       \
+  do {                                        \
+    if ((expr) != cudaSuccess) return launch_status(); \
+  } while (0)
+
+// ------------------------------------------------------------------ GEMV entry
+GemvArgs plan_of(const Dsv41GemvArgs* a, float* out) {
+  return gemv_plan(ptr<const uint8_t>(a->w), ptr<const uint8_t>(a->codes),
+                   ptr<const __nv_bfloat16>(a->x), out, (int)a->M, (int)a->N, (int)a->K,
+                   (int)a->x_ld, (int)a->x_group_rows, sm_count());
+}
+
+bool gemv_args_ok(const Dsv41GemvArgs* a) {
+  return a && a->w && a->codes && a->x && a->y && a->M >= 1 && a->M <= 48 && a->N >= 1 &&
+         a->K >= 128 && a->K % 128 == 0 && a->x_ld >= a->K && a->x_ld % 4 == 0 &&
+         (a->x_group_rows == 0 || (a->x_group_rows % 16 == 0 && a->N % a->x_group_rows == 0)) &&
+         a->w % 16 == 0 && a->x % 8 == 0;
+}
+
+// ------------------------------------------------------------------ K1
+bool k1_ok(const Dsv41K1Args* a) {
+  if (!a || a->M < 1 || a->M > 48 || a->hidden % 256 || a->hidden > 16384) return false;
+  if (!(a->q_lora == 256 || a->q_lora == 512 || a->q_lora == 1024)) return false;
+  if (a->nope % 64 || a->rope != 64 || a->nope < 64 || a->nope > 512) return false;
+  if (a->heads < 1 || (a->heads * (a->nope + a->rope)) % 16) return false;
+  if (!a->res_in || !a->hc_fn || !a->norm_w || !a->wqkv || !a->wqb || !a->q || !a->cache) return false;
+  if (a->fold && (!a->x_in || !a->post_in || !a->comb_in)) return false;
+  if (!a->first && !a->pre_in) return false;
+  if (a->build_kt && (!a->kt || !a->klen || !a->swa_idx || !a->swa_lens)) return false;
+  if (a->build_kt && a->topk_width > 0 && (!a->topk_idx || !a->topk_lens)) return false;
+  if (a->index && !a->qr) return false;
+  if (a->hidden % 128 || a->q_lora % 128) return false;
+  return true;
+}
+
+int k1_run(const Dsv41K1Args* a, cudaStream_t st, bool go, int64_t* need) {
+  if (!k1_ok(a)) return DSV41_EINVAL;
+  const int M = (int)a->M, H = (int)a->hidden, QL = (int)a->q_lora;
+  const int nope = (int)a->nope, rope = (int)a->rope, D = nope + rope, heads = (int)a->heads;
+  const int QKV = QL + D;
+  const int sms = sm_count();
+  Carver c{go ? ptr<uint8_t>(a->scratch) : nullptr};
+  auto* lin = c.take<__nv_bfloat16>((int64_t)M * H);
+  auto* part = c.take<float>((int64_t)M * (H / 32) * kPart);
+  auto* xq = c.take<__nv_bfloat16>((int64_t)M * H);
+  auto* x8 = a->x8 ? ptr<uint8_t>(a->x8) : c.take<uint8_t>((int64_t)M * H);
+  auto* x8s = a->x8s ? ptr<uint8_t>(a->x8s) : c.take<uint8_t>((int64_t)M * H / 32);
+  auto* normed = a->normed ? ptr<__nv_bfloat16>(a->normed) : c.take<__nv_bfloat16>((int64_t)M * H);
+  auto* res_out = a->res_out ? ptr<__nv_bfloat16>(a->res_out) : c.take<__nv_bfloat16>((int64_t)M * 4 * H);
+  auto* post_out = a->post_out ? ptr<float>(a->post_out) : c.take<float>(M * 4);
+  auto* comb_out = a->comb_out ? ptr<float>(a->comb_out) : c.take<float>(M * 16);
+  auto* pre_out = a->pre_out ? ptr<float>(a->pre_out) : c.take<float>(M * 4);
+  GemvArgs g1 = gemv_plan(ptr<const uint8_t>(a->wqkv), ptr<const uint8_t>(a->wqkv_codes), xq, nullptr,
+                          M, QKV, H, H, 0, sms);
+  g1.out = c.take<float>((int64_t)g1.kslices * M * QKV);
+  auto* qxq = c.take<__nv_bfloat16>((int64_t)M * QL);
+  auto* qx8 = a->qx8 ? ptr<uint8_t>(a->qx8) : c.take<uint8_t>((int64_t)M * QL);
+  auto* qx8s = a->qx8s ? ptr<uint8_t>(a->qx8s) : c.take<uint8_t>((int64_t)M * QL / 32);
+  GemvArgs g2 = gemv_plan(ptr<const uint8_t>(a->wqb), ptr<const uint8_t>(a->wqb_codes), qxq, nullptr,
+                          M, heads * D, QL, QL, 0, sms);
+  g2.out = c.take<float>((int64_t)g2.kslices * M * heads * D);
+  *need = c.off;
+  if (!go) return DSV41_OK;
+  if (!a->scratch || a->scratch_bytes < c.off) return DSV41_ESCRATCH;
+
+  SeamArgs s = {};
+  s.M = M; s.H = H; s.fold = (int)a->fold; s.first = (int)a->first; s.aiter = 0;
+  s.res_in = ptr<const __nv_bfloat16>(a->res_in); s.x = ptr<const __nv_bfloat16>(a->x_in);
+  s.post_in = ptr<const float>(a->post_in); s.comb_in = ptr<const float>(a->comb_in);
+  s.pre_in = ptr<const float>(a->pre_in); s.hc_fn = ptr<const float>(a->hc_fn);
+  s.hc_scale = ptr<const float>(a->hc_scale); s.hc_base = ptr<const float>(a->hc_base);
+  s.norm_w = ptr<const __nv_bfloat16>(a->norm_w);
+  s.res_out = res_out; s.pre_out = pre_out; s.post_out = post_out; s.comb_out = comb_out;
+  s.normed = normed; s.x8 = x8; s.x8s = x8s; s.xq = xq; s.lin = lin; s.part = part;
+  DSV41_TRY(launch(seam_slice_kernel, dim3(H / kSliceCols), dim3(256), 0, st, s));
+  DSV41_TRY(launch(seam_gate_norm_kernel, dim3(M), dim3(256), 0, st, s));
+  DSV41_TRY(gemv_launch(g1, st, use_pdl()));
+  FrontArgs f = {};
+  f.M = M; f.QL = QL; f.KVD = D; f.nope = nope; f.rope = rope; f.kslices = g1.kslices;
+  f.index = (int)a->index; f.qkv_part = g1.out;
+  f.q_norm_w = ptr<const __nv_bfloat16>(a->q_norm); f.kv_norm_w = ptr<const __nv_bfloat16>(a->kv_norm);
+  f.cos_sin = ptr<const float>(a->cos_sin); f.pos = ptr<const int64_t>(a->pos);
+  f.slot = ptr<const int64_t>(a->slot); f.cache = ptr<uint8_t>(a->cache);
+  f.page_stride = a->page_stride; f.blk = (int)a->blk;
+  f.qr = ptr<__nv_bfloat16>(a->qr); f.qx8 = qx8; f.qx8s = qx8s; f.qxq = qxq;
+  f.qkv_out = ptr<float>(a->qkv_out);
+  DSV41_TRY(launch(front_qkv_kernel, dim3(M), dim3(256), 0, st, f));
+  if (a->build_kt) {
+    KeyTableArgs k = {};
+    k.M = M; k.swa_width = (int)a->swa_width; k.topk_width = (int)a->topk_width;
+    k.slot = ptr<const int64_t>(a->slot); k.swa_idx = ptr<const int32_t>(a->swa_idx);
+    k.swa_lens = ptr<const int32_t>(a->swa_lens); k.topk = ptr<const int32_t>(a->topk_idx);
+    k.topk_lens = ptr<const int32_t>(a->topk_lens); k.kt = ptr<int32_t>(a->kt);
+    k.klen = ptr<int32_t>(a->klen);
+    DSV41_TRY(launch(key_table_kernel, dim3(M), dim3(256), 0, st, k));
+  }
+  DSV41_TRY(gemv_launch(g2, st, use_pdl()));
+  QRopeArgs qr = {};
+  qr.M = M; qr.heads = heads; qr.D = D; qr.nope = nope; qr.rope = rope; qr.kslices = g2.kslices;
+  qr.part = g2.out; qr.cos_sin = ptr<const float>(a->cos_sin); qr.pos = ptr<const int64_t>(a->pos);
+  qr.q = ptr<__nv_bfloat16>(a->q);
+  DSV41_TRY(launch(q_rope_kernel, dim3(cdiv(heads * D / 2, 256), M), dim3(256), 0, st, qr));
+  return launch_status();
+}
+
+// ------------------------------------------------------------------ K2
+bool k2_ok(const Dsv41K2Args* a) {
+  if (!a || a->M < 1 || a->M > 48 || a->hidden % 256 || a->hidden > 16384) return false;
+  if (a->nope % 64 || a->rope != 64 || a->nope > 512 || a->heads < 1) return false;
+  if (a->o_groups < 1 || a->o_rank % 128 || a->heads % a->o_groups) return false;
+  if (((a->heads / a->o_groups) * (a->nope + a->rope)) % 128) return false;
+  if (a->experts < 1 || a->experts > 512 || a->topk < 1 || a->topk > 32) return false;
+  if (a->inter % 128 || a->shared_inter % 128 || a->tp != 1) return false;
+  if (!a->q || !a->kt || !a->klen || !a->swa || !a->sink || !a->woa || !a->wob) return false;
+  if (!a->res_in || !a->post_in || !a->comb_in || !a->pre_in || !a->hc_fn || !a->norm_w) return false;
+  if (!a->gate_w || !a->w13 || !a->w2 || !a->sgu || !a->sw2 || !a->out || !a->ids || !a->wts) return false;
+  if (!a->route_softmax && !a->bias) return false;
+  if (a->hidden % 1024 && a->hidden > 1024) return false;
+  return true;
+}
+
+struct K2Plan {
+  int head_tiles, nchunks, chunk_keys;
+  GemvArgs ga, gb, gs, gd;
+  ExpertArgs eu, ed;
+};
+
+int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
+  if (!k2_ok(a)) return DSV41_EINVAL;
+  const int M = (int)a->M, H = (int)a->hidden, nope = (int)a->nope, rope = (int)a->rope;
+  const int D = nope + rope, heads = (int)a->heads, G = (int)a->o_groups, O = (int)a->o_rank;
+  const int E = (int)a->experts, TK = (int)a->topk, I = (int)a->inter, SI = (int)a->shared_inter;
+  const int P = M * TK, keys = (int)a->keys_ld;
+  const int sms = sm_count();
+  Carver c{go ? ptr<uint8_t>(a->scratch) : nullptr};
+  // attention split plan
+  const int head_tiles = cdiv(heads, 16);
+  int nchunks = cdiv(2 * sms, M * head_tiles);
+  nchunks = std::max(1, std::min(nchunks, cdiv(keys, kSub)));
+  const int chunk_keys = cdiv(cdiv(keys, nchunks), kSub) * kSub;
+  nchunks = cdiv(keys, chunk_keys);
+  auto* part_o = c.take<float>((int64_t)M * nchunks * heads * D);
+  auto* part_ml = c.take<float>((int64_t)M * nchunks * heads * 2);
+  auto* xo = a->xo ? ptr<__nv_bfloat16>(a->xo) : c.take<__nv_bfloat16>((int64_t)M * heads * D);
+  const int gk = heads / G * D;  // wo_a's K a group
+  GemvArgs ga = gemv_plan(ptr<const uint8_t>(a->woa), ptr<const uint8_t>(a->woa_codes), xo, nullptr,
+                          M, G * O, gk, heads * D, O, sms);
+  ga.out = c.take<float>((int64_t)ga.kslices * M * G * O);
+  auto* x8bq = c.take<__nv_bfloat16>((int64_t)M * G * O);
+  auto* x8b = a->x8b ? ptr<uint8_t>(a->x8b) : c.take<uint8_t>((int64_t)M * G * O);
+  auto* x8bs = a->x8bs ? ptr<uint8_t>(a->x8bs) : c.take<uint8_t>((int64_t)M * G * O / 32);
+  GemvArgs gb = gemv_plan(ptr<const uint8_t>(a->wob), ptr<const uint8_t>(a->wob_codes), x8bq, nullptr,
+                          M, H, G * O, G * O, 0, sms);
+  gb.out = c.take<float>((int64_t)gb.kslices * M * H);
+  auto* attn_part = a->attn_part ? ptr<__nv_bfloat16>(a->attn_part) : c.take<__nv_bfloat16>((int64_t)M * H);
+  auto* attn = a->attn ? ptr<__nv_bfloat16>(a->attn) : c.take<__nv_bfloat16>((int64_t)M * H);
+  // FFN seam
+  auto* lin = c.take<__nv_bfloat16>((int64_t)M * H);
+  auto* spart = c.take<float>((int64_t)M * (H / 32) * kPart);
+  auto* xq = c.take<__nv_bfloat16>((int64_t)M * H);
+  auto* x8 = c.take<uint8_t>((int64_t)M * H);
+  auto* x8s = c.take<uint8_t>((int64_t)M * H / 32);
+  auto* x8r = c.take<uint8_t>((int64_t)M * H);
+  auto* x8rs = c.take<uint8_t>((int64_t)M * H / 32);
+  auto* normed = a->normed ? ptr<__nv_bfloat16>(a->normed) : c.take<__nv_bfloat16>((int64_t)M * H);
+  auto* res_out = a->res_out ? ptr<__nv_bfloat16>(a->res_out) : c.take<__nv_bfloat16>((int64_t)M * 4 * H);
+  auto* post_out = a->post_out ? ptr<float>(a->post_out) : c.take<float>(M * 4);
+  auto* comb_out = a->comb_out ? ptr<float>(a->comb_out) : c.take<float>(M * 16);
+  auto* pre_out = a->pre_out ? ptr<float>(a->pre_out) : c.take<float>(M * 4);
+  // MoE
+  auto* logits = a->logits ? ptr<float>(a->logits) : c.take<float>((int64_t)M * E);
+  auto* n_u = c.take<int32_t>(1);
+  auto* u_expert = c.take<int32_t>(E);
+  auto* u_off = c.take<int32_t>(E + 1);
+  auto* picks = c.take<int32_t>(P);
+  GemvArgs gs = gemv_plan(ptr<const uint8_t>(a->sgu), ptr<const uint8_t>(a->sgu_codes), xq, nullptr,
+                          M, 2 * SI, H, H, 0, sms);
+  gs.out = c.take<float>((int64_t)gs.kslices * M * 2 * SI);
+  auto* smq = c.take<uint8_t>((int64_t)M * SI);
+  auto* smqs = c.take<uint8_t>((int64_t)M * SI / 32);
+  auto* smx = c.take<__nv_bfloat16>((int64_t)M * SI);
+  GemvArgs gd = gemv_plan(ptr<const uint8_t>(a->sw2), ptr<const uint8_t>(a->sw2_codes), smx, nullptr,
+                          M, H, SI, SI, 0, sms);
+  gd.out = c.take<float>((int64_t)gd.kslices * M * H);
+  const int max_units = std::min(E, P);
+  ExpertArgs eu = {};
+  eu.M = M; eu.topk = TK; eu.N = 2 * I; eu.K = H; eu.ks_len = std::min(H, 1024);
+  eu.kslices = cdiv(H, eu.ks_len); eu.row_groups = cdiv(2 * I / 16, 8); eu.max_units = max_units;
+  eu.w = ptr<const uint8_t>(a->w13); eu.ws = ptr<const uint8_t>(a->w13_codes);
+  eu.x = x8r; eu.xs = x8rs; eu.x_by_pick = 0;
+  eu.n_u = n_u; eu.u_expert = u_expert; eu.u_off = u_off; eu.picks = picks;
+  eu.out = c.take<float>((int64_t)eu.kslices * P * 2 * I);
+  auto* mid = c.take<uint8_t>((int64_t)P * I);
+  auto* mids = c.take<uint8_t>((int64_t)P * I / 32);
+  ExpertArgs ed = eu;
+  ed.N = H; ed.K = I; ed.ks_len = std::min(I, 1024); ed.kslices = cdiv(I, ed.ks_len);
+  ed.row_groups = cdiv(H / 16, 8); ed.w = ptr<const uint8_t>(a->w2); ed.ws = ptr<const uint8_t>(a->w2_codes);
+  ed.x = mid; ed.xs = mids; ed.x_by_pick = 1;
+  ed.out = c.take<float>((int64_t)ed.kslices * P * H);
+  auto* moe_part = a->moe_part ? ptr<__nv_bfloat16>(a->moe_part) : c.take<__nv_bfloat16>((int64_t)M * H);
+  *need = c.off;
+  if (!go) return DSV41_OK;
+  if (!a->scratch || a->scratch_bytes < c.off) return DSV41_ESCRATCH;
+  if (eu.ks_len % 128 || ed.ks_len % 128 || H % eu.ks_len || I % ed.ks_len) return DSV41_EINVAL;
+
+  // ---- attention
+  AttnArgs at = {};
+  at.M = M; at.heads = heads; at.D = D; at.nope = nope; at.rope = rope; at.keys_ld = keys;
+  at.nchunks = nchunks; at.chunk_keys = chunk_keys; at.head_tiles = head_tiles;
+  at.q = ptr<const __nv_bfloat16>(a->q); at.kt = ptr<const int32_t>(a->kt); at.klen = ptr<const int32_t>(a->klen);
+  at.swa = ptr<const uint8_t>(a->swa); at.swa_stride = a->swa_stride; at.swa_blk = (int)a->swa_blk;
+  at.comp = ptr<const uint8_t>(a->comp); at.comp_stride = a->comp_stride; at.comp_blk = (int)(a->comp_blk ? a->comp_blk : 1);
+  at.scale_log2 = (float)(1.0 / sqrt((double)D) * 1.4426950408889634);
+  at.part_o = part_o; at.part_ml = part_ml;
+  DSV41_TRY(launch(attn_split_kernel, dim3(M * nchunks * head_tiles), dim3(256), attn_smem_bytes(D), st, at));
+  CombineArgs cb = {};
+  cb.M = M; cb.heads = heads; cb.D = D; cb.nope = nope; cb.rope = rope; cb.nchunks = nchunks;
+  cb.part_o = part_o; cb.part_ml = part_ml; cb.sink = ptr<const float>(a->sink);
+  cb.cos_sin = ptr<const float>(a->cos_sin); cb.pos = ptr<const int64_t>(a->pos); cb.xo = xo;
+  DSV41_TRY(launch(attn_combine_kernel, dim3(M * heads), dim3(128), 0, st, cb));
+  // ---- wo_a -> X8B -> wo_b -> partial -> reduce
+  DSV41_TRY(gemv_launch(ga, st, use_pdl()));
+  FinalizeArgs fa = {M, G * O, ga.kslices, ga.out, x8bq, x8b, x8bs};
+  DSV41_TRY(launch(finalize_kernel, dim3(grid_for((int64_t)M * G * O / 8, 256)), dim3(256), 0, st, fa));
+  DSV41_TRY(gemv_launch(gb, st, use_pdl()));
+  FinalizeArgs fb = {M, H, gb.kslices, gb.out, attn_part, nullptr, nullptr};
+  DSV41_TRY(launch(finalize_kernel, dim3(grid_for((int64_t)M * H / 8, 256)), dim3(256), 0, st, fb));
+  // tp == 1: the all-reduce of one rank's bf16 partial is the partial itself
+  const __nv_bfloat16* reduced = attn_part;
+  if (attn != attn_part) {
+    DSV41_TRY(cudaMemcpyAsync(attn, attn_part, (size_t)M * H * 2, cudaMemcpyDeviceToDevice, st));
+    reduced = attn;
+  }
+  // ---- FFN seam
+  SeamArgs s = {};
+  s.M = M; s.H = H; s.fold = 1; s.first = 0; s.aiter = 1;
+  s.res_in = ptr<const __nv_bfloat16>(a->res_in); s.x = reduced;
+  s.post_in = ptr<const float>(a->post_in); s.comb_in = ptr<const float>(a->comb_in);
+  s.pre_in = ptr<const float>(a->pre_in); s.hc_fn = ptr<const float>(a->hc_fn);
+  s.hc_scale = ptr<const float>(a->hc_scale); s.hc_base = ptr<const float>(a->hc_base);
+  s.norm_w = ptr<const __nv_bfloat16>(a->norm_w);
+  s.res_out = res_out; s.pre_out = pre_out; s.post_out = post_out; s.comb_out = comb_out;
+  s.normed = normed; s.x8 = x8; s.x8s = x8s; s.xq = xq; s.x8r = x8r; s.x8rs = x8rs;
+  s.lin = lin; s.part = spart;
+  DSV41_TRY(launch(seam_slice_kernel, dim3(H / kSliceCols), dim3(256), 0, st, s));
+  DSV41_TRY(launch(seam_gate_norm_kernel, dim3(M), dim3(256), 0, st, s));
+  // ---- router, routing, union
+  RouterArgs ra = {M, E, H, normed, ptr<const __nv_bfloat16>(a->gate_w), logits};
+  DSV41_TRY(launch(router_kernel, dim3(cdiv(E, 8), cdiv(M, 8)), dim3(256), 0, st, ra));
+  RouteArgs rt = {M, E, TK, (int)a->route_softmax, logits, ptr<const float>(a->bias),
+                  ptr<int32_t>(a->ids), ptr<float>(a->wts)};
+  DSV41_TRY(launch(route_kernel, dim3(M), dim3(32), 0, st, rt));
+  PlanArgs pl = {M, E, TK, ptr<const int32_t>(a->ids), n_u, u_expert, u_off, picks};
+  DSV41_TRY(launch(moe_plan_kernel, dim3(1), dim3(512), 0, st, pl));
+  // ---- shared expert
+  DSV41_TRY(gemv_launch(gs, st, use_pdl()));
+  SharedActArgs sa = {M, SI, gs.kslices, gs.out, smq, smqs, smx};
+  DSV41_TRY(launch(shared_act_kernel, dim3(grid_for((int64_t)M * SI / 8, 256)), dim3(256), 0, st, sa));
+  DSV41_TRY(gemv_launch(gd, st, use_pdl()));
+  // ---- routed experts
+  DSV41_TRY(launch(expert_gemv_kernel, dim3(max_units * eu.row_groups * eu.kslices), dim3(256),
+                   expert_smem_bytes(eu.ks_len), st, eu));
+  ExpertActArgs ea = {P, I, eu.kslices, eu.out, mid, mids};
+  DSV41_TRY(launch(expert_act_kernel, dim3(grid_for((int64_t)P * I / 8, 256)), dim3(256), 0, st, ea));
+  DSV41_TRY(launch(expert_gemv_kernel, dim3(max_units * ed.row_groups * ed.kslices), dim3(256),
+                   expert_smem_bytes(ed.ks_len), st, ed));
+  CombineMoeArgs cm = {M, H, TK, ed.kslices, gd.kslices, ed.out, ptr<const float>(a->wts), gd.out, moe_part};
+  DSV41_TRY(launch(moe_combine_kernel, dim3(grid_for((int64_t)M * H, 256)), dim3(256), 0, st, cm));
+  // tp == 1: the MoE all-reduce of one partial is the partial
+  if (ptr<__nv_bfloat16>(a->out) != moe_part)
+    DSV41_TRY(cudaMemcpyAsync(ptr<void>(a->out), moe_part, (size_t)M * H * 2, cudaMemcpyDeviceToDevice, st));
+  return launch_status();
+}
+
+}  // namespace
+
+extern "C" {
+
+int dsv41_version(void) { return 1; }
+int dsv41_arch(void) { return 100; }
+
+int64_t dsv41_gemv_fp8_scratch_bytes(const Dsv41GemvArgs* a) {
+  if (!gemv_args_ok(a)) return DSV41_EINVAL;
+  GemvArgs g = plan_of(a, nullptr);
+  return g.kslices > 1 ? (int64_t)g.kslices * a->M * a->N * 4 : 0;
+}
+
+int dsv41_gemv_fp8(const Dsv41GemvArgs* a, void* stream) {
+  if (!gemv_args_ok(a)) return DSV41_EINVAL;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  GemvArgs g = plan_of(a, ptr<float>(a->y));
+  if (g.kslices > 1) {
+    const int64_t need = (int64_t)g.kslices * a->M * a->N * 4;
+    if (!a->scratch || a->scratch_bytes < need) return DSV41_ESCRATCH;
+    g.out = ptr<float>(a->scratch);
+  }
+  if (gemv_launch(g, st, false) != cudaSuccess) return launch_status();
+  if (g.kslices > 1) {
+    const int total = (int)(a->M * a->N);
+    sum_slices_kernel<<<grid_for(total, 256), 256, 0, st>>>(g.out, ptr<float>(a->y), g.kslices, total);
+  }
+  return launch_status();
+}
+
+int dsv41_relayout_mxfp4(const Dsv41RelayoutArgs* a, void* stream) {
+  if (!a || !a->src || !a->src_codes || !a->dst || !a->dst_codes || a->E < 1 || a->N % 16 ||
+      a->K % 128 || a->N < 16)
+    return DSV41_EINVAL;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  relayout_mxfp4_kernel<<<4 * 148 * 4, 256, 0, st>>>(ptr<const uint8_t>(a->src), ptr<const uint8_t>(a->src_codes),
+                                                     ptr<uint8_t>(a->dst), ptr<uint8_t>(a->dst_codes), a->E,
+                                                     (int)a->N, (int)a->K);
+  return launch_status();
+}
+
+int64_t dsv41_k1_scratch_bytes(const Dsv41K1Args* a) {
+  int64_t need = 0;
+  const int rc = k1_run(a, nullptr, false, &need);
+  return rc < 0 ? rc : need;
+}
+
+int dsv41_k1(const Dsv41K1Args* a, void* stream) {
+  int64_t need = 0;
+  return k1_run(a, reinterpret_cast<cudaStream_t>(stream), true, &need);
+}
+
+int64_t dsv41_k2_scratch_bytes(const Dsv41K2Args* a) {
+  int64_t need = 0;
+  const int rc = k2_run(a, nullptr, false, &need);
+  return rc < 0 ? rc : need;
+}
+
+int dsv41_k2(const Dsv41K2Args* a, void* stream) {
+  int64_t need = 0;
+  return k2_run(a, reinterpret_cast<cudaStream_t>(stream), true, &need);
+}
+
+}  // extern "C"

@@ -1,0 +1,481 @@
+// K2's MoE (stages/moe.py of the reference): router, routing, expert union, the MXFP4 routed
+// experts, the shared expert's activation, and the top-k-order combine.
+//
+// Bit-exact contract for routing: the router logit of (row t, expert e) is the fp64 sum of
+// the exact bf16 x bf16 products in a fixed order -- lane l of a warp owns k = 8 l + 256 i + j
+// (j < 8), sums i-major / j-minor, then the 32 lanes fold by an xor-butterfly -- rounded once
+// to fp32; scores use the deterministic fp64 softplus (detmath.cuh); the top-k takes the
+// largest (score + bias), ties to the lower expert id.
+//
+// Routed experts run on a one-time fragment relayout of the MXFP4 weights (logged by the
+// runner): a 16-row x 128-K tile is 1 KB, lane L holding bytes 16 L .. and 512 + 16 L ..,
+// i.e. the A fragments of 8 mma.m16n8k16 (4 E8M0 blocks x 2 halves) for rows g, g + 8; the
+// tile's 64 E8M0 codes are stored 8 a row pair. Activations (MXFP8 e4m3) convert exactly to
+// f16, weights by cvt.e2m1x2; each 32-K block's fp32 partial is scaled by
+// 2^(cw + cx - 254) into the accumulator.
+#pragma once
+
+#include "common.cuh"
+#include "detmath.cuh"
+
+namespace dsv41 {
+
+constexpr float kLimit = 10.0f;
+constexpr float kRouteScale = 1.5f;
+
+// ------------------------------------------------------------------ router
+struct RouterArgs {
+  int M, E, K;
+  const __nv_bfloat16* x;     // [M, K] normed
+  const __nv_bfloat16* gate;  // [E, K]
+  float* logits;              // [M, E]
+};
+
+// grid (E / 8, ceil(M / 8)); warp w of CTA (ex, tg) = expert 8 ex + w, rows 8 tg .. 8 tg + 7.
+__global__ void __launch_bounds__(256) router_kernel(const RouterArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x * 8 + warp;
+  if (e >= a.E) return;
+  pdl_wait();
+  const int iters = a.K / 256;
+  const __nv_bfloat16* w = a.gate + (size_t)e * a.K + 8 * lane;
+  const int t0 = blockIdx.y * 8, t1 = min(t0 + 8, a.M);
+  for (int t = t0; t < t1; ++t) {
+    const __nv_bfloat16* x = a.x + (size_t)t * a.K + 8 * lane;
+    double acc = 0.0;
+    for (int i = 0; i < iters; ++i) {
+      const uint4 wv = ldg16(w + 256 * i), xv = *reinterpret_cast<const uint4*>(x + 256 * i);
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w}, xx[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t wb = (j & 1) ? (ww[j >> 1] & 0xffff0000u) : (ww[j >> 1] << 16);
+        const uint32_t xb = (j & 1) ? (xx[j >> 1] & 0xffff0000u) : (xx[j >> 1] << 16);
+        acc = __fma_rn((double)__uint_as_float(xb), (double)__uint_as_float(wb), acc);
+      }
+    }
+    acc = warp_sum_d(acc);
+    if (lane == 0) a.logits[(size_t)t * a.E + e] = (float)acc;
+  }
+  pdl_launch();
+}
+
+// ------------------------------------------------------------------ routing
+struct RouteArgs {
+  int M, E, topk;
+  int softmax;          // 1: softmax top-k; 0: sqrtsoftplus + bias
+  const float* logits;  // [M, E]
+  const float* bias;    // [E] fp32 (sqrtsoftplus)
+  int32_t* ids;         // [M, topk], top-k order
+  float* wts;           // [M, topk]
+};
+
+// One warp a row; experts e = lane + 32 i.
+__global__ void route_kernel(const RouteArgs a) {
+  const int t = blockIdx.x, lane = threadIdx.x;
+  pdl_wait();
+  constexpr int kMaxPer = 16;  // E <= 512
+  const int per = (a.E + 31) / 32;
+  float val[kMaxPer], orig[kMaxPer];
+  for (int i = 0; i < kMaxPer; ++i) {
+    val[i] = -INFINITY;
+    orig[i] = 0.f;
+    const int e = lane + 32 * i;
+    if (i < per && e < a.E) {
+      const float l = a.logits[(size_t)t * a.E + e];
+      if (a.softmax) {
+        val[i] = isnan(l) ? -INFINITY : l;
+        orig[i] = l;
+      } else {
+        const float sc = route_score(l);
+        orig[i] = isnan(sc) ? 0.f : sc;
+        const float v = __fadd_rn(sc, a.bias[e]);
+        val[i] = isnan(v) ? -INFINITY : v;
+      }
+    }
+  }
+  float my_w = 0.f;
+  int my_id = 0;
+  float total = 0.f;
+  double ex[32];
+  float first = 0.f;
+  for (int k = 0; k < a.topk; ++k) {
+    // the best (value, lowest id) of the lane, then of the warp
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = 0; i < per; ++i) {
+      const int e = lane + 32 * i;
+      if (e < a.E && (val[i] > bv || (val[i] == bv && e < bi))) {
+        bv = val[i];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, d);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, d);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    // the winner's original value; retire it as NaN, which no comparison selects
+    float ow = 0.f;
+    if ((bi & 31) == lane) {
+      const int i = bi >> 5;
+      for (int q = 0; q < per; ++q)
+        if (q == i) {
+          ow = orig[q];
+          val[q] = __int_as_float(0x7fc00000);
+        }
+    }
+    ow = __shfl_sync(0xffffffffu, ow, bi & 31);
+    if (a.softmax) {
+      if (k == 0) first = ow;
+      ex[k] = det_exp(__dadd_rn((double)ow, -(double)first));
+    } else {
+      total = __fadd_rn(total, ow);
+    }
+    if (lane == k) {
+      my_w = ow;
+      my_id = bi;
+    }
+  }
+  if (a.softmax) {
+    double tot = 0.0;
+    for (int k = 0; k < a.topk; ++k) tot = __dadd_rn(tot, ex[k]);
+    if (lane < a.topk) {
+      double mine = 0.0;
+      for (int k = 0; k < a.topk; ++k)
+        if (k == lane) mine = ex[k];
+      a.ids[(size_t)t * a.topk + lane] = my_id;
+      a.wts[(size_t)t * a.topk + lane] = (float)__ddiv_rn(mine, tot);
+    }
+  } else if (lane < a.topk) {
+    const float scale = __fdiv_rn(kRouteScale, fmaxf(total, 1e-20f));
+    a.ids[(size_t)t * a.topk + lane] = my_id;
+    a.wts[(size_t)t * a.topk + lane] = __fmul_rn(my_w, scale);
+  }
+  pdl_launch();
+}
+
+// ------------------------------------------------------------------ expert union and picks
+struct PlanArgs {
+  int M, E, topk;
+  const int32_t* ids;  // [M, topk]
+  int32_t* n_u;        // [1]
+  int32_t* u_expert;   // [E]: the union's experts, ascending
+  int32_t* u_off;      // [E + 1]: each union expert's first pick in ``picks``
+  int32_t* picks;      // [M * topk]: natural pick indices t * topk + k, grouped by expert, ascending
+};
+
+__global__ void __launch_bounds__(512) moe_plan_kernel(const PlanArgs a) {
+  __shared__ int cnt[512];
+  __shared__ int off[513];
+  pdl_wait();
+  const int P = a.M * a.topk, tid = threadIdx.x;
+  for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  for (int p = tid; p < P; p += blockDim.x) atomicAdd(&cnt[a.ids[p]], 1);
+  __syncthreads();
+  if (tid == 0) {
+    int o = 0, u = 0;
+    for (int e = 0; e < a.E; ++e) {
+      off[e] = o;
+      if (cnt[e] > 0) {
+        a.u_expert[u] = e;
+        a.u_off[u] = o;
+        ++u;
+      }
+      o += cnt[e];
+    }
+    a.u_off[u] = o;
+    *a.n_u = u;
+    off[a.E] = o;
+  }
+  __syncthreads();
+  for (int p = tid; p < P; p += blockDim.x) {
+    const int e = a.ids[p];
+    int before = 0;
+    for (int q = 0; q < p; ++q) before += (a.ids[q] == e);
+    a.picks[off[e] + before] = p;
+  }
+  pdl_launch();
+}
+
+// ------------------------------------------------------------------ routed expert GEMV
+struct ExpertArgs {
+  int M, topk, N, K;   // N rows of the expert matrix (2 I for gate/up, H for down), K
+  int kslices, ks_len;  // K slices (ks_len a multiple of 128)
+  int row_groups;       // 128-row groups of N
+  int max_units;        // union slots launched for (min(E, M topk))
+  const uint8_t* w;     // relayout [E][N/16][K/128][1024]
+  const uint8_t* ws;    // relayout codes [E][N/16][K/128][64]
+  const uint8_t* x;     // e4m3 [rows, K] activations: token rows (gate/up) or pick rows (down)
+  const uint8_t* xs;    // codes [rows, K / 32]
+  int x_by_pick;        // 1: x rows are natural pick indices; 0: token rows (pick / topk)
+  const int32_t* n_u;
+  const int32_t* u_expert;
+  const int32_t* u_off;
+  const int32_t* picks;
+  float* out;           // [kslices][M * topk][N] fp32 partials, by natural pick index
+};
+
+constexpr int kExpMaxPicks = 16;  // picks staged at once (n-tiles <= 2); more loop over the weights
+
+__host__ __device__ inline int expert_smem_bytes(int ks_len) {
+  return kExpMaxPicks * (ks_len + 8) * 2 + kExpMaxPicks * (ks_len / 32) * 4;
+}
+
+// CTA = (union slot, 128-row group, K slice); warp w = 16-row tile w of the group.
+template <int NT>
+__device__ __forceinline__ void expert_tile(const ExpertArgs& a, const uint8_t* wt, const uint8_t* st,
+                                            int ksteps, uint32_t xs_base, int xs_ld,
+                                            const float* sx, int sx_ld, float (&acc)[2][4], int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t lm = ((lane & 7) * xs_ld + 8 * (lane >> 3)) * 2;
+  for (int s = 0; s < ksteps; ++s) {
+    const uint4 A0 = ldg_stream(wt + (size_t)s * 1024 + 16 * lane);
+    const uint4 A1 = ldg_stream(wt + (size_t)s * 1024 + 512 + 16 * lane);
+    const uint2 cw = *reinterpret_cast<const uint2*>(st + (size_t)s * 64 + 8 * g);
+    const uint32_t words[8] = {A0.x, A0.y, A0.z, A0.w, A1.x, A1.y, A1.z, A1.w};
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const uint32_t cws = b < 2 ? cw.x : cw.y;
+      const float sw0 = pow2c((cws >> (16 * (b & 1))) & 0xff);
+      const float sw1 = pow2c((cws >> (16 * (b & 1) + 8)) & 0xff);
+      float blk[NT][4];
+#pragma unroll
+      for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) blk[n][i] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint32_t wd = words[2 * b + j];
+        const uint32_t a0 = e2m1x2_f16(wd & 0xff), a1 = e2m1x2_f16((wd >> 8) & 0xff);
+        const uint32_t a2 = e2m1x2_f16((wd >> 16) & 0xff), a3 = e2m1x2_f16(wd >> 24);
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+          uint32_t bb[2];
+          ldmatrix_x2(bb, xs_base + lm + (uint32_t)((n * 8 * xs_ld + s * 128 + 32 * b + 16 * j) * 2));
+          mma_f16(blk[n], a0, a1, a2, a3, bb[0], bb[1]);
+        }
+      }
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const float sx0 = sx[(n * 8 + 2 * t) * sx_ld + 4 * s + b];
+        const float sx1 = sx[(n * 8 + 2 * t + 1) * sx_ld + 4 * s + b];
+        acc[n][0] = fmaf(blk[n][0], sw0 * sx0, acc[n][0]);
+        acc[n][1] = fmaf(blk[n][1], sw0 * sx1, acc[n][1]);
+        acc[n][2] = fmaf(blk[n][2], sw1 * sx0, acc[n][2]);
+        acc[n][3] = fmaf(blk[n][3], sw1 * sx1, acc[n][3]);
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) expert_gemv_kernel(const ExpertArgs a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int ks = blockIdx.x % a.kslices;
+  const int rg = (blockIdx.x / a.kslices) % a.row_groups;
+  const int u = blockIdx.x / (a.kslices * a.row_groups);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  pdl_wait();
+  if (u >= *a.n_u) return;
+  const int e = a.u_expert[u];
+  const int p0 = a.u_off[u], np_all = a.u_off[u + 1] - p0;
+  const int k0 = ks * a.ks_len, klen = min(a.ks_len, a.K - k0);
+  const int xs_ld = a.ks_len + 8;
+  __half* xs = reinterpret_cast<__half*>(smem);
+  float* sx = reinterpret_cast<float*>(smem + kExpMaxPicks * xs_ld * 2);
+  const int sx_ld = a.ks_len / 32;
+  const int tiles = a.N / 16;
+  const int tile = rg * 8 + warp;
+  const size_t kt_count = a.K / 128;
+  for (int pb = 0; pb < np_all; pb += kExpMaxPicks) {
+    const int np = min(kExpMaxPicks, np_all - pb);
+    const int npad = (np + 7) / 8 * 8;
+    __syncthreads();
+    // stage the picks' activations (e4m3 -> f16, exact) and their block scales
+    for (int i = threadIdx.x; i < npad * (klen / 4); i += blockDim.x) {
+      const int r = i / (klen / 4), q = i % (klen / 4);
+      uint32_t v = 0;
+      if (r < np) {
+        const int pick = a.picks[p0 + pb + r];
+        const int row = a.x_by_pick ? pick : pick / a.topk;
+        v = *reinterpret_cast<const uint32_t*>(a.x + (size_t)row * a.K + k0 + 4 * q);
+      }
+      uint2 h = make_uint2(e4m3x2_f16(v & 0xffff), e4m3x2_f16(v >> 16));
+      *reinterpret_cast<uint2*>(xs + r * xs_ld + 4 * q) = h;
+    }
+    for (int i = threadIdx.x; i < npad * sx_ld; i += blockDim.x) {
+      const int r = i / sx_ld, b = i % sx_ld;
+      float v = 0.f;
+      if (r < np && b < klen / 32) {
+        const int pick = a.picks[p0 + pb + r];
+        const int row = a.x_by_pick ? pick : pick / a.topk;
+        v = pow2c(a.xs[(size_t)row * (a.K / 32) + k0 / 32 + b]);
+      }
+      sx[r * sx_ld + b] = v;
+    }
+    __syncthreads();
+    if (tile >= tiles) continue;
+    const uint8_t* wt = a.w + (((size_t)e * tiles + tile) * kt_count + k0 / 128) * 1024;
+    const uint8_t* st = a.ws + (((size_t)e * tiles + tile) * kt_count + k0 / 128) * 64;
+    float acc[2][4];
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[n][i] = 0.f;
+    const uint32_t xb = smem_u32(xs);
+    const int nt = npad / 8;
+    if (nt == 1) expert_tile<1>(a, wt, st, klen / 128, xb, xs_ld, sx, sx_ld, acc, lane);
+    else expert_tile<2>(a, wt, st, klen / 128, xb, xs_ld, sx, sx_ld, acc, lane);
+    float* out = a.out + (size_t)ks * a.M * a.topk * a.N;
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = n * 8 + 2 * t + (i & 1);
+        if (n < nt && r < np) {
+          const int pick = a.picks[p0 + pb + r];
+          out[(size_t)pick * a.N + tile * 16 + g + 8 * (i >> 1)] = acc[n][i];
+        }
+      }
+  }
+  pdl_launch();
+}
+
+// ------------------------------------------------------------------ routed activation
+struct ExpertActArgs {
+  int P, I, kslices;   // picks, intermediate width, gate/up K slices
+  const float* part;   // [kslices][P][2 I]
+  uint8_t* mid;        // [P, I] e4m3 (aiter rule)
+  uint8_t* mids;       // [P, I / 32]
+};
+
+// v = bf16(gc sigmoid(gc) uc), gc = min(g, 10), uc = clamp(u, +-10); aiter MXFP8 a 32.
+// Thread = 8 consecutive columns; 4 threads a group.
+__global__ void expert_act_kernel(const ExpertActArgs a) {
+  pdl_wait();
+  const int groups8 = a.I / 8;
+  const int total = a.P * groups8, padded = (total + 31) / 32 * 32;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < padded; i += gridDim.x * blockDim.x) {
+    const bool live = i < total;
+    const int p = live ? i / groups8 : 0, c = live ? (i % groups8) * 8 : 0;
+    float v[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float gg = 0.f, uu = 0.f;
+      for (int s = 0; live && s < a.kslices; ++s) {
+        const float* row = a.part + ((size_t)s * a.P + p) * 2 * a.I;
+        gg += row[c + q];
+        uu += row[a.I + c + q];
+      }
+      const float gc = fminf(gg, kLimit), uc = fminf(fmaxf(uu, -kLimit), kLimit);
+      v[q] = bf16r(gc * (1.0f / (1.0f + expf(-gc))) * uc);
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) amax = fmaxf(amax, fabsf(v[q]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const int code = mx_code_aiter(amax);
+    const float mul = mx_mul(code);
+    uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint32_t b = e4m3_byte(v[q] * mul);
+      if (q < 4) w0 |= b << (8 * q);
+      else w1 |= b << (8 * (q - 4));
+    }
+    if (!live) continue;
+    *reinterpret_cast<uint2*>(a.mid + (size_t)p * a.I + c) = make_uint2(w0, w1);
+    if ((c & 31) == 0) a.mids[(size_t)p * (a.I / 32) + c / 32] = (uint8_t)code;
+  }
+  pdl_launch();
+}
+
+// ------------------------------------------------------------------ shared expert activation
+struct SharedActArgs {
+  int M, SI, kslices;
+  const float* part;      // [kslices][M][2 SI] (gate rows, then up rows)
+  uint8_t* smq;           // [M, SI] e4m3 (vLLM rule)
+  uint8_t* smqs;          // [M, SI / 32]
+  __nv_bfloat16* smx;     // [M, SI] dequantized (the down GEMV's input)
+};
+
+// g = bf16(min(bf16(h_g), 10)), u = clamp(bf16(h_u), +-10), act = bf16(g / (1 + e^-g)),
+// v = bf16(act u) (moe.py:502-507); vLLM MXFP8 a 32.
+__global__ void shared_act_kernel(const SharedActArgs a) {
+  pdl_wait();
+  const int groups8 = a.SI / 8;
+  const int total = a.M * groups8, padded = (total + 31) / 32 * 32;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < padded; i += gridDim.x * blockDim.x) {
+    const bool live = i < total;
+    const int t = live ? i / groups8 : 0, c = live ? (i % groups8) * 8 : 0;
+    float v[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float gg = 0.f, uu = 0.f;
+      for (int s = 0; live && s < a.kslices; ++s) {
+        const float* row = a.part + ((size_t)s * a.M + t) * 2 * a.SI;
+        gg += row[c + q];
+        uu += row[a.SI + c + q];
+      }
+      const float gq = bf16r(fminf(bf16r(gg), kLimit));
+      const float uq = fminf(fmaxf(bf16r(uu), -kLimit), kLimit);
+      const float act = bf16r(gq / (1.0f + expf(-gq)));
+      v[q] = bf16r(act * uq);
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) amax = fmaxf(amax, fabsf(v[q]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const int code = mx_code_vllm(amax);
+    const float mul = mx_mul(code), sc = pow2c(code);
+    uint32_t w0 = 0, w1 = 0, d[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint8_t b = e4m3_byte(v[q] * mul);
+      if (q < 4) w0 |= (uint32_t)b << (8 * q);
+      else w1 |= (uint32_t)b << (8 * (q - 4));
+      d[q >> 1] |= (uint32_t)f2bfbits(e4m3_float(b) * sc) << (16 * (q & 1));
+    }
+    if (!live) continue;
+    *reinterpret_cast<uint2*>(a.smq + (size_t)t * a.SI + c) = make_uint2(w0, w1);
+    if ((c & 31) == 0) a.smqs[(size_t)t * (a.SI / 32) + c / 32] = (uint8_t)code;
+    *reinterpret_cast<uint4*>(a.smx + (size_t)t * a.SI + c) = make_uint4(d[0], d[1], d[2], d[3]);
+  }
+  pdl_launch();
+}
+
+// ------------------------------------------------------------------ combine
+struct CombineMoeArgs {
+  int M, H, topk, routed_slices, shared_slices;
+  const float* routed;   // [routed_slices][M * topk][H] down partials by natural pick
+  const float* wts;      // [M, topk]
+  const float* shared;   // [shared_slices][M][H] shared down partials
+  __nv_bfloat16* out;    // [M, H]: bf16(routed + shared)
+};
+
+// routed = bf16(routed + bf16(y_k w_k)) in top-k order; out = bf16(routed + bf16(shared)).
+__global__ void moe_combine_kernel(const CombineMoeArgs a) {
+  pdl_wait();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.M * a.H; i += gridDim.x * blockDim.x) {
+    const int t = i / a.H, n = i % a.H;
+    float routed = 0.f;
+    for (int k = 0; k < a.topk; ++k) {
+      const size_t pick = (size_t)t * a.topk + k;
+      float y = 0.f;
+      for (int s = 0; s < a.routed_slices; ++s) y += a.routed[((size_t)s * a.M * a.topk + pick) * a.H + n];
+      routed = bf16r(routed + bf16r(y * a.wts[pick]));
+    }
+    float sh = 0.f;
+    for (int s = 0; s < a.shared_slices; ++s) sh += a.shared[((size_t)s * a.M + t) * a.H + n];
+    a.out[i] = __float2bfloat16_rn(routed + bf16r(sh));
+  }
+  pdl_launch();
+}
+
+}  // namespace dsv41

@@ -1,0 +1,234 @@
+// mHC seam (hc_mult 4): the boundary before each sublayer (K1's attention seam, K2's FFN
+// seam). Restates seam.py:137-378 of the reference:
+//   R_new[o] = bf16(fma(c3 r3, ((post_o x + r0 c0o) + c1o r1) + c2o r2))   (a post owed)
+//   LIN      = bf16(sum_h pre_prev[h] R_new[h])  (copy 0 of R on the first layer)
+//   mixes    = hc_fn . R_new (24), sumsq = |R_new|^2  -> gate: pre / post / comb (Sinkhorn)
+//   normed   = bf16((LIN rstd) w)  -> MXFP8 (vLLM rule; K2 also the aiter rule)
+// Two launches: seam_slice (32-column slices, partial mixes per slice) and seam_gate_norm (a
+// CTA per row: slices summed in slice order, gate, RMSNorm and quantization).
+#pragma once
+
+#include "common.cuh"
+
+namespace dsv41 {
+
+constexpr int kHC = 4;
+constexpr int kMix = 24;
+constexpr int kPart = kMix + 1;  // a slice's partials a row: 24 mixes, then the sum of squares
+constexpr int kSliceCols = 32;
+constexpr float kHcEps = 1e-6f;
+
+struct SeamArgs {
+  int M, H;
+  int fold;   // a post is owed: fold x into the residual
+  int first;  // the first layer: the collapse is copy 0
+  int aiter;  // also write the aiter-rule MXFP8 (routed experts' input)
+  const __nv_bfloat16* res_in;  // [M, 4, H]
+  const __nv_bfloat16* x;       // [M, H] pending sublayer output (fold)
+  const float* post_in;         // [M, 4]
+  const float* comb_in;         // [M, 4(src), 4(dst)]
+  const float* pre_in;          // [M, 4] previous pre (collapse)
+  const float* hc_fn;           // [24, 4 H]
+  const float* hc_scale;        // [3]
+  const float* hc_base;         // [24]
+  const __nv_bfloat16* norm_w;  // [H]
+  // outputs
+  __nv_bfloat16* res_out;   // [M, 4, H]
+  float* pre_out;           // [M, 4]
+  float* post_out;          // [M, 4]
+  float* comb_out;          // [M, 4, 4]
+  __nv_bfloat16* normed;    // [M, H]
+  uint8_t* x8;              // [M, H] e4m3 (vLLM rule)
+  uint8_t* x8s;             // [M, H / 32] codes
+  __nv_bfloat16* xq;        // [M, H] x8 dequantized (the GEMVs' input)
+  uint8_t* x8r;             // [M, H] e4m3 (aiter rule), when aiter
+  uint8_t* x8rs;            // [M, H / 32]
+  // scratch
+  __nv_bfloat16* lin;       // [M, H]
+  float* part;              // [M, H / 32, 25]
+};
+
+__global__ void __launch_bounds__(256) seam_slice_kernel(const SeamArgs a) {
+  __shared__ float fn[kMix * kHC * kSliceCols];   // this slice's mix weights
+  __shared__ float rs[48 * kHC * kSliceCols];     // R_new of every row (bf16-valued)
+  const int s = blockIdx.x, c0 = s * kSliceCols, H = a.H;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // mix weights first: they wait on nothing
+  for (int e = tid; e < kMix * kHC * kSliceCols; e += blockDim.x) {
+    const int j = e / (kHC * kSliceCols), r = e % (kHC * kSliceCols), o = r / kSliceCols,
+              c = r % kSliceCols;
+    fn[e] = __ldg(a.hc_fn + (size_t)j * kHC * H + (size_t)o * H + c0 + c);
+  }
+  pdl_wait();
+  for (int e = tid; e < a.M * kHC * kSliceCols; e += blockDim.x) {
+    const int t = e / (kHC * kSliceCols), r = e % (kHC * kSliceCols), o = r / kSliceCols,
+              c = r % kSliceCols;
+    const size_t at = ((size_t)t * kHC + o) * H + c0 + c;
+    float v;
+    if (a.fold) {
+      const float* cm = a.comb_in + t * 16;
+      float r0 = bf2f(a.res_in[((size_t)t * kHC + 0) * H + c0 + c]);
+      float r1 = bf2f(a.res_in[((size_t)t * kHC + 1) * H + c0 + c]);
+      float r2 = bf2f(a.res_in[((size_t)t * kHC + 2) * H + c0 + c]);
+      float r3 = bf2f(a.res_in[((size_t)t * kHC + 3) * H + c0 + c]);
+      float xv = bf2f(a.x[(size_t)t * H + c0 + c]);
+      v = __fadd_rn(__fmul_rn(a.post_in[t * kHC + o], xv), __fmul_rn(r0, cm[0 * 4 + o]));
+      v = __fadd_rn(v, __fmul_rn(cm[1 * 4 + o], r1));
+      v = __fadd_rn(v, __fmul_rn(cm[2 * 4 + o], r2));
+      v = bf16r(__fmaf_rn(cm[3 * 4 + o], r3, v));
+    } else {
+      v = bf2f(a.res_in[at]);
+    }
+    a.res_out[at] = __float2bfloat16_rn(v);
+    rs[t * kHC * kSliceCols + r] = v;
+  }
+  __syncthreads();
+  // the layer input: R_new collapsed with the previous pre, h in order
+  for (int e = tid; e < a.M * kSliceCols; e += blockDim.x) {
+    const int t = e / kSliceCols, c = e % kSliceCols;
+    float acc;
+    if (a.first) {
+      acc = rs[t * kHC * kSliceCols + c];
+    } else {
+      acc = 0.f;
+#pragma unroll
+      for (int h = 0; h < kHC; ++h)
+        acc = __fadd_rn(acc, __fmul_rn(a.pre_in[t * kHC + h], rs[t * kHC * kSliceCols + h * kSliceCols + c]));
+    }
+    a.lin[(size_t)t * H + c0 + c] = __float2bfloat16_rn(acc);
+  }
+  // partial mixes and the sum of squares: a warp a (row, projection), 4 terms a lane
+  const int nslices = H / kSliceCols;
+  for (int p = warp; p < a.M * kPart; p += 8) {
+    const int t = p / kPart, j = p % kPart;
+    const float* r = rs + t * kHC * kSliceCols;
+    float acc = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int e = lane + 32 * q;
+      acc = fmaf(j < kMix ? fn[j * kHC * kSliceCols + e] : r[e], r[e], acc);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) a.part[((size_t)t * nslices + s) * kPart + j] = acc;
+  }
+  pdl_launch();
+}
+
+// Store one row's 32-value group as MXFP8 (vLLM or aiter rule) from 8 values a lane; lanes
+// 4 g .. 4 g + 3 of a warp hold group g.
+__device__ __forceinline__ void mx_group_store(const float (&v)[8], bool vllm, uint8_t* q8,
+                                               uint8_t* codes, __nv_bfloat16* deq, int col) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  const int code = vllm ? mx_code_vllm(amax) : mx_code_aiter(amax);
+  const float mul = mx_mul(code), sc = pow2c(code);
+  uint32_t w0 = 0, w1 = 0;
+  uint32_t d[4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint8_t b = e4m3_byte(v[i] * mul);
+    if (i < 4) w0 |= (uint32_t)b << (8 * i);
+    else w1 |= (uint32_t)b << (8 * (i - 4));
+    if (deq) {
+      const float dv = e4m3_float(b) * sc;
+      if (i & 1) d[i >> 1] |= (uint32_t)f2bfbits(dv) << 16;
+      else d[i >> 1] = f2bfbits(dv);
+    }
+  }
+  *reinterpret_cast<uint2*>(q8 + col) = make_uint2(w0, w1);
+  if ((threadIdx.x & 3) == 0) codes[col / 32] = (uint8_t)code;
+  if (deq) *reinterpret_cast<uint4*>(deq + col) = make_uint4(d[0], d[1], d[2], d[3]);
+}
+
+__global__ void __launch_bounds__(256) seam_gate_norm_kernel(const SeamArgs a) {
+  __shared__ float red[8];
+  __shared__ float tot_s;
+  const int t = blockIdx.x, H = a.H, tid = threadIdx.x;
+  pdl_wait();
+  // ---- gate: one thread, slices in order
+  if (tid == 0) {
+    const int nslices = H / kSliceCols;
+    float mix[kPart];
+    for (int j = 0; j < kPart; ++j) mix[j] = 0.f;
+    for (int s = 0; s < nslices; ++s)
+      for (int j = 0; j < kPart; ++j) mix[j] += a.part[((size_t)t * nslices + s) * kPart + j];
+    const float rstd = 1.0f / sqrtf(mix[kMix] / (float)(kHC * H) + kRmsEps);
+    float v[kMix];
+    for (int j = 0; j < kMix; ++j) v[j] = mix[j] * rstd;
+    const float s0 = a.hc_scale[0], s1 = a.hc_scale[1], s2 = a.hc_scale[2];
+    for (int i = 0; i < kHC; ++i) {
+      a.pre_out[t * kHC + i] = 1.0f / (1.0f + expf(-(v[i] * s0 + a.hc_base[i]))) + kHcEps;
+      a.post_out[t * kHC + i] = 2.0f / (1.0f + expf(-(v[kHC + i] * s1 + a.hc_base[kHC + i])));
+    }
+    float cv[16];
+    for (int e = 0; e < 16; ++e) cv[e] = v[8 + e] * s2 + a.hc_base[8 + e];
+    for (int r = 0; r < 4; ++r) {
+      float m = fmaxf(fmaxf(cv[4 * r], cv[4 * r + 1]), fmaxf(cv[4 * r + 2], cv[4 * r + 3]));
+      float sum = 0.f;
+      for (int c = 0; c < 4; ++c) {
+        cv[4 * r + c] = expf(cv[4 * r + c] - m);
+        sum += cv[4 * r + c];
+      }
+      for (int c = 0; c < 4; ++c) cv[4 * r + c] = cv[4 * r + c] / sum + kHcEps;
+    }
+    for (int it = 0; it < 20; ++it) {
+      if (it > 0)
+        for (int r = 0; r < 4; ++r) {
+          const float sum = (cv[4 * r] + cv[4 * r + 1]) + (cv[4 * r + 2] + cv[4 * r + 3]) + kHcEps;
+          for (int c = 0; c < 4; ++c) cv[4 * r + c] /= sum;
+        }
+      for (int c = 0; c < 4; ++c) {
+        const float sum = (cv[c] + cv[4 + c]) + (cv[8 + c] + cv[12 + c]) + kHcEps;
+        for (int r = 0; r < 4; ++r) cv[4 * r + c] /= sum;
+      }
+    }
+    for (int e = 0; e < 16; ++e) a.comb_out[t * 16 + e] = cv[e];
+  }
+  // ---- norm: 8 consecutive columns a thread
+  float ss = 0.f;
+  for (int c = tid * 8; c < H; c += blockDim.x * 8) {
+    const uint4 w = *reinterpret_cast<const uint4*>(a.lin + (size_t)t * H + c);
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float lo = __uint_as_float(ws[i] << 16), hi = __uint_as_float(ws[i] & 0xffff0000u);
+      ss = fmaf(lo, lo, ss);
+      ss = fmaf(hi, hi, ss);
+    }
+  }
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  if (tid == 0) {
+    float s = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += red[w];
+    tot_s = s;
+  }
+  __syncthreads();
+  const float r = 1.0f / sqrtf(tot_s / (float)H + kRmsEps);
+  for (int c = tid * 8; c < H; c += blockDim.x * 8) {
+    const uint4 w = *reinterpret_cast<const uint4*>(a.lin + (size_t)t * H + c);
+    const uint4 nw = *reinterpret_cast<const uint4*>(a.norm_w + c);
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    const uint32_t ns[4] = {nw.x, nw.y, nw.z, nw.w};
+    float y[8];
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      y[2 * i] = bf16r((__uint_as_float(ws[i] << 16) * r) * __uint_as_float(ns[i] << 16));
+      y[2 * i + 1] = bf16r((__uint_as_float(ws[i] & 0xffff0000u) * r) * __uint_as_float(ns[i] & 0xffff0000u));
+      o[i] = pack_bf16x2(y[2 * i], y[2 * i + 1]);
+    }
+    const size_t at = (size_t)t * H + c;
+    *reinterpret_cast<uint4*>(a.normed + at) = make_uint4(o[0], o[1], o[2], o[3]);
+    mx_group_store(y, true, a.x8 + (size_t)t * H, a.x8s + (size_t)t * (H / 32), a.xq + (size_t)t * H, c);
+    if (a.aiter)
+      mx_group_store(y, false, a.x8r + (size_t)t * H, a.x8rs + (size_t)t * (H / 32), nullptr, c);
+  }
+  pdl_launch();
+}
+
+}  // namespace dsv41

@@ -1,0 +1,156 @@
+"""K1 and K2 on the GPU against the CPU oracle, stage by stage, on BASELINE-config shapes.
+
+Each stage's oracle runs on the GPU's own inputs to that stage, so integer outputs (KV record
+bytes, key tables, router logits, routing ids, MXFP8 codes) must match bit for bit, and
+floating-point outputs within the reference's bounds (``deepseek_v41/spec.py:287-318`` of
+the reference: k1.q.cosine 0.99999, k1.q.rel 5e-3, k2.attn_out.cosine 0.9998, k2.wo_a.rel
+5e-3, k2.wo_b.rel 1e-3, ffn.moe.cosine 0.9999, ffn.moe.rel 0.015, ffn.mix.rel 1e-4). The
+whole layer is then checked end to end: max |out - oracle| <= 2e-2 x RMS(oracle).
+"""
+
+import pytest
+import torch
+
+from oracle import layer as OL
+from oracle import numerics as N
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda")
+
+
+def cos(a, b):
+    return torch.nn.functional.cosine_similarity(a.double().flatten(), b.double().flatten(), dim=0).item()
+
+
+def rel(a, b):
+    a, b = a.double().flatten(), b.double().flatten()
+    return ((a - b).norm() / b.norm()).item()
+
+
+def cpu(d):
+    return {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in d.items()}
+
+
+SMALL2 = dict(hidden=2048, heads=16, nope=512, rope=64, q_lora=512, o_groups=2, o_rank=1024,
+              experts=32, topk=8, inter=512, shared_inter=512)
+
+
+def _setup(shape_kw, M, ctx, seed):
+    from sgl_amd_mono_b200.deepseek_v41 import synth
+    from sgl_amd_mono_b200.deepseek_v41.shapes import CONFIG1, LayerShape
+    from sgl_amd_mono_b200.deepseek_v41.sm100a.runner import MonoRunner
+    s = CONFIG1 if shape_kw == "config1" else LayerShape(**shape_kw)
+    w = synth.make_layer(s, seed, DEV, positions=max(ctx + 8, 4096))
+    step = synth.make_step(s, M, ctx, seed + 100, DEV)
+    r = MonoRunner(s, DEV)
+    L = r.bind(w)
+    return s, w, step, r, L
+
+
+@pytest.mark.parametrize("shape_kw,M,ctx", [("config1", 4, 1024), (SMALL2, 5, 300), (SMALL2, 33, 129)])
+def test_k1_k2_stages(shape_kw, M, ctx):
+    s, w, step, r, L = _setup(shape_kw, M, ctx, seed=3)
+    cache0 = step["cache"].clone()
+    b = r.k1(L, step, M)
+    r.k2(L, step, M, b)
+    torch.cuda.synchronize()
+    W, S, B = cpu(w), cpu(step), cpu(b)
+    H, QL, D, nope = s.hidden, s.q_lora, s.head_dim, s.nope
+    cs = W["cos_sin"][S["pos"]]
+    cosv, sinv = cs[:, :32], cs[:, 32:]
+
+    # ---- K1 seam
+    rn, normed, pre, post, comb = OL.seam(S["res"].float(), S["x"].float(), S["post"], S["comb"], S["pre"],
+                                          W["hc_attn_fn"], W["hc_attn_scale"], W["hc_attn_base"],
+                                          W["attn_norm"])
+    assert rel(B["res1"].float(), rn) < 1e-3
+    for got, ref in ((B["pre_a"], pre), (B["post_a"], post), (B["comb_a"], comb)):
+        assert (got - ref).abs().max().item() < 1e-5 + 1e-4 * ref.abs().max().item()
+    assert cos(B["normed_a"].float(), normed) > 0.9999 and rel(B["normed_a"].float(), normed) < 0.012
+    q8, q8s = N.mxfp8_quant(B["normed_a"].float(), "vllm")
+    assert torch.equal(q8, B["x8"]) and torch.equal(q8s, B["x8s"])
+    # ---- wqkv_a
+    qkv = OL.gemv_x8_fp8(B["x8"], B["x8s"], W["wqkv"], W["wqkv_s"])
+    assert rel(B["qkv"], qkv) < 1e-5
+    # ---- q path (q_norm's sum in another order: compare values)
+    ys, qx8, qx8s = OL.q_path(B["qkv"][:, :QL], W["q_norm"])
+    assert rel(N.mxfp8_dequant(B["qx8"], B["qx8s"]), N.mxfp8_dequant(qx8, qx8s)) < 4e-3
+    # ---- the KV record: bit-exact
+    nb, rb, codes = OL.kv_record(B["qkv"][:, QL:], W["kv_norm"], cosv, sinv, nope)
+    data, sc = OL.record_bytes(nb, rb, codes, 8)
+    ref_cache = cache0.cpu().clone()
+    OL.write_records(ref_cache, S["slot"], data, sc, S["blk"])
+    assert torch.equal(S["cache"], ref_cache)
+    # ---- wq_b + RoPE
+    v = OL.bf(OL.gemv_x8_fp8(B["qx8"], B["qx8s"], W["wqb"], W["wqb_s"])).view(M, -1, D)
+    q = OL.rope_q(v, cosv, sinv, nope)
+    assert cos(B["q"].float(), q) > 0.99999 and rel(B["q"].float(), q) < 5e-3
+    # ---- key table
+    kt, klen = OL.key_table(S["slot"], S["swa_idx"], S["swa_lens"], None, torch.zeros(M, dtype=torch.int32),
+                            S["swa_idx"].shape[1], 0)
+    assert torch.equal(B["kt"], kt) and torch.equal(B["klen"], klen)
+
+    # ---- K2 attention (the GPU's q and table)
+    xo = OL.attention(B["q"].float(), B["kt"], B["klen"], S["cache"], S["blk"], None, 1, W["sink"], cosv,
+                      sinv, nope, s.rope, 8)
+    assert cos(B["xo"].float(), xo) > 0.9998
+    # ---- wo_a -> X8B, wo_b
+    _, x8b, x8bs = OL.wo_a(B["xo"].float(), W["woa"], W["woa_s"], s.groups_local, s.o_rank)
+    assert rel(N.mxfp8_dequant(B["x8b"], B["x8bs"]), N.mxfp8_dequant(x8b, x8bs)) < 5e-3
+    part = OL.wo_b(B["x8b"], B["x8bs"], W["wob"], W["wob_s"])
+    assert rel(B["attn_part"].float(), part) < 1e-3
+    assert torch.equal(B["attn"], B["attn_part"])
+    # ---- FFN seam
+    rn2, normed2, pre2, post2, comb2 = OL.seam(B["res1"].float(), B["attn"].float(), B["post_a"], B["comb_a"],
+                                               B["pre_a"], W["hc_ffn_fn"], W["hc_ffn_scale"],
+                                               W["hc_ffn_base"], W["ffn_norm"])
+    assert rel(B["res2"].float(), rn2) < 1e-3
+    assert cos(B["normed_f"].float(), normed2) > 0.9999
+    # ---- router logits and routing: bit-exact on the GPU's normed row
+    logits = OL.router_logits(B["normed_f"].float(), W["gate_w"])
+    assert torch.equal(B["logits"], logits)
+    ids, wts = OL.route(B["logits"], W.get("bias"), s.topk, s.route)
+    assert torch.equal(B["ids"], ids)
+    assert torch.equal(B["wts"], wts)
+    # ---- MoE partial
+    moe, _, _, _ = OL.moe_partial(B["normed_f"].float(), dict(W, w13=W["w13"], s13=W["s13"]), s.route, s.topk)
+    assert cos(B["out"].float(), moe) > 0.9999 and rel(B["out"].float(), moe) < 0.015
+
+
+@pytest.mark.parametrize("shape_kw,M,ctx", [("config1", 4, 1024), (SMALL2, 7, 200)])
+def test_layer_end_to_end(shape_kw, M, ctx):
+    """The whole layer from the same inputs: oracle end to end vs K1 + K2."""
+    s, w, step, r, L = _setup(shape_kw, M, ctx, seed=11)
+    cache0 = step["cache"].clone()
+    b = r.k1(L, step, M)
+    r.k2(L, step, M, b)
+    torch.cuda.synchronize()
+    W, S = cpu(w), cpu(step)
+    cache = cache0.cpu()
+    cs = W["cos_sin"][S["pos"]]
+    cosv, sinv = cs[:, :32], cs[:, 32:]
+    QL, D, nope = s.q_lora, s.head_dim, s.nope
+    rn, normed, pre, post, comb = OL.seam(S["res"].float(), S["x"].float(), S["post"], S["comb"], S["pre"],
+                                          W["hc_attn_fn"], W["hc_attn_scale"], W["hc_attn_base"], W["attn_norm"])
+    x8, x8s = N.mxfp8_quant(normed, "vllm")
+    qkv = OL.gemv_x8_fp8(x8, x8s, W["wqkv"], W["wqkv_s"])
+    _, qx8, qx8s = OL.q_path(qkv[:, :QL], W["q_norm"])
+    nb, rb, codes = OL.kv_record(qkv[:, QL:], W["kv_norm"], cosv, sinv, nope)
+    data, sc = OL.record_bytes(nb, rb, codes, 8)
+    OL.write_records(cache, S["slot"], data, sc, S["blk"])
+    q = OL.rope_q(OL.bf(OL.gemv_x8_fp8(qx8, qx8s, W["wqb"], W["wqb_s"])).view(M, -1, D), cosv, sinv, nope)
+    kt, klen = OL.key_table(S["slot"], S["swa_idx"], S["swa_lens"], None, torch.zeros(M, dtype=torch.int32),
+                            S["swa_idx"].shape[1], 0)
+    xo = OL.attention(q, kt, klen, cache, S["blk"], None, 1, W["sink"], cosv, sinv, nope, s.rope, 8)
+    _, x8b, x8bs = OL.wo_a(xo, W["woa"], W["woa_s"], s.groups_local, s.o_rank)
+    attn = OL.all_reduce([OL.wo_b(x8b, x8bs, W["wob"], W["wob_s"])])
+    rn2, normed2, *_ = OL.seam(rn, attn, post, comb, pre, W["hc_ffn_fn"], W["hc_ffn_scale"],
+                               W["hc_ffn_base"], W["ffn_norm"])
+    out, ids, _, _ = OL.moe_partial(normed2, W, s.route, s.topk)
+    got = b["out"].float().cpu()
+    rms = out.pow(2).mean().sqrt().item()
+    assert (got - out).abs().max().item() <= 2e-2 * rms, ((got - out).abs().max().item(), rms)
+    assert (b["res2"].float().cpu() - rn2).abs().max().item() <= 2e-2 * rn2.pow(2).mean().sqrt().item()
+    same = (b["ids"].cpu().sort(1).values == ids.sort(1).values).all(1).float().mean().item()
+    assert same >= 0.9
