@@ -1,0 +1,396 @@
+"""Benchmark of the DeepSeek-V4.1 decode monokernel path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--rows M] [--impl ours|reference]
+
+Workload: BASELINE config 2 -- one full-size synthetic MoE decode layer (hidden 4096, 64 heads
+of 512 + 64 latent dims, 256 experts top-8 + 1 shared, expert intermediate 2048, MXFP4
+experts, FP8 block-scaled projections) at KV context 8192, random-init (seed 1). A step is
+one decoder layer (K1 + K2, CUDA-graph replayed) over M decode rows; steps alternate
+between distinct layer copies and their caches, so no step reads weights another step left
+in L2 (each step also reads more than L2 holds). ``value`` = decode tokens/s of the layer
+(M rows / layer time, summed over ranks); the sweep over M = 1, 4, 16, 48 and the per-M
+fraction of the HBM weight-streaming roofline are in ``config``.
+
+With N > 1 (torchrun), each rank runs its own replica of the layer (weak scaling: no data-path
+collective in this mode); ``value`` sums the ranks' rows over the max-over-ranks time.
+
+``--impl reference`` times the reference path's CPU restatement (the repository's oracle:
+torch fp32/fp64 on the host cores, all threads) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "decode tokens/s (one config-2 MoE decode layer, K1 + K2)"
+UNIT = "tokens/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--rows", type=int, default=48, help="headline decode rows M")
+    ap.add_argument("--sweep", default="1,4,16,48")
+    ap.add_argument("--ctx", type=int, default=8192)
+    ap.add_argument("--layers", type=int, default=2, help="distinct layer copies stepped round-robin")
+    ap.add_argument("--seed", type=int, default=1)
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------- distributed plumbing
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- clocks during the timed region
+class Clocks:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={self.QUERY}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.flush()
+        rows = []
+        with open(self.f.name) as fh:
+            for line in fh:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- the CPU reference path
+def cpu_layer(w, step, shape, rows: int) -> float:
+    """Time one layer of the oracle (the reference path's CPU restatement) over ``rows`` rows."""
+    from oracle import layer as OL
+    from oracle import numerics as N
+    W = w
+    S = {k: (v[:rows] if torch.is_tensor(v) and k not in ("cache",) else v) for k, v in step.items()}
+    cache = step["cache"].clone()
+    t0 = time.perf_counter()
+    cs = W["cos_sin"][S["pos"]]
+    cosv, sinv = cs[:, :32], cs[:, 32:]
+    QL, D, nope = shape.q_lora, shape.head_dim, shape.nope
+    rn, normed, pre, post, comb = OL.seam(S["res"].float(), S["x"].float(), S["post"], S["comb"], S["pre"],
+                                          W["hc_attn_fn"], W["hc_attn_scale"], W["hc_attn_base"], W["attn_norm"])
+    x8, x8s = N.mxfp8_quant(normed, "vllm")
+    qkv = OL.gemv_x8_fp8(x8, x8s, W["wqkv"], W["wqkv_s"])
+    _, qx8, qx8s = OL.q_path(qkv[:, :QL], W["q_norm"])
+    nb, rb, codes = OL.kv_record(qkv[:, QL:], W["kv_norm"], cosv, sinv, nope)
+    data, sc = OL.record_bytes(nb, rb, codes, 8)
+    OL.write_records(cache, S["slot"], data, sc, S["blk"])
+    q = OL.rope_q(OL.bf(OL.gemv_x8_fp8(qx8, qx8s, W["wqb"], W["wqb_s"])).view(rows, -1, D), cosv, sinv, nope)
+    kt, klen = OL.key_table(S["slot"], S["swa_idx"], S["swa_lens"], None, torch.zeros(rows, dtype=torch.int32),
+                            S["swa_idx"].shape[1], 0)
+    xo = OL.attention(q, kt, klen, cache, S["blk"], None, 1, W["sink"], cosv, sinv, nope, shape.rope, 8)
+    _, x8b, x8bs = OL.wo_a(xo, W["woa"], W["woa_s"], shape.groups_local, shape.o_rank)
+    attn = OL.all_reduce([OL.wo_b(x8b, x8bs, W["wob"], W["wob_s"])])
+    rn2, normed2, *_ = OL.seam(rn, attn, post, comb, pre, W["hc_ffn_fn"], W["hc_ffn_scale"],
+                               W["hc_ffn_base"], W["ffn_norm"])
+    OL.moe_partial(normed2, W, shape.route, shape.topk)
+    return time.perf_counter() - t0
+
+
+def cpu_inputs(args, shape):
+    """Config-2 weights and a one-row step on the host (drawn on the GPU when there is one)."""
+    from sgl_amd_mono_b200.deepseek_v41 import synth
+    dev = torch.device("cuda") if torch.cuda.is_available() else torch.device("cpu")
+    w = synth.make_layer(shape, args.seed, dev, positions=args.ctx + 8)
+    step = synth.make_step(shape, 1, args.ctx, args.seed + 1000, dev)
+    cpu = lambda d: {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in d.items()}  # noqa: E731
+    return cpu(w), cpu(step)
+
+
+def run_reference(args, world, rank):
+    from sgl_amd_mono_b200.deepseek_v41.shapes import CONFIG2
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    w, step = cpu_inputs(args, CONFIG2)
+    for _ in range(args.warmup):
+        cpu_layer(w, step, CONFIG2, 1)
+    ts = [cpu_layer(w, step, CONFIG2, 1) for _ in range(args.steps)]
+    t = sum(ts) / len(ts)
+    v = 1.0 / t
+    sample = f"1 decode row of config 2 (ctx {args.ctx}), one layer, a step; torch CPU, {threads} threads"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic (random-init, seeded)",
+        "config": {"workload": "config2: one MoE decode layer, ctx %d" % args.ctx, "rows": 1,
+                   "reference_kind": "port (the repository's CPU oracle of the reference path)"},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- the GPU path
+def run_ours(args, world, rank, local):
+    from sgl_amd_mono_b200.common import ext
+    from sgl_amd_mono_b200.deepseek_v41 import roofline, synth
+    from sgl_amd_mono_b200.deepseek_v41.shapes import CONFIG2
+    from sgl_amd_mono_b200.deepseek_v41.sm100a import abi
+    from sgl_amd_mono_b200.deepseek_v41.sm100a.runner import MonoRunner
+
+    dev = torch.device("cuda", local if world > 1 else 0)
+    shape = CONFIG2
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            peaks = json.load(fh)
+    except OSError:
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    runner = MonoRunner(shape, dev)
+    layers = [runner.bind(synth.make_layer(shape, args.seed + 7919 * i + rank, dev, positions=args.ctx + 8),
+                          tag=f"layer{i}") for i in range(args.layers)]
+    sweep = sorted({int(x) for x in args.sweep.split(",") if x} | {args.rows})
+    stream = torch.cuda.current_stream()
+    results, graphs_by_m, steps_by_m, bufs_by_m = {}, {}, {}, {}
+    launches_per_step = None
+    for M in sweep:
+        steps = [synth.make_step(shape, M, args.ctx, args.seed + 100 * i + M + 1000 * rank, dev)
+                 for i in range(args.layers)]
+        graphs, bufs = [], []
+        for L, st in zip(layers, steps):
+            b = runner.k1(L, st, M)  # eager: allocates buffers and scratch outside capture
+            runner.k2(L, st, M, b)
+            c0 = ext.launch_count()
+            runner.k1(L, st, M)
+            runner.k2(L, st, M, b)
+            if launches_per_step is None or M == args.rows:
+                launches_per_step = ext.launch_count() - c0
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                runner.k1(L, st, M)
+                runner.k2(L, st, M, b)
+            graphs.append(g)
+            bufs.append(b)
+        for i in range(args.warmup):
+            graphs[i % len(graphs)].replay()
+        torch.cuda.synchronize()
+        barrier(world)
+        clocks = Clocks(local if world > 1 else 0) if M == args.rows else None
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for i in range(args.steps):
+            graphs[i % len(graphs)].replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        clk = clocks.stop() if clocks else None
+        barrier(world)
+        ms = max_over_ranks(ms, world)
+        # algorithmic bytes of the step (the run's own routing union, the keys read)
+        unions = [int(torch.unique(b["ids"]).numel()) for b in bufs]
+        keys = [int(b["klen"][:M].sum().item()) for b in bufs]
+        lb = [roofline.layer_bytes(shape, u, k)["total"] for u, k in zip(unions, keys)]
+        avg_bytes = sum(lb) / len(lb)
+        gbs = avg_bytes / (ms * 1e-3) / 1e9
+        results[M] = {"us_per_layer": round(ms * 1e3, 2), "tokens_s": round(world * M / (ms * 1e-3), 1),
+                      "algorithmic_MB": round(avg_bytes / 1e6, 1), "union": unions,
+                      "GBs": round(gbs, 1), "frac_hbm": round(gbs / hbm_peak, 4)}
+        if clk is not None:
+            results[M]["clocks"] = clk
+        graphs_by_m[M], steps_by_m[M], bufs_by_m[M] = graphs, steps, bufs
+
+    M = args.rows
+    ms = results[M]["us_per_layer"] / 1e3
+    value = world * M / (ms * 1e-3)
+
+    # ---- stage timeline of the headline width (eager launches, CUDA events on the stream)
+    n1, n2 = len(abi.K1_STAGES), len(abi.K2_STAGES)
+    ev1 = [torch.cuda.Event(enable_timing=True) for _ in range(n1 + 1)]
+    ev2 = [torch.cuda.Event(enable_timing=True) for _ in range(n2 + 1)]
+    arr1 = (ctypes_events(ev1))
+    arr2 = (ctypes_events(ev2))
+    stage_ms = {k: 0.0 for k in abi.K1_STAGES + abi.K2_STAGES}
+    reps = max(3, min(args.steps, 10))
+    for i in range(reps):
+        L, st, b = layers[i % len(layers)], steps_by_m[M][i % len(layers)], bufs_by_m[M][i % len(layers)]
+        a1, _ = runner.k1_args(L, st, M, events=arr1.addr)
+        ext.call("dsv41_k1", a1, stream.cuda_stream)
+        a2 = runner.k2_args(L, st, M, b, events=arr2.addr)
+        ext.call("dsv41_k2", a2, stream.cuda_stream)
+        torch.cuda.synchronize()
+        for j, name in enumerate(abi.K1_STAGES):
+            stage_ms[name] += ev1[j].elapsed_time(ev1[j + 1]) / reps
+        for j, name in enumerate(abi.K2_STAGES):
+            stage_ms[name] += ev2[j].elapsed_time(ev2[j + 1]) / reps
+    union = sum(results[M]["union"]) / len(results[M]["union"])
+    exp_bytes = union * roofline.expert_bytes(shape)
+    t_exp = stage_ms["routed experts"] * 1e-3
+    achieved = exp_bytes / t_exp / 1e9
+
+    # ---- end to end through the C-ABI with host buffers
+    names = ("res", "x", "post", "comb", "pre", "pos", "slot", "swa_idx", "swa_lens")
+    host_in = [[st[n].cpu().pin_memory() for n in names] for st in steps_by_m[M]]
+    host_out = [[torch.empty_like(b[n], device="cpu").pin_memory() for n in ("out", "res2")]
+                for b in bufs_by_m[M]]
+    h2d = sum(t.numel() * t.element_size() for t in host_in[0])
+    d2h = sum(t.numel() * t.element_size() for t in host_out[0])
+    graphs = graphs_by_m[M]
+
+    def e2e_step(i):
+        k = i % len(graphs)
+        for n, t in zip(names, host_in[k]):
+            steps_by_m[M][k][n].copy_(t, non_blocking=True)
+        graphs[k].replay()
+        for n, t in zip(("out", "res2"), host_out[k]):
+            t.copy_(bufs_by_m[M][k][n], non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        W = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in layers[0].w.items()}
+        S = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in steps_by_m[M][0].items()}
+        cpu_layer(W, S, shape, 1)
+        t_cpu = min(cpu_layer(W, S, shape, 1) for _ in range(2))
+        cpu = {"value": 1.0 / t_cpu, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"1 decode row of the same layer (ctx {args.ctx}), best of 2 after a warm-up; "
+                         f"torch CPU oracle, {threads} threads"}
+        del W, S
+
+    if rank == 0:
+        clk = results[M].get("clocks", {"sm_mhz": None, "sm_max_mhz": None, "reasons": []})
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp8/mxfp4 weights, bf16 activations",
+            "data": "synthetic (random-init, seeded)",
+            "config": {"workload": f"config2: one MoE decode layer (K1 + K2), {M} rows, ctx {args.ctx}",
+                       "rows": M, "ctx": args.ctx, "tp": 1, "parallelism": f"replicas x{world}",
+                       "l2": f"steps alternate {args.layers} layer copies; a step reads "
+                             f"{results[M]['algorithmic_MB']} MB (> 126 MB L2)",
+                       "layer_roofline": {"GBs": results[M]["GBs"], "frac": results[M]["frac_hbm"],
+                                          "peak_GBs": hbm_peak, "peak": peak_src},
+                       "sweep": {str(k): {kk: vv for kk, vv in v.items() if kk != "clocks"}
+                                 for k, v in results.items()},
+                       "stages_us": {k: round(v * 1e3, 2) for k, v in stage_ms.items()}},
+            "roofline": {"bound": "hbm", "kernel": "routed experts (gate/up + act + down)",
+                         "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(achieved / hbm_peak, 4), "traffic": None,
+                         "algorithmic_bytes": int(exp_bytes), "peak_source": peak_src},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(world * M / (e2e_ms * 1e-3), 1), "unit": UNIT,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+
+
+class ctypes_events:
+    """A host array of cudaEvent_t handles for the C-ABI's stage events."""
+
+    def __init__(self, events):
+        import ctypes
+        for e in events:  # torch creates the CUDA event at its first record
+            e.record()
+        torch.cuda.synchronize()
+        self.arr = (ctypes.c_void_p * len(events))(*[e.cuda_event for e in events])
+        self.addr = ctypes.addressof(self.arr)
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -75,8 +75,12 @@ typedef struct {
   int64_t swa_idx, swa_lens, topk_idx, topk_lens, kt, klen;
   /* wq_b and outputs */
   int64_t wqb, wqb_codes, q, qr, qx8, qx8s, qkv_out;
+  /* optional host array of DSV41_K1_STAGES + 1 cudaEvent_t recorded at stage boundaries
+   * (seam, wqkv_a, q/kv, wq_b) for profiling; 0 = none */
+  int64_t events;
   int64_t scratch, scratch_bytes;
 } Dsv41K1Args;
+#define DSV41_K1_STAGES 4
 int64_t dsv41_k1_scratch_bytes(const Dsv41K1Args* a);
 int dsv41_k1(const Dsv41K1Args* a, void* stream);
 
@@ -102,8 +106,16 @@ typedef struct {
   int64_t out, ids, wts, xo, x8b, x8bs, attn_part, attn, logits, moe_part;
   /* tensor parallelism */
   int64_t peer_attn, peer_moe, peer_flags, epoch, deadline_ns;
+  /* optional host array of DSV41_K2_STAGES + 1 cudaEvent_t recorded at stage boundaries
+   * (attention, wo_a + wo_b, all-reduce + FFN seam, router + routing, shared expert,
+   * routed experts, combine + all-reduce); 0 = none */
+  int64_t events;
   int64_t scratch, scratch_bytes;
 } Dsv41K2Args;
+#define DSV41_K2_STAGES 7
+
+/* Kernels this library has launched in this process (all entry points): for profiling. */
+int64_t dsv41_launch_count(void);
 int64_t dsv41_k2_scratch_bytes(const Dsv41K2Args* a);
 int dsv41_k2(const Dsv41K2Args* a, void* stream);
 

@@ -237,22 +237,18 @@ def attention(q, kt, klen, swa, swa_blk, comp, comp_blk, sink, cos, sin, nope, r
     xo = torch.zeros(M, Hh, D)
     for t in range(M):
         n = int(klen[t])
-        vals = kt[t, :n].tolist()
-        rows = []
-        for v in vals:
-            if v == -1:
-                continue
-            if v < 0:
-                rows.append(("c", v & 0x7FFFFFFF))
-            else:
-                rows.append(("s", v))
-        if not rows:
+        vals = kt[t, :n].long()
+        vals = vals[vals != -1]
+        if vals.numel() == 0:
             continue
-        ks = []
-        for which, s in rows:
-            cache, blk = (comp, comp_blk) if which == "c" else (swa, swa_blk)
-            ks.append(read_records(cache, [s], blk, nope, rope, scale_bytes))
-        k = torch.cat(ks).double()
+        is_c = vals < 0
+        parts = []
+        if bool(is_c.any()):
+            parts.append(read_records(comp, (vals[is_c] & 0x7FFFFFFF), comp_blk, nope, rope, scale_bytes))
+        if bool((~is_c).any()):
+            parts.append(read_records(swa, vals[~is_c], swa_blk, nope, rope, scale_bytes))
+        # the key order inside a row does not change the softmax; keep compressed keys first
+        k = torch.cat(parts).double()
         s = (f32(q[t]).double() @ k.T) * (D ** -0.5)
         m = torch.maximum(s.amax(1), f32(sink).double())
         p = torch.exp(s - m[:, None])

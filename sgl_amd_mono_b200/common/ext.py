@@ -60,3 +60,11 @@ def query(fn: str, args: ctypes.Structure) -> int:
     f.restype = ctypes.c_int64
     f.argtypes = [ctypes.c_void_p]
     return check(int(f(ctypes.byref(args))), fn)
+
+
+def launch_count() -> int:
+    """Kernels the library has launched in this process."""
+    f = lib().dsv41_launch_count
+    f.restype = ctypes.c_int64
+    f.argtypes = []
+    return int(f())

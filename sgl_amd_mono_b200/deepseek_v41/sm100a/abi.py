@@ -19,9 +19,10 @@ K1Args = struct("Dsv41K1Args", [
     "wqkv", "wqkv_codes", "q_norm", "kv_norm", "cos_sin", "pos",
     "slot", "cache", "page_stride", "blk",
     "swa_idx", "swa_lens", "topk_idx", "topk_lens", "kt", "klen",
-    "wqb", "wqb_codes", "q", "qr", "qx8", "qx8s", "qkv_out",
+    "wqb", "wqb_codes", "q", "qr", "qx8", "qx8s", "qkv_out", "events",
     "scratch", "scratch_bytes",
 ])
+K1_STAGES = ("seam", "wqkv_a", "q/kv", "wq_b")
 
 K2Args = struct("Dsv41K2Args", [
     "M", "hidden", "nope", "rope", "heads", "o_groups", "o_rank",
@@ -33,9 +34,11 @@ K2Args = struct("Dsv41K2Args", [
     "res_out", "post_out", "comb_out", "pre_out", "normed",
     "gate_w", "bias", "w13", "w13_codes", "w2", "w2_codes", "sgu", "sgu_codes", "sw2", "sw2_codes",
     "out", "ids", "wts", "xo", "x8b", "x8bs", "attn_part", "attn", "logits", "moe_part",
-    "peer_attn", "peer_moe", "peer_flags", "epoch", "deadline_ns",
+    "peer_attn", "peer_moe", "peer_flags", "epoch", "deadline_ns", "events",
     "scratch", "scratch_bytes",
 ])
+K2_STAGES = ("attention", "wo_a+wo_b", "reduce+ffn seam", "router", "shared expert", "routed experts",
+             "combine+reduce")
 
 STRUCTS = {
     "Dsv41GemvArgs": GemvArgs,

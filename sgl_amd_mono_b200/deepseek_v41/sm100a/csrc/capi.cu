@@ -5,7 +5,10 @@
 // what the previous one wrote.
 #include <cstdio>
 #include <algorithm>
+#include <atomic>
 #include <cmath>
+#include <map>
+#include <mutex>
 #include <cstdlib>
 
 #include "../../../../include/dsv41_b200.h"
@@ -18,6 +21,20 @@
 #include "seam.cuh"
 
 using namespace dsv41;
+
+cudaError_t dsv41::ensure_smem(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> done;  // (kernel, device) -> bytes set
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_pair(kernel, dev);
+  auto it = done.find(key);
+  if (it != done.end() && it->second >= bytes) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done[key] = bytes;
+  return e;
+}
 
 namespace {
 
@@ -52,10 +69,23 @@ int launch_status() {
   return DSV41_OK;
 }
 
+std::atomic<int64_t> g_launches{0};
+
+// Record stage-boundary event i of an optional host array of cudaEvent_t.
+void mark(int64_t events, int i, cudaStream_t st) {
+  if (events) cudaEventRecord(reinterpret_cast<cudaEvent_t*>(events)[i], st);
+}
+
+cudaError_t gemv_go(const GemvArgs& g, cudaStream_t st) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return gemv_launch(g, st, use_pdl());
+}
+
 template <typename Kern, typename Args>
 cudaError_t launch(Kern kernel, dim3 grid, dim3 block, int smem, cudaStream_t st, const Args& args) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = ensure_smem(reinterpret_cast<const void*>(kernel), smem);
     if (e != cudaSuccess) return e;
   }
   cudaLaunchConfig_t cfg = {};
@@ -182,9 +212,12 @@ int k1_run(const Dsv41K1Args* a, cudaStream_t st, bool go, int64_t* need) {
   s.norm_w = ptr<const __nv_bfloat16>(a->norm_w);
   s.res_out = res_out; s.pre_out = pre_out; s.post_out = post_out; s.comb_out = comb_out;
   s.normed = normed; s.x8 = x8; s.x8s = x8s; s.xq = xq; s.lin = lin; s.part = part;
+  mark(a->events, 0, st);
   DSV41_TRY(launch(seam_slice_kernel, dim3(H / kSliceCols), dim3(256), 0, st, s));
   DSV41_TRY(launch(seam_gate_norm_kernel, dim3(M), dim3(256), 0, st, s));
-  DSV41_TRY(gemv_launch(g1, st, use_pdl()));
+  mark(a->events, 1, st);
+  DSV41_TRY(gemv_go(g1, st));
+  mark(a->events, 2, st);
   FrontArgs f = {};
   f.M = M; f.QL = QL; f.KVD = D; f.nope = nope; f.rope = rope; f.kslices = g1.kslices;
   f.index = (int)a->index; f.qkv_part = g1.out;
@@ -204,12 +237,14 @@ int k1_run(const Dsv41K1Args* a, cudaStream_t st, bool go, int64_t* need) {
     k.klen = ptr<int32_t>(a->klen);
     DSV41_TRY(launch(key_table_kernel, dim3(M), dim3(256), 0, st, k));
   }
-  DSV41_TRY(gemv_launch(g2, st, use_pdl()));
+  mark(a->events, 3, st);
+  DSV41_TRY(gemv_go(g2, st));
   QRopeArgs qr = {};
   qr.M = M; qr.heads = heads; qr.D = D; qr.nope = nope; qr.rope = rope; qr.kslices = g2.kslices;
   qr.part = g2.out; qr.cos_sin = ptr<const float>(a->cos_sin); qr.pos = ptr<const int64_t>(a->pos);
   qr.q = ptr<__nv_bfloat16>(a->q);
   DSV41_TRY(launch(q_rope_kernel, dim3(cdiv(heads * D / 2, 256), M), dim3(256), 0, st, qr));
+  mark(a->events, 4, st);
   return launch_status();
 }
 
@@ -322,6 +357,7 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   at.comp = ptr<const uint8_t>(a->comp); at.comp_stride = a->comp_stride; at.comp_blk = (int)(a->comp_blk ? a->comp_blk : 1);
   at.scale_log2 = (float)(1.0 / sqrt((double)D) * 1.4426950408889634);
   at.part_o = part_o; at.part_ml = part_ml;
+  mark(a->events, 0, st);
   DSV41_TRY(launch(attn_split_kernel, dim3(M * nchunks * head_tiles), dim3(256), attn_smem_bytes(D), st, at));
   CombineArgs cb = {};
   cb.M = M; cb.heads = heads; cb.D = D; cb.nope = nope; cb.rope = rope; cb.nchunks = nchunks;
@@ -329,12 +365,14 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   cb.cos_sin = ptr<const float>(a->cos_sin); cb.pos = ptr<const int64_t>(a->pos); cb.xo = xo;
   DSV41_TRY(launch(attn_combine_kernel, dim3(M * heads), dim3(128), 0, st, cb));
   // ---- wo_a -> X8B -> wo_b -> partial -> reduce
-  DSV41_TRY(gemv_launch(ga, st, use_pdl()));
+  mark(a->events, 1, st);
+  DSV41_TRY(gemv_go(ga, st));
   FinalizeArgs fa = {M, G * O, ga.kslices, ga.out, x8bq, x8b, x8bs};
   DSV41_TRY(launch(finalize_kernel, dim3(grid_for((int64_t)M * G * O / 8, 256)), dim3(256), 0, st, fa));
-  DSV41_TRY(gemv_launch(gb, st, use_pdl()));
+  DSV41_TRY(gemv_go(gb, st));
   FinalizeArgs fb = {M, H, gb.kslices, gb.out, attn_part, nullptr, nullptr};
   DSV41_TRY(launch(finalize_kernel, dim3(grid_for((int64_t)M * H / 8, 256)), dim3(256), 0, st, fb));
+  mark(a->events, 2, st);
   // tp == 1: the all-reduce of one rank's bf16 partial is the partial itself
   const __nv_bfloat16* reduced = attn_part;
   if (attn != attn_part) {
@@ -356,6 +394,7 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   DSV41_TRY(launch(seam_gate_norm_kernel, dim3(M), dim3(256), 0, st, s));
   // ---- router, routing, union
   RouterArgs ra = {M, E, H, normed, ptr<const __nv_bfloat16>(a->gate_w), logits};
+  mark(a->events, 3, st);
   DSV41_TRY(launch(router_kernel, dim3(cdiv(E, 8), cdiv(M, 8)), dim3(256), 0, st, ra));
   RouteArgs rt = {M, E, TK, (int)a->route_softmax, logits, ptr<const float>(a->bias),
                   ptr<int32_t>(a->ids), ptr<float>(a->wts)};
@@ -363,10 +402,12 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   PlanArgs pl = {M, E, TK, ptr<const int32_t>(a->ids), n_u, u_expert, u_off, picks};
   DSV41_TRY(launch(moe_plan_kernel, dim3(1), dim3(512), 0, st, pl));
   // ---- shared expert
-  DSV41_TRY(gemv_launch(gs, st, use_pdl()));
+  mark(a->events, 4, st);
+  DSV41_TRY(gemv_go(gs, st));
   SharedActArgs sa = {M, SI, gs.kslices, gs.out, smq, smqs, smx};
   DSV41_TRY(launch(shared_act_kernel, dim3(grid_for((int64_t)M * SI / 8, 256)), dim3(256), 0, st, sa));
-  DSV41_TRY(gemv_launch(gd, st, use_pdl()));
+  DSV41_TRY(gemv_go(gd, st));
+  mark(a->events, 5, st);
   // ---- routed experts
   DSV41_TRY(launch(expert_gemv_kernel, dim3(max_units * eu.row_groups * eu.kslices), dim3(256),
                    expert_smem_bytes(eu.ks_len), st, eu));
@@ -375,16 +416,20 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   DSV41_TRY(launch(expert_gemv_kernel, dim3(max_units * ed.row_groups * ed.kslices), dim3(256),
                    expert_smem_bytes(ed.ks_len), st, ed));
   CombineMoeArgs cm = {M, H, TK, ed.kslices, gd.kslices, ed.out, ptr<const float>(a->wts), gd.out, moe_part};
+  mark(a->events, 6, st);
   DSV41_TRY(launch(moe_combine_kernel, dim3(grid_for((int64_t)M * H, 256)), dim3(256), 0, st, cm));
   // tp == 1: the MoE all-reduce of one partial is the partial
   if (ptr<__nv_bfloat16>(a->out) != moe_part)
     DSV41_TRY(cudaMemcpyAsync(ptr<void>(a->out), moe_part, (size_t)M * H * 2, cudaMemcpyDeviceToDevice, st));
+  mark(a->events, 7, st);
   return launch_status();
 }
 
 }  // namespace
 
 extern "C" {
+
+int64_t dsv41_launch_count(void) { return g_launches.load(); }
 
 int dsv41_version(void) { return 1; }
 int dsv41_arch(void) { return 100; }

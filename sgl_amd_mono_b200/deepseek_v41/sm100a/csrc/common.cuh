@@ -186,4 +186,8 @@ __device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.laun
 
 __host__ __device__ __forceinline__ int cdiv(int a, int b) { return (a + b - 1) / b; }
 
+// Raise a kernel's dynamic shared-memory limit once per (kernel, device) -- not on every
+// launch, so launches captured into a CUDA graph make no attribute calls after the first.
+cudaError_t ensure_smem(const void* kernel, int bytes);
+
 }  // namespace dsv41

@@ -267,7 +267,8 @@ inline cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t st, bool pdl) {
 #define DSV41_GEMV_CASE(NT)                                                                 \
   case NT: {                                                                                \
     auto k = gemv_fp8_kernel<NT>;                                                           \
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);             \
+    cudaError_t e = ensure_smem(reinterpret_cast<const void*>(k), smem);                    \
+    if (e != cudaSuccess) return e;                                                         \
     return cudaLaunchKernelEx(&cfg, k, a);                                                  \
   }
   switch (nt) {

@@ -112,9 +112,12 @@ class MonoRunner:
                 normed_f=z(M, H, dt=bf), out=z(M, H, dt=bf), ids=z(M, s.topk, dt=i32),
                 wts=z(M, s.topk), xo=z(M, s.heads_local * D, dt=bf),
                 x8b=z(M, s.groups_local * s.o_rank, dt=u8), x8bs=z(M, s.groups_local * s.o_rank // 32, dt=u8),
-                attn_part=z(M, H, dt=bf), attn=z(M, H, dt=bf), logits=z(M, s.experts),
-                moe_part=z(M, H, dt=bf),
+                attn_part=z(M, H, dt=bf), logits=z(M, s.experts),
             )
+            b = self._bufs[key]
+            # one rank: the reduced attention output is the partial, the MoE output its partial
+            b["attn"] = b["attn_part"] if s.tp == 1 else z(M, H, dt=bf)
+            b["moe_part"] = b["out"] if s.tp == 1 else z(M, H, dt=bf)
         return self._bufs[key]
 
     def _scratch_for(self, kind: str, M: int, need: int) -> torch.Tensor:
@@ -127,7 +130,7 @@ class MonoRunner:
 
     # ------------------------------------------------------------ K1
     def k1_args(self, L: Layer, step: dict, M: int, *, fold=True, first=False, index=False,
-                build_kt=True, swa_width=None, topk_width=0, topk_idx=None, topk_lens=None):
+                build_kt=True, swa_width=None, topk_width=0, topk_idx=None, topk_lens=None, events=0):
         s = self.s
         keys = (swa_width or step["swa_idx"].shape[1]) + topk_width
         b = self.buffers(M, keys)
@@ -147,7 +150,8 @@ class MonoRunner:
             swa_idx=_p(step["swa_idx"]), swa_lens=_p(step["swa_lens"]), topk_idx=_p(topk_idx),
             topk_lens=_p(topk_lens), kt=_p(b["kt"]), klen=_p(b["klen"]),
             wqb=_p(w["wqb"]), wqb_codes=_p(w["wqb_s"]), q=_p(b["q"]), qr=_p(b["qr"]),
-            qx8=_p(b["qx8"]), qx8s=_p(b["qx8s"]), qkv_out=_p(b["qkv"]), scratch=0, scratch_bytes=0,
+            qx8=_p(b["qx8"]), qx8s=_p(b["qx8s"]), qkv_out=_p(b["qkv"]), events=events, scratch=0,
+            scratch_bytes=0,
         )
         need = ext.query("dsv41_k1_scratch_bytes", a)
         sc = self._scratch_for("k1", M, need)
@@ -160,7 +164,8 @@ class MonoRunner:
         return b
 
     # ------------------------------------------------------------ K2
-    def k2_args(self, L: Layer, step: dict, M: int, b: dict, *, comp=None, comp_stride=0, comp_blk=0):
+    def k2_args(self, L: Layer, step: dict, M: int, b: dict, *, comp=None, comp_stride=0, comp_blk=0,
+                events=0):
         s = self.s
         w = L
         a = abi.K2Args(
@@ -183,6 +188,7 @@ class MonoRunner:
             out=_p(b["out"]), ids=_p(b["ids"]), wts=_p(b["wts"]), xo=_p(b["xo"]), x8b=_p(b["x8b"]),
             x8bs=_p(b["x8bs"]), attn_part=_p(b["attn_part"]), attn=_p(b["attn"]), logits=_p(b["logits"]),
             moe_part=_p(b["moe_part"]), peer_attn=0, peer_moe=0, peer_flags=0, epoch=0, deadline_ns=0,
+            events=events,
             scratch=0, scratch_bytes=0,
         )
         need = ext.query("dsv41_k2_scratch_bytes", a)
