@@ -42,6 +42,17 @@ typedef struct {
 int64_t dsv41_gemv_fp8_scratch_bytes(const Dsv41GemvArgs* a);
 int dsv41_gemv_fp8(const Dsv41GemvArgs* a, void* stream);
 
+/* The same GEMV for callers that cannot allocate device memory (a server whose KV-cache pool
+ * took the spare HBM at start-up, a foreign runtime without a device allocator): the K-slice
+ * partials go to a library-owned device array of DSV41_NOALLOC_SCRATCH_BYTES (held by every
+ * GPU that loads the library until exit) instead of caller scratch; scratch and
+ * scratch_bytes are ignored. A shape whose partials exceed the array returns DSV41_ESCRATCH.
+ * The first call on a device resolves the array's address there; make it before any stream
+ * capture. All calls share the array: calls that overlap on the GPU race. No counterpart in
+ * the reference (its launches take caller buffers only). */
+#define DSV41_NOALLOC_SCRATCH_BYTES (4 << 20)
+int dsv41_gemv_fp8_noalloc(const Dsv41GemvArgs* a, void* stream);
+
 /* ---------------------------------------------------------------- MXFP4 expert relayout
  * One-time copy of routed-expert weights from the checkpoint layout -- w [E, N, K/2] E2M1
  * (even K in the low nibble) with E8M0 codes [E, N, K/32] -- into the kernels' fragment
