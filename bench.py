@@ -41,8 +41,8 @@ UNIT = "tokens/s"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--rows", type=int, default=48, help="headline decode rows M")
     ap.add_argument("--sweep", default="1,4,16,48")
     ap.add_argument("--ctx", type=int, default=8192)
@@ -96,7 +96,7 @@ class Clocks:
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={self.QUERY}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                       "--format=csv,noheader,nounits", "-lms", "50"],
                                       stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
@@ -271,25 +271,31 @@ def run_ours(args, world, rank, local):
     ms = results[M]["us_per_layer"] / 1e3
     value = world * M / (ms * 1e-3)
 
-    # ---- stage timeline of the headline width (eager launches, CUDA events on the stream)
+    # ---- stage timelines (eager launches, CUDA events at stage boundaries on the stream)
     n1, n2 = len(abi.K1_STAGES), len(abi.K2_STAGES)
     ev1 = [torch.cuda.Event(enable_timing=True) for _ in range(n1 + 1)]
     ev2 = [torch.cuda.Event(enable_timing=True) for _ in range(n2 + 1)]
     arr1 = (ctypes_events(ev1))
     arr2 = (ctypes_events(ev2))
-    stage_ms = {k: 0.0 for k in abi.K1_STAGES + abi.K2_STAGES}
     reps = max(3, min(args.steps, 10))
-    for i in range(reps):
-        L, st, b = layers[i % len(layers)], steps_by_m[M][i % len(layers)], bufs_by_m[M][i % len(layers)]
-        a1, _ = runner.k1_args(L, st, M, events=arr1.addr)
-        ext.call("dsv41_k1", a1, stream.cuda_stream)
-        a2 = runner.k2_args(L, st, M, b, events=arr2.addr)
-        ext.call("dsv41_k2", a2, stream.cuda_stream)
-        torch.cuda.synchronize()
-        for j, name in enumerate(abi.K1_STAGES):
-            stage_ms[name] += ev1[j].elapsed_time(ev1[j + 1]) / reps
-        for j, name in enumerate(abi.K2_STAGES):
-            stage_ms[name] += ev2[j].elapsed_time(ev2[j + 1]) / reps
+    stages_by_m = {}
+    for Ms in sweep:
+        sm = {k: 0.0 for k in abi.K1_STAGES + abi.K2_STAGES}
+        for i in range(reps):
+            k = i % len(layers)
+            L, st, b = layers[k], steps_by_m[Ms][k], bufs_by_m[Ms][k]
+            a1, _ = runner.k1_args(L, st, Ms, events=arr1.addr)
+            ext.call("dsv41_k1", a1, stream.cuda_stream)
+            a2 = runner.k2_args(L, st, Ms, b, events=arr2.addr)
+            ext.call("dsv41_k2", a2, stream.cuda_stream)
+            torch.cuda.synchronize()
+            for j, name in enumerate(abi.K1_STAGES):
+                sm[name] += ev1[j].elapsed_time(ev1[j + 1]) / reps
+            for j, name in enumerate(abi.K2_STAGES):
+                sm[name] += ev2[j].elapsed_time(ev2[j + 1]) / reps
+        stages_by_m[Ms] = sm
+        results[Ms]["stages_us"] = {k: round(v * 1e3, 1) for k, v in sm.items()}
+    stage_ms = stages_by_m[M]
     union = sum(results[M]["union"]) / len(results[M]["union"])
     exp_bytes = union * roofline.expert_bytes(shape)
     t_exp = stage_ms["routed experts"] * 1e-3

@@ -39,7 +39,7 @@ constexpr int kSub = 64;  // keys a sub-block
 
 __host__ __device__ inline int attn_smem_bytes(int D) {
   return 16 * (D + 8) * 2 + kSub * (D + 8) * 2 + 2 * 16 * (kSub + 8) * 2 + 2 * 8 * 16 * 4 +
-         kSub * 8 + kSub * 8;
+         2 * kSub * 8 + 2 * kSub * 8;
 }
 
 __global__ void __launch_bounds__(256, 2) attn_split_kernel(const AttnArgs a) {
@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(256, 2) attn_split_kernel(const AttnArgs a) {
   float* redm = reinterpret_cast<float*>(Pl + 16 * (kSub + 8));
   float* redl = redm + 8 * 16;
   const uint8_t** kdata = reinterpret_cast<const uint8_t**>(redl + 8 * 16);
-  uint64_t* kcodes = reinterpret_cast<uint64_t*>(kdata + kSub);
+  uint64_t* kcodes = reinterpret_cast<uint64_t*>(kdata + 2 * kSub);
 
   const int ht = blockIdx.x % a.head_tiles;
   const int ch = (blockIdx.x / a.head_tiles) % a.nchunks;
@@ -82,49 +82,80 @@ __global__ void __launch_bounds__(256, 2) attn_split_kernel(const AttnArgs a) {
     for (int i = 0; i < 4; ++i) o[n][i] = 0.f;
   const int data_bytes = a.nope + 2 * a.rope;
 
-  for (int kb = k0; kb < k1; kb += kSub) {
-    // ---- resolve this sub-block's keys
+  // key k of the row -> its record's data pointer (null: masked) and its 8 scale codes
+  auto resolve = [&](int k, const uint8_t*& dp, uint64_t& cw) {
+    dp = nullptr;
+    cw = 0;
+    if (k >= k1) return;
+    const int v = a.kt[(size_t)t * a.keys_ld + k];
+    if (v == -1) return;
+    const bool comp = v < 0 && a.comp != nullptr;
+    if (v < 0 && !comp) return;
+    const int s = v & 0x7fffffff;
+    const int blk = comp ? a.comp_blk : a.swa_blk;
+    const uint8_t* page = (comp ? a.comp : a.swa) + (int64_t)(s / blk) * (comp ? a.comp_stride : a.swa_stride);
+    const int off = s % blk;
+    dp = page + (size_t)off * data_bytes;
+    cw = *reinterpret_cast<const uint64_t*>(page + (size_t)blk * data_bytes + (size_t)off * 8);
+  };
+  const uint8_t* ndp = nullptr;
+  uint64_t ncw = 0;
+  if (tid < kSub) resolve(k0 + tid, ndp, ncw);
+  int buf = 0;
+  for (int kb = k0; kb < k1; kb += kSub, buf ^= 1) {
+    const uint8_t** kd = kdata + buf * kSub;
+    const uint64_t* kc = kcodes + buf * kSub;
     if (tid < kSub) {
-      const int k = kb + tid;
-      const uint8_t* dp = nullptr;
-      uint64_t cw = 0;
-      if (k < k1) {
-        const int v = a.kt[(size_t)t * a.keys_ld + k];
-        if (v != -1) {
-          const bool comp = v < 0 && a.comp != nullptr;
-          const int s = v & 0x7fffffff;
-          const int blk = comp ? a.comp_blk : a.swa_blk;
-          const uint8_t* page = (comp ? a.comp : a.swa) + (int64_t)(s / blk) * (comp ? a.comp_stride : a.swa_stride);
-          const int off = s % blk;
-          if (v >= 0 || comp) {
-            dp = page + (size_t)off * data_bytes;
-            cw = *reinterpret_cast<const uint64_t*>(page + (size_t)blk * data_bytes + (size_t)off * 8);
-          }
-        }
-      }
-      kdata[tid] = dp;
-      kcodes[tid] = cw;
+      kdata[buf * kSub + tid] = ndp;
+      kcodes[buf * kSub + tid] = ncw;
     }
     __syncthreads();
-    // ---- dequantize into the bf16 K/V tile
-    const int chunks = data_bytes / 16;
-    for (int e = tid; e < kSub * chunks; e += blockDim.x) {
+    // ---- every record load of the sub-block in flight at once, then the next sub-block's keys
+    const int chunks = data_bytes / 16;  // <= 40 (nope <= 512, rope 64)
+    constexpr int kItems = kSub * 40 / 256;
+    uint4 raw[kItems];
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) {
+      const int e = tid + 256 * i;
+      raw[i] = make_uint4(0, 0, 0, 0);
+      if (e < kSub * chunks) {
+        const uint8_t* dp = kd[e / chunks];
+        if (dp) raw[i] = ldg16(dp + 16 * (e % chunks));
+      }
+    }
+    if (tid < kSub) resolve(kb + kSub + tid, ndp, ncw);
+    // ---- dequantize into the fp16 K/V tile
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) {
+      const int e = tid + 256 * i;
+      if (e >= kSub * chunks) continue;
       const int k = e / chunks, c = e % chunks;
-      const uint8_t* dp = kdata[k];
+      const uint8_t* dp = kd[k];
       uint4 out0 = make_uint4(0, 0, 0, 0), out1 = make_uint4(0, 0, 0, 0);
       const int b0 = 16 * c;
       if (b0 < a.nope) {
         if (dp) {
-          const uint4 raw = ldg16(dp + b0);
-          const int code = (int)((kcodes[k] >> (8 * (b0 / 64))) & 0xff);
-          const float sc = pow2c(code);
-          const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+          const int code = (int)((kc[k] >> (8 * (b0 / 64))) & 0xff);
+          const uint32_t w[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
           uint32_t r[8];
+          if (code >= 113 && code <= 134) {
+            // e4m3 -> f16 is exact, and so is the product by 2^(code-127) in this code range
+            // (no f16 overflow; the smallest e4m3 subnormal stays on f16's subnormal grid)
+            const uint32_t s1 = (uint32_t)(code - 112) << 10;
+            const uint32_t s2 = s1 | (s1 << 16);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 fl = e4m3x2_float2(w[i] & 0xffff), fh = e4m3x2_float2(w[i] >> 16);
-            r[2 * i] = pack_f16x2(fl.x * sc, fl.y * sc);
-            r[2 * i + 1] = pack_f16x2(fh.x * sc, fh.y * sc);
+            for (int i = 0; i < 4; ++i) {
+              r[2 * i] = hmul2_bits(e4m3x2_f16(w[i] & 0xffff), s2);
+              r[2 * i + 1] = hmul2_bits(e4m3x2_f16(w[i] >> 16), s2);
+            }
+          } else {
+            const float sc = pow2c(code);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float2 fl = e4m3x2_float2(w[i] & 0xffff), fh = e4m3x2_float2(w[i] >> 16);
+              r[2 * i] = pack_f16x2(fl.x * sc, fl.y * sc);
+              r[2 * i + 1] = pack_f16x2(fh.x * sc, fh.y * sc);
+            }
           }
           out0 = make_uint4(r[0], r[1], r[2], r[3]);
           out1 = make_uint4(r[4], r[5], r[6], r[7]);
@@ -133,9 +164,8 @@ __global__ void __launch_bounds__(256, 2) attn_split_kernel(const AttnArgs a) {
         *reinterpret_cast<uint4*>(Ks + k * ld + b0 + 8) = out1;
       } else {
         if (dp) {
-          out0 = ldg16(dp + b0);
-          out0 = make_uint4(bf16x2_to_f16x2(out0.x), bf16x2_to_f16x2(out0.y), bf16x2_to_f16x2(out0.z),
-                            bf16x2_to_f16x2(out0.w));
+          out0 = make_uint4(bf16x2_to_f16x2(raw[i].x), bf16x2_to_f16x2(raw[i].y), bf16x2_to_f16x2(raw[i].z),
+                            bf16x2_to_f16x2(raw[i].w));
         }
         *reinterpret_cast<uint4*>(Ks + k * ld + a.nope + (b0 - a.nope) / 2) = out0;
       }
@@ -144,21 +174,37 @@ __global__ void __launch_bounds__(256, 2) attn_split_kernel(const AttnArgs a) {
     // ---- S = Q K^T: warp w takes keys 8 w .. 8 w + 7
     float s[4] = {0.f, 0.f, 0.f, 0.f};
     {
+      // three independent accumulation chains over the head dims, summed at the end
+      float s1[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
       const uint32_t qa = smem_u32(Qs) + (uint32_t)((((lane & 7) + 8 * ((lane >> 3) & 1)) * ld + 8 * (lane >> 4)) * 2);
       const uint32_t kbase = smem_u32(Ks) + (uint32_t)(((8 * warp + (lane & 7)) * ld + 8 * ((lane >> 3) & 1)) * 2);
-      for (int kk = 0; kk < D / 16; ++kk) {
+      int kk = 0;
+      for (; kk + 2 < D / 16; kk += 3) {
+        uint32_t af[3][4], bfr[3][2];
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+          ldmatrix_x4(af[j], qa + (kk + j) * 32);
+          ldmatrix_x2(bfr[j], kbase + (kk + j) * 32);
+        }
+        mma_f16(s, af[0][0], af[0][1], af[0][2], af[0][3], bfr[0][0], bfr[0][1]);
+        mma_f16(s1, af[1][0], af[1][1], af[1][2], af[1][3], bfr[1][0], bfr[1][1]);
+        mma_f16(s2, af[2][0], af[2][1], af[2][2], af[2][3], bfr[2][0], bfr[2][1]);
+      }
+      for (; kk < D / 16; ++kk) {
         uint32_t af[4], bfr[2];
         ldmatrix_x4(af, qa + kk * 32);
         ldmatrix_x2(bfr, kbase + kk * 32);
-        mma_f16(s, af[0], af[1], af[2], af[3], bfr[0], bfr[1]);
+        mma_f16(s1, af[0], af[1], af[2], af[3], bfr[0], bfr[1]);
       }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) s[i] = (s[i] + s1[i]) + s2[i];
     }
     // scale and mask; per-head max of this warp's keys
     float mx[2];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int key = 8 * warp + 2 * tq + (i & 1);
-      s[i] = kdata[key] ? s[i] * a.scale_log2 : -INFINITY;
+      s[i] = kd[key] ? s[i] * a.scale_log2 : -INFINITY;
     }
     mx[0] = fmaxf(s[0], s[1]);
     mx[1] = fmaxf(s[2], s[3]);

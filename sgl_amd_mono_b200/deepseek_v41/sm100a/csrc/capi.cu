@@ -235,7 +235,9 @@ int k1_run(const Dsv41K1Args* a, cudaStream_t st, bool go, int64_t* need) {
     k.swa_lens = ptr<const int32_t>(a->swa_lens); k.topk = ptr<const int32_t>(a->topk_idx);
     k.topk_lens = ptr<const int32_t>(a->topk_lens); k.kt = ptr<int32_t>(a->kt);
     k.klen = ptr<int32_t>(a->klen);
-    DSV41_TRY(launch(key_table_kernel, dim3(M), dim3(256), 0, st, k));
+    const int kt_keys = (int)(a->swa_width + a->topk_width);
+    DSV41_TRY(launch(key_table_kernel, dim3(M, std::max(1, std::min(cdiv(kt_keys, 1024), 16))), dim3(256), 0,
+                     st, k));
   }
   mark(a->events, 3, st);
   DSV41_TRY(gemv_go(g2, st));
@@ -398,7 +400,7 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   DSV41_TRY(launch(router_kernel, dim3(cdiv(E, 8), cdiv(M, 8)), dim3(256), 0, st, ra));
   RouteArgs rt = {M, E, TK, (int)a->route_softmax, logits, ptr<const float>(a->bias),
                   ptr<int32_t>(a->ids), ptr<float>(a->wts)};
-  DSV41_TRY(launch(route_kernel, dim3(M), dim3(32), 0, st, rt));
+  DSV41_TRY(launch(route_kernel, dim3(M), dim3(256), 0, st, rt));
   PlanArgs pl = {M, E, TK, ptr<const int32_t>(a->ids), n_u, u_expert, u_off, picks};
   DSV41_TRY(launch(moe_plan_kernel, dim3(1), dim3(512), 0, st, pl));
   // ---- shared expert
@@ -409,11 +411,12 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   DSV41_TRY(gemv_go(gd, st));
   mark(a->events, 5, st);
   // ---- routed experts
-  DSV41_TRY(launch(expert_gemv_kernel, dim3(max_units * eu.row_groups * eu.kslices), dim3(256),
+  // persistent: exactly the resident CTAs (two an SM), each looping over work items
+  DSV41_TRY(launch(expert_gemv_kernel, dim3(std::min(2 * sms, max_units * eu.row_groups * eu.kslices)), dim3(256),
                    expert_smem_bytes(eu.ks_len), st, eu));
   ExpertActArgs ea = {P, I, eu.kslices, eu.out, mid, mids};
   DSV41_TRY(launch(expert_act_kernel, dim3(grid_for((int64_t)P * I / 8, 256)), dim3(256), 0, st, ea));
-  DSV41_TRY(launch(expert_gemv_kernel, dim3(max_units * ed.row_groups * ed.kslices), dim3(256),
+  DSV41_TRY(launch(expert_gemv_kernel, dim3(std::min(2 * sms, max_units * ed.row_groups * ed.kslices)), dim3(256),
                    expert_smem_bytes(ed.ks_len), st, ed));
   CombineMoeArgs cm = {M, H, TK, ed.kslices, gd.kslices, ed.out, ptr<const float>(a->wts), gd.out, moe_part};
   mark(a->events, 6, st);

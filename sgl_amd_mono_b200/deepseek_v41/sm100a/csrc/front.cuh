@@ -207,7 +207,7 @@ __global__ void key_table_kernel(const KeyTableArgs a) {
   const int ntopk = (live && a.topk_width > 0) ? min(a.topk_lens[t], a.topk_width) : 0;
   const int kv = ntopk + nswa;
   const int keys = a.topk_width + a.swa_width;
-  for (int k = threadIdx.x; k < keys; k += blockDim.x) {
+  for (int k = blockIdx.y * blockDim.x + threadIdx.x; k < keys; k += gridDim.y * blockDim.x) {
     int v = -1;
     if (k < ntopk) {
       const int c = a.topk[(size_t)t * a.topk_width + k];
@@ -218,7 +218,7 @@ __global__ void key_table_kernel(const KeyTableArgs a) {
     }
     a.kt[(size_t)t * keys + k] = v;
   }
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0 && blockIdx.y == 0) {
     a.klen[t] = kv;
     a.klen[a.M + t] = ntopk;
   }

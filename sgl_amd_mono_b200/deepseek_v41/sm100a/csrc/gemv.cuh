@@ -116,6 +116,34 @@ __global__ void __launch_bounds__(256, 2) gemv_fp8_kernel(const GemvArgs a) {
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem);
   float* red = reinterpret_cast<float*>(smem + MP * xs_ld * 2);
 
+  const int wk = a.wk;
+  const int lanes = 8 / wk;
+  const int wt = warp / wk, wkk = warp - wt * wk;
+  const int nb = kb1 - kb0;
+  const int kw0 = wkk * nb / wk, kw1 = (wkk + 1) * nb / wk;
+  const int nsteps = 2 * (kw1 - kw0);
+  const int ntiles_local = cdiv(tile1 - tile0 - wt, lanes);
+  constexpr int PF = 4;
+  uint4 wa[PF], wb[PF];
+  auto tile_ptrs = [&](int it, const uint8_t*& p0, const uint8_t*& p1) {
+    const int row0 = (tile0 + wt + it * lanes) * 16;
+    const int r0 = min(row0 + g, a.N - 1), r1 = min(row0 + g + 8, a.N - 1);
+    p0 = a.w + (size_t)r0 * a.K + (size_t)(kb0 + kw0) * 128 + 16 * t;
+    p1 = a.w + (size_t)r1 * a.K + (size_t)(kb0 + kw0) * 128 + 16 * t;
+  };
+  // the weights wait on nothing: stream the first tile's first steps before the dependency
+  // wait, overlapping the previous kernel's tail (programmatic dependent launch)
+  if (ntiles_local > 0) {
+    const uint8_t *p0, *p1;
+    tile_ptrs(0, p0, p1);
+#pragma unroll
+    for (int i = 0; i < PF; ++i)
+      if (i < nsteps) {
+        wa[i] = ldg_stream(p0 + 64 * i);
+        wb[i] = ldg_stream(p1 + 64 * i);
+      }
+  }
+
   pdl_wait();
   // ---- stage x's K slice, permuted into mma slot order and scaled by 2^64
   {
@@ -138,23 +166,15 @@ __global__ void __launch_bounds__(256, 2) gemv_fp8_kernel(const GemvArgs a) {
   }
   __syncthreads();
 
-  const int wk = a.wk;
-  const int lanes = 8 / wk;
-  const int wt = warp / wk, wkk = warp - wt * wk;
-  const int nb = kb1 - kb0;
-  const int kw0 = wkk * nb / wk, kw1 = (wkk + 1) * nb / wk;
-  const int nsteps = 2 * (kw1 - kw0);
   const uint32_t xs_base = smem_u32(xs);
   // ldmatrix row address of this lane: token (lane & 7) of the n-tile, 8 slots at 8 * (lane >> 3)
   const uint32_t lm_off = ((lane & 7) * xs_ld + 8 * (lane >> 3)) * 2;
-  const int ntiles_local = cdiv(tile1 - tile0 - wt, lanes);
 
   for (int it = 0; it < ntiles_local; ++it) {
     const int tile = tile0 + wt + it * lanes;
     const int row0 = tile * 16;
-    const int r0 = min(row0 + g, a.N - 1), r1 = min(row0 + g + 8, a.N - 1);
-    const uint8_t* p0 = a.w + (size_t)r0 * a.K + (size_t)(kb0 + kw0) * 128 + 16 * t;
-    const uint8_t* p1 = a.w + (size_t)r1 * a.K + (size_t)(kb0 + kw0) * 128 + 16 * t;
+    const uint8_t *p0, *p1;
+    tile_ptrs(it, p0, p1);
     const uint8_t* cp = a.codes + (size_t)(row0 >> 7) * nblocks + kb0 + kw0;
     float acc[NT][4];
     float blk[NT][4];
@@ -163,14 +183,14 @@ __global__ void __launch_bounds__(256, 2) gemv_fp8_kernel(const GemvArgs a) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[n][i] = blk[n][i] = 0.f;
 
-    constexpr int PF = 4;
-    uint4 wa[PF], wb[PF];
+    if (it > 0) {
 #pragma unroll
-    for (int i = 0; i < PF; ++i)
-      if (i < nsteps) {
-        wa[i] = ldg_stream(p0 + 64 * i);
-        wb[i] = ldg_stream(p1 + 64 * i);
-      }
+      for (int i = 0; i < PF; ++i)
+        if (i < nsteps) {
+          wa[i] = ldg_stream(p0 + 64 * i);
+          wb[i] = ldg_stream(p1 + 64 * i);
+        }
+    }
     for (int s0 = 0; s0 < nsteps; s0 += PF) {
 #pragma unroll
       for (int i = 0; i < PF; ++i) {

@@ -146,46 +146,56 @@ __device__ __forceinline__ void mx_group_store(const float (&v)[8], bool vllm, u
 __global__ void __launch_bounds__(256) seam_gate_norm_kernel(const SeamArgs a) {
   __shared__ float red[8];
   __shared__ float tot_s;
-  const int t = blockIdx.x, H = a.H, tid = threadIdx.x;
+  __shared__ float gsum[8][kPart];
+  const int t = blockIdx.x, H = a.H, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   pdl_wait();
-  // ---- gate: one thread, slices in order
-  if (tid == 0) {
+  // ---- gate: the slices' partials summed in slice order (warp w: a contiguous eighth of the
+  // slices, then the eight warp sums in warp order), then one warp computes the gates
+  {
     const int nslices = H / kSliceCols;
-    float mix[kPart];
-    for (int j = 0; j < kPart; ++j) mix[j] = 0.f;
-    for (int s = 0; s < nslices; ++s)
-      for (int j = 0; j < kPart; ++j) mix[j] += a.part[((size_t)t * nslices + s) * kPart + j];
-    const float rstd = 1.0f / sqrtf(mix[kMix] / (float)(kHC * H) + kRmsEps);
-    float v[kMix];
-    for (int j = 0; j < kMix; ++j) v[j] = mix[j] * rstd;
-    const float s0 = a.hc_scale[0], s1 = a.hc_scale[1], s2 = a.hc_scale[2];
-    for (int i = 0; i < kHC; ++i) {
-      a.pre_out[t * kHC + i] = 1.0f / (1.0f + expf(-(v[i] * s0 + a.hc_base[i]))) + kHcEps;
-      a.post_out[t * kHC + i] = 2.0f / (1.0f + expf(-(v[kHC + i] * s1 + a.hc_base[kHC + i])));
+    const int s0 = warp * nslices / 8, s1 = (warp + 1) * nslices / 8;
+    if (lane < kPart) {
+      float acc = 0.f;
+      for (int s = s0; s < s1; ++s) acc += a.part[((size_t)t * nslices + s) * kPart + lane];
+      gsum[warp][lane] = acc;
     }
-    float cv[16];
-    for (int e = 0; e < 16; ++e) cv[e] = v[8 + e] * s2 + a.hc_base[8 + e];
-    for (int r = 0; r < 4; ++r) {
-      float m = fmaxf(fmaxf(cv[4 * r], cv[4 * r + 1]), fmaxf(cv[4 * r + 2], cv[4 * r + 3]));
-      float sum = 0.f;
-      for (int c = 0; c < 4; ++c) {
-        cv[4 * r + c] = expf(cv[4 * r + c] - m);
-        sum += cv[4 * r + c];
-      }
-      for (int c = 0; c < 4; ++c) cv[4 * r + c] = cv[4 * r + c] / sum + kHcEps;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float mix = 0.f, sq = 0.f;
+    for (int w = 0; w < 8; ++w) {
+      mix += gsum[w][min(lane, kMix - 1)];
+      sq += gsum[w][kMix];
     }
-    for (int it = 0; it < 20; ++it) {
-      if (it > 0)
-        for (int r = 0; r < 4; ++r) {
-          const float sum = (cv[4 * r] + cv[4 * r + 1]) + (cv[4 * r + 2] + cv[4 * r + 3]) + kHcEps;
-          for (int c = 0; c < 4; ++c) cv[4 * r + c] /= sum;
-        }
-      for (int c = 0; c < 4; ++c) {
-        const float sum = (cv[c] + cv[4 + c]) + (cv[8 + c] + cv[12 + c]) + kHcEps;
-        for (int r = 0; r < 4; ++r) cv[4 * r + c] /= sum;
-      }
+    const float v = mix * (1.0f / sqrtf(sq / (float)(kHC * H) + kRmsEps));
+    const int j = min(lane, kMix - 1);
+    if (lane < kHC) {
+      a.pre_out[t * kHC + lane] = 1.0f / (1.0f + expf(-(v * a.hc_scale[0] + a.hc_base[j]))) + kHcEps;
+    } else if (lane < 2 * kHC) {
+      a.post_out[t * kHC + lane - kHC] = 2.0f / (1.0f + expf(-(v * a.hc_scale[1] + a.hc_base[j])));
     }
-    for (int e = 0; e < 16; ++e) a.comb_out[t * 16 + e] = cv[e];
+    // comb: lanes 8 .. 23 hold entry (r, c) = lane - 8 = 4 r + c; the 16-lane group 8..23 is
+    // mapped onto lanes 0..15 by a shuffle so row / column partners are xor 1, 2 / 4, 8 apart
+    float cv = v * a.hc_scale[2] + a.hc_base[j];
+    cv = __shfl_sync(0xffffffffu, cv, (lane & 15) + 8);
+    auto rsum = [&](float x) {
+      const float p = x + __shfl_xor_sync(0xffffffffu, x, 1);
+      return p + __shfl_xor_sync(0xffffffffu, p, 2);
+    };
+    auto csum = [&](float x) {
+      const float p = x + __shfl_xor_sync(0xffffffffu, x, 4);
+      return p + __shfl_xor_sync(0xffffffffu, p, 8);
+    };
+    float m = fmaxf(cv, __shfl_xor_sync(0xffffffffu, cv, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    cv = expf(cv - m);
+    cv = cv / rsum(cv) + kHcEps;
+    cv = cv / (csum(cv) + kHcEps);
+    for (int it = 1; it < 20; ++it) {
+      cv = cv / (rsum(cv) + kHcEps);
+      cv = cv / (csum(cv) + kHcEps);
+    }
+    if (lane < 16) a.comb_out[t * 16 + lane] = cv;
   }
   // ---- norm: 8 consecutive columns a thread
   float ss = 0.f;

@@ -5,7 +5,8 @@ bytes, key tables, router logits, routing ids, MXFP8 codes) must match bit for b
 floating-point outputs within the reference's bounds (``deepseek_v41/spec.py:287-318`` of
 the reference: k1.q.cosine 0.99999, k1.q.rel 5e-3, k2.attn_out.cosine 0.9998, k2.wo_a.rel
 5e-3, k2.wo_b.rel 1e-3, ffn.moe.cosine 0.9999, ffn.moe.rel 0.015, ffn.mix.rel 1e-4). The
-whole layer is then checked end to end: max |out - oracle| <= 2e-2 x RMS(oracle).
+whole layer is then checked end to end: every element within 2e-2 x RMS(oracle) plus one
+bf16 rounding step of the oracle's element (``e2e_excess``), and rel-norm error below 1e-2.
 """
 
 import pytest
@@ -30,6 +31,21 @@ def rel(a, b):
 
 def cpu(d):
     return {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in d.items()}
+
+
+def bf16_ulp(x):
+    """The bf16 rounding step at each element's magnitude."""
+    _, e = torch.frexp(x.abs().clamp_min(2.0**-126))
+    return torch.ldexp(torch.ones_like(x), e - 8)
+
+
+def e2e_excess(got, ref):
+    """(max over elements of |got - ref| beyond one bf16 step of ref, RMS of ref): the
+    end-to-end criterion. Outputs are bf16, so two computations that agree to any precision
+    short of bit-exactness still differ by one rounding step wherever an element lands near a
+    rounding boundary; an outlier element's step alone can exceed 2e-2 x RMS."""
+    excess = ((got.double() - ref.double()).abs() - bf16_ulp(ref.double())).clamp_min(0).max().item()
+    return excess, ref.double().pow(2).mean().sqrt().item()
 
 
 SMALL2 = dict(hidden=2048, heads=16, nope=512, rope=64, q_lora=512, o_groups=2, o_rank=1024,
@@ -148,9 +164,9 @@ def test_layer_end_to_end(shape_kw, M, ctx):
     rn2, normed2, *_ = OL.seam(rn, attn, post, comb, pre, W["hc_ffn_fn"], W["hc_ffn_scale"],
                                W["hc_ffn_base"], W["ffn_norm"])
     out, ids, _, _ = OL.moe_partial(normed2, W, s.route, s.topk)
-    got = b["out"].float().cpu()
-    rms = out.pow(2).mean().sqrt().item()
-    assert (got - out).abs().max().item() <= 2e-2 * rms, ((got - out).abs().max().item(), rms)
-    assert (b["res2"].float().cpu() - rn2).abs().max().item() <= 2e-2 * rn2.pow(2).mean().sqrt().item()
+    for got, ref in ((b["out"].float().cpu(), out), (b["res2"].float().cpu(), rn2)):
+        excess, rms = e2e_excess(got, ref)
+        assert excess <= 2e-2 * rms, (excess, rms)
+        assert rel(got, ref) < 1e-2
     same = (b["ids"].cpu().sort(1).values == ids.sort(1).values).all(1).float().mean().item()
     assert same >= 0.9
