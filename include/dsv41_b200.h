@@ -125,6 +125,54 @@ typedef struct {
 } Dsv41K2Args;
 #define DSV41_K2_STAGES 7
 
+/* ---------------------------------------------------------------- K2i and the index selection
+ * The FULL walk plan from device bounds: pieces of <= 6 rows of one owner (page-table row),
+ * [ctas, 4] int32 (lead, span, ch0, ch1). Replaces walk_plan.fill_walk_plan_device
+ * (gfx950/indexer/walk_plan.py:32-87; host twin index_plan.py:42-82). */
+typedef struct {
+  int64_t rows, ctas, topk, bounds, owners, plan;
+} Dsv41WalkPlanArgs;
+int dsv41_walk_plan(const Dsv41WalkPlanArgs* a, void* stream);
+
+/* K2i: index logits [rows, lstride] f32 of the FP4 query (q [rows, heads, 64] E2M1 pairs,
+ * qscale [rows, 1, 4, 16, 4], w [rows, heads] bf16) against the FP4 index plane (payload
+ * [pages, 1, 4, 64, 16], kscale [pages, 1, 4, 64]) through a page table of entry_rows keys an
+ * entry (64: plane pages; 8: a REINDEX table's blocks). FULL (reindex 0) follows the walk
+ * plan (grid = ctas); REINDEX scores reindex_chunks 128-column chunks a row (grid = ctas).
+ * heads % 16 == 0, heads <= 64. Replaces build_k2i's launch (gfx950/indexer/k2i.py:39-85,
+ * called from indexer/runner.py:228-251). */
+typedef struct {
+  int64_t rows, heads, q, qscale, w, payload, kscale;
+  int64_t plan, ctas, itab, itab_stride, itab_len, entry_rows, owners, bounds;
+  int64_t logits, lstride, reindex, reindex_chunks;
+} Dsv41K2iArgs;
+int dsv41_k2i(const Dsv41K2iArgs* a, void* stream);
+
+/* Top-k of each row's first n[t] values (group > 1: of the maxima of groups of `group`
+ * values -- candidate blocks), ties to the lower position, written in ascending position
+ * order, -1 padded; optional paged twin page_out = table[owners[t]][pos / page] * page +
+ * pos % page. Replaces SGLang's topk_transform_paged(_hip) and select_candidate_blocks_hip
+ * (called at indexer/runner.py:158-190, deepseek_v41/spec.py:697-706). */
+typedef struct {
+  int64_t rows, k, vals, vstride, n, group, out, page_out, table, table_stride, page, owners;
+} Dsv41TopkArgs;
+int dsv41_topk(const Dsv41TopkArgs* a, void* stream);
+
+/* A REINDEX layer's candidate table (indexer/candidate_table.py:19-99). */
+typedef struct {
+  int64_t rows, topk_blocks, units, block_rows, ids, ids_stride, page_table, page_stride;
+  int64_t owners, visible, ids_out, table, context;
+} Dsv41ReindexArgs;
+int dsv41_reindex_table(const Dsv41ReindexArgs* a, void* stream);
+
+/* A REINDEX layer's compact selection mapped back to positions and pool slots
+ * (indexer/candidate_table.py:103-163). */
+typedef struct {
+  int64_t rows, topk, block_rows, page, compact, ids, ids_stride, page_table, table_stride;
+  int64_t owners, raw_out, page_out, out_stride;
+} Dsv41MapCompactArgs;
+int dsv41_map_compact(const Dsv41MapCompactArgs* a, void* stream);
+
 /* Kernels this library has launched in this process (all entry points): for profiling. */
 int64_t dsv41_launch_count(void);
 int64_t dsv41_k2_scratch_bytes(const Dsv41K2Args* a);

@@ -38,15 +38,19 @@ def key_dims(payload, kscale, page, slot):
     return k, ke.to(torch.int64)
 
 
-def index_logits(q, qscale, w, payload, kscale, table, t, cols):
+def index_logits(q, qscale, w, payload, kscale, table, t, cols, entry_rows=PAGE):
     """fp32 logits of row t at ``cols`` (``test_deepseek_v41_k2i.py:148-171``), bit-exact
     contract: per (head h, chunk c) the exact integer dot I of the 2 * E2M1 values; x_h =
     sum over c = 0..3 (sequential, fp64) of I 2^(qe + ke - 256); relu; the head terms
-    w_h x_h (exact in fp64) summed h = 0..heads-1 sequentially in fp64; rounded once to fp32."""
+    w_h x_h (exact in fp64) summed in the kernel's tree: for g = 0..7, s_g = the terms of
+    heads g, g + 8, g + 16, ... added in that order; then ((s0 + s4) + (s2 + s6)) +
+    ((s1 + s5) + (s3 + s7)); rounded once to fp32."""
     cols = torch.as_tensor(cols, dtype=torch.long)
     heads = q.shape[1]
-    page = table[t][cols // PAGE].long()
-    slot = cols % PAGE
+    # a table entry covers ``entry_rows`` keys: 64 (plane pages) or 8 (a REINDEX table's blocks)
+    vrow = table[t][cols // entry_rows].long() * entry_rows + cols % entry_rows
+    page = vrow // PAGE
+    slot = vrow % PAGE
     k, ke = key_dims(payload, kscale, page, slot)  # [n, 4, 32], [n, 4]
     qv = _e2m1_x2(q[t].view(heads, 4, 16))  # [heads, 4, 32]
     h = torch.arange(heads)
@@ -57,23 +61,26 @@ def index_logits(q, qscale, w, payload, kscale, table, t, cols):
         x = x + torch.ldexp(dots[:, :, c].double(), (qe[:, c, None] + ke[None, :, c] - 256))
     x = x.clamp_min(0.0)
     wd = w[t].float().double()
-    acc = torch.zeros(cols.numel(), dtype=torch.float64)
-    for hh in range(heads):
-        acc = acc + wd[hh] * x[hh]
-    return acc.float()
+    s = torch.zeros(8, cols.numel(), dtype=torch.float64)
+    for j in range(heads // 8):
+        for g in range(8):
+            s[g] = s[g] + wd[g + 8 * j] * x[g + 8 * j]
+    s = s[:4] + s[4:]
+    s = s[:2] + s[2:]
+    return (s[0] + s[1]).float()
 
 
 def topk_rows(logits, bound, k):
-    """Top-k positions of one row's logits[:bound], descending, ties to the lower position;
-    all positions in order when bound <= k; -1 padded to k (the north star's rule for
-    SGLang's ``topk_transform_paged``). int32 [k]."""
+    """The k largest of one row's logits[:bound], ties to the lower position (the north
+    star's rule for SGLang's ``topk_transform_paged``), as positions in ascending order; every
+    position when bound <= k; -1 padded to k. int32 [k]."""
     out = torch.full((k,), -1, dtype=torch.int32)
     if bound <= k:
         out[:bound] = torch.arange(bound, dtype=torch.int32)
         return out
     v = logits[:bound].double().numpy()
     order = np.lexsort((np.arange(bound), -v))[:k]
-    out[:] = torch.from_numpy(order.astype(np.int32))
+    out[:] = torch.from_numpy(np.sort(order).astype(np.int32))
     return out
 
 
@@ -88,7 +95,7 @@ def page_indices(raw, table_row, page_size):
 def candidate_blocks(logits, bound, nblocks=TOPK_BLOCKS, rows=BLOCK_ROWS):
     """A producer row's candidate blocks: block b covers positions [8 b, 8 b + 8) of the
     row's bound; its score is the largest logit in it; the top ``nblocks`` blocks by
-    score, ties to the lower block, -1 padded (restating SGLang's
+    score, ties to the lower block, in ascending block order, -1 padded (restating SGLang's
     ``select_candidate_blocks``, absent here, from its use at ``indexer/runner.py:158-190``)."""
     nb = -(-bound // rows)
     out = torch.full((nblocks,), -1, dtype=torch.int32)
@@ -97,7 +104,7 @@ def candidate_blocks(logits, bound, nblocks=TOPK_BLOCKS, rows=BLOCK_ROWS):
     v = torch.full((nb * rows,), -float("inf"), dtype=torch.float64)
     v[:bound] = logits[:bound].double()
     score = v.view(nb, rows).amax(1).numpy()
-    order = np.lexsort((np.arange(nb), -score))[:nblocks]
+    order = np.sort(np.lexsort((np.arange(nb), -score))[:nblocks])
     out[: order.size] = torch.from_numpy(order.astype(np.int32))
     return out
 

@@ -40,9 +40,37 @@ K2Args = struct("Dsv41K2Args", [
 K2_STAGES = ("attention", "wo_a+wo_b", "reduce+ffn seam", "router", "shared expert", "routed experts",
              "combine+reduce")
 
+WalkPlanArgs = struct("Dsv41WalkPlanArgs", ["rows", "ctas", "topk", "bounds", "owners", "plan"])
+
+K2iArgs = struct("Dsv41K2iArgs", [
+    "rows", "heads", "q", "qscale", "w", "payload", "kscale",
+    "plan", "ctas", "itab", "itab_stride", "itab_len", "entry_rows", "owners", "bounds",
+    "logits", "lstride", "reindex", "reindex_chunks",
+])
+
+TopkArgs = struct("Dsv41TopkArgs", [
+    "rows", "k", "vals", "vstride", "n", "group", "out", "page_out", "table", "table_stride", "page",
+    "owners",
+])
+
+ReindexArgs = struct("Dsv41ReindexArgs", [
+    "rows", "topk_blocks", "units", "block_rows", "ids", "ids_stride", "page_table", "page_stride",
+    "owners", "visible", "ids_out", "table", "context",
+])
+
+MapCompactArgs = struct("Dsv41MapCompactArgs", [
+    "rows", "topk", "block_rows", "page", "compact", "ids", "ids_stride", "page_table", "table_stride",
+    "owners", "raw_out", "page_out", "out_stride",
+])
+
 STRUCTS = {
     "Dsv41GemvArgs": GemvArgs,
     "Dsv41RelayoutArgs": RelayoutArgs,
     "Dsv41K1Args": K1Args,
     "Dsv41K2Args": K2Args,
+    "Dsv41WalkPlanArgs": WalkPlanArgs,
+    "Dsv41K2iArgs": K2iArgs,
+    "Dsv41TopkArgs": TopkArgs,
+    "Dsv41ReindexArgs": ReindexArgs,
+    "Dsv41MapCompactArgs": MapCompactArgs,
 }

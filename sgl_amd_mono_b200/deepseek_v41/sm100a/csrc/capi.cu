@@ -17,6 +17,7 @@
 #include "epilogue.cuh"
 #include "front.cuh"
 #include "gemv.cuh"
+#include "k2i.cuh"
 #include "moe.cuh"
 #include "seam.cuh"
 
@@ -457,6 +458,71 @@ int dsv41_gemv_fp8(const Dsv41GemvArgs* a, void* stream) {
     const int total = (int)(a->M * a->N);
     sum_slices_kernel<<<grid_for(total, 256), 256, 0, st>>>(g.out, ptr<float>(a->y), g.kslices, total);
   }
+  return launch_status();
+}
+
+int dsv41_walk_plan(const Dsv41WalkPlanArgs* a, void* stream) {
+  if (!a || a->rows < 1 || a->rows > 48 || a->ctas < 1 || a->ctas > 4096 || !a->bounds || !a->owners ||
+      !a->plan)
+    return DSV41_EINVAL;
+  WalkPlanArgs w = {(int)a->rows, (int)a->ctas, (int)a->topk, ptr<const int32_t>(a->bounds),
+                    ptr<const int32_t>(a->owners), ptr<int32_t>(a->plan)};
+  DSV41_TRY(launch(walk_plan_kernel, dim3(1), dim3(32), 0, reinterpret_cast<cudaStream_t>(stream), w));
+  return launch_status();
+}
+
+int dsv41_k2i(const Dsv41K2iArgs* a, void* stream) {
+  if (!a || a->rows < 1 || a->rows > 48 || a->heads < 16 || a->heads > 64 || a->heads % 16 || !a->q ||
+      !a->qscale || !a->w || !a->payload || !a->kscale || !a->itab || !a->owners || !a->bounds ||
+      !a->logits || a->ctas < 1 || (!a->reindex && !a->plan) ||
+      !(a->entry_rows == 64 || a->entry_rows == 8) || a->lstride < 1 || a->payload % 16)
+    return DSV41_EINVAL;
+  K2iArgs k = {};
+  k.rows = (int)a->rows; k.heads = (int)a->heads;
+  k.q = ptr<const uint8_t>(a->q); k.qscale = ptr<const uint8_t>(a->qscale);
+  k.w = ptr<const __nv_bfloat16>(a->w); k.payload = ptr<const uint8_t>(a->payload);
+  k.kscale = ptr<const uint8_t>(a->kscale); k.plan = ptr<const int32_t>(a->plan);
+  k.itab = ptr<const int32_t>(a->itab); k.itab_stride = (int)a->itab_stride; k.itab_len = (int)a->itab_len;
+  k.entry_rows = (int)a->entry_rows; k.owners = ptr<const int32_t>(a->owners);
+  k.bounds = ptr<const int32_t>(a->bounds); k.logits = ptr<float>(a->logits); k.lstride = (int)a->lstride;
+  k.reindex = (int)a->reindex; k.reindex_chunks = (int)a->reindex_chunks;
+  DSV41_TRY(launch(k2i_score_kernel, dim3((int)a->ctas), dim3(256), k2i_smem_bytes(k.heads),
+                   reinterpret_cast<cudaStream_t>(stream), k));
+  return launch_status();
+}
+
+int dsv41_topk(const Dsv41TopkArgs* a, void* stream) {
+  if (!a || a->rows < 1 || a->k < 1 || a->k > 65536 || !a->vals || !a->n || !a->out || a->group < 1 ||
+      (a->page_out && (!a->table || !a->owners || a->page < 1)))
+    return DSV41_EINVAL;
+  TopkArgs t = {(int)a->rows, (int)a->k, ptr<const float>(a->vals), (int)a->vstride, ptr<const int32_t>(a->n),
+                (int)a->group, ptr<int32_t>(a->out), ptr<int32_t>(a->page_out), ptr<const int32_t>(a->table),
+                (int)a->table_stride, (int)a->page, ptr<const int32_t>(a->owners)};
+  DSV41_TRY(launch(topk_kernel, dim3((int)a->rows), dim3(1024), 0, reinterpret_cast<cudaStream_t>(stream), t));
+  return launch_status();
+}
+
+int dsv41_reindex_table(const Dsv41ReindexArgs* a, void* stream) {
+  if (!a || a->rows < 1 || a->topk_blocks < 1 || a->units < 1 || a->block_rows < 1 || !a->ids ||
+      !a->page_table || !a->owners || !a->visible || !a->ids_out || !a->table || !a->context)
+    return DSV41_EINVAL;
+  ReindexArgs r = {(int)a->rows, (int)a->topk_blocks, (int)a->units, (int)a->block_rows,
+                   ptr<const int32_t>(a->ids), (int)a->ids_stride, ptr<const int32_t>(a->page_table),
+                   (int)a->page_stride, ptr<const int32_t>(a->owners), ptr<const int32_t>(a->visible),
+                   ptr<int32_t>(a->ids_out), ptr<int32_t>(a->table), ptr<int32_t>(a->context)};
+  DSV41_TRY(launch(reindex_kernel, dim3((int)a->rows), dim3(32), 0, reinterpret_cast<cudaStream_t>(stream), r));
+  return launch_status();
+}
+
+int dsv41_map_compact(const Dsv41MapCompactArgs* a, void* stream) {
+  if (!a || a->rows < 1 || a->topk < 1 || !a->compact || !a->ids || !a->page_table || !a->owners ||
+      !a->raw_out || !a->page_out || a->block_rows < 1 || a->page < 1)
+    return DSV41_EINVAL;
+  MapCompactArgs m = {(int)a->rows, (int)a->topk, (int)a->block_rows, (int)a->page,
+                      ptr<const int32_t>(a->compact), ptr<const int32_t>(a->ids), (int)a->ids_stride,
+                      ptr<const int32_t>(a->page_table), (int)a->table_stride, ptr<const int32_t>(a->owners),
+                      ptr<int32_t>(a->raw_out), ptr<int32_t>(a->page_out), (int)a->out_stride};
+  DSV41_TRY(launch(map_compact_kernel, dim3((int)a->rows), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), m));
   return launch_status();
 }
 

@@ -1,0 +1,432 @@
+// K2i, the index sources' FP4 scorer, and the index selection around it (the reference's
+// gfx950/indexer/{index_plan,walk_plan,score_fp4,candidate_table}.py and SGLang's top-k
+// kernels, which are absent here and restated).
+//
+// Logits (bit-exact contract, oracle/indexer.py:index_logits): for row t and column col,
+//   x_h = sum_{c=0..3} I_{h,c} 2^(qe_{h,c} + ke_{col,c} - 256)   (fp64, c in order),
+//   I_{h,c} = the integer dot of the 2 x E2M1 values of q_h and k_col over chunk c,
+//   logit = fp32( tree-sum over heads of w_h relu(x_h) ) with the tree: s_g = terms of heads
+//   g, g+8, g+16, ... in order, then ((s0 + s4) + (s2 + s6)) + ((s1 + s5) + (s3 + s7)).
+// I_{h,c} comes from mma.sync m16n8k16 f16 on cvt.e2m1x2 operands: every product is a
+// multiple of 1/4 and a 32-dim sum stays below 2^11, so the fp32 accumulation is exact. The
+// f16 operands carry the real E2M1 values (I / 4), so the scale exponent is qe + ke - 254.
+#pragma once
+
+#include "common.cuh"
+
+namespace dsv41 {
+
+constexpr int kPlaneRows = 64;   // keys an index-plane page
+constexpr int kIdxChunk = 128;   // columns a score chunk
+constexpr int kWalkRows = 6;     // rows a walk piece (one page table)
+constexpr int kIdxMaxSpan = 6;
+
+// ------------------------------------------------------------------ walk plan
+struct WalkPlanArgs {
+  int rows, ctas, topk;
+  const int32_t* bounds;  // [rows]
+  const int32_t* owners;  // [rows]: each row's request (page-table row)
+  int32_t* plan;          // [ctas, 4]: (lead, span, ch0, ch1), zeros past the last task
+};
+
+// index_plan.py:42-82 restated: pieces of <= 6 adjacent rows of one owner; a piece needs
+// ceil(max bound / 128) chunks when a row's bound exceeds topk; each piece gets
+// ceil(need / width) tasks sharing its chunks evenly at the smallest width whose task count
+// fits the CTAs. One thread (rows <= 48).
+__global__ void walk_plan_kernel(const WalkPlanArgs a) {
+  pdl_wait();
+  if (threadIdx.x != 0) return;
+  int lead[64], span[64], need[64];
+  int np = 0, run_first = 0;
+  for (int t = 0; t < a.rows; ++t) {
+    const bool start = t == 0 || a.owners[t] != a.owners[t - 1];
+    if (start) run_first = t;
+    if (start || (t - run_first) % kWalkRows == 0) lead[np++] = t;
+  }
+  int pieces = 0;
+  for (int i = 0; i < np; ++i) {
+    const int l = lead[i], e = i + 1 < np ? lead[i + 1] : a.rows;
+    int nd = 0;
+    for (int t = l; t < e; ++t) {
+      const int b = a.bounds[t];
+      if (b > a.topk) nd = max(nd, (b + kIdxChunk - 1) / kIdxChunk);
+    }
+    if (nd > 0) {
+      lead[pieces] = l;
+      span[pieces] = e - l;
+      need[pieces] = nd;
+      ++pieces;
+    }
+  }
+  for (int i = 0; i < a.ctas * 4; ++i) a.plan[i] = 0;
+  if (pieces == 0 || pieces >= a.ctas) return;
+  long total = 0;
+  for (int i = 0; i < pieces; ++i) total += need[i];
+  int width = (int)max((total + a.ctas - 1) / a.ctas, 1L);
+  for (;; ++width) {
+    long tasks = 0;
+    for (int i = 0; i < pieces; ++i) tasks += (need[i] + width - 1) / width;
+    if (tasks <= a.ctas) break;
+  }
+  int r = 0;
+  for (int i = 0; i < pieces; ++i) {
+    const int k = (need[i] + width - 1) / width;
+    for (int j = 0; j < k; ++j, ++r) {
+      a.plan[4 * r + 0] = lead[i];
+      a.plan[4 * r + 1] = span[i];
+      a.plan[4 * r + 2] = j * need[i] / k;
+      a.plan[4 * r + 3] = (j + 1) * need[i] / k;
+    }
+  }
+  pdl_launch();
+}
+
+// ------------------------------------------------------------------ scorer
+struct K2iArgs {
+  int rows, heads;
+  const uint8_t* q;        // [rows, heads, 64] E2M1 pairs (128 dims a head)
+  const uint8_t* qscale;   // [rows, 1, 4, 16, 4]: head h, chunk c at [c][h % 16][h / 16]
+  const __nv_bfloat16* w;  // [rows, heads]
+  const uint8_t* payload;  // [pages, 1, 4, 64, 16]
+  const uint8_t* kscale;   // [pages, 1, 4, 64]: key s at (s % 16) * 4 + s / 16
+  const int32_t* plan;     // FULL: [ctas, 4] walk plan
+  const int32_t* itab;     // page table: row owners[t], entries of ``entry_rows`` keys
+  int itab_stride, itab_len, entry_rows;  // 64 (plane pages) or 8 (a REINDEX table's blocks)
+  const int32_t* owners;   // [rows]
+  const int32_t* bounds;   // [rows]: columns a row sees
+  float* logits;           // [rows, lstride]
+  int lstride;
+  int reindex;             // 1: CTA b scores chunk range b % per of row b / per (no plan)
+  int reindex_chunks;      // a REINDEX row's chunks
+};
+
+__host__ __device__ inline int k2i_smem_bytes(int heads) {
+  return kIdxMaxSpan * heads * 68 + kIdxMaxSpan * 4 * heads + 4 * kIdxChunk * 16 + 4 * kIdxChunk;
+}
+
+__global__ void __launch_bounds__(256) k2i_score_kernel(const K2iArgs a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int H = a.heads, mtiles = H / 16;
+  uint8_t* qraw = smem;                                  // [span][H][68]
+  uint8_t* qe = qraw + kIdxMaxSpan * H * 68;             // [span][4][H]
+  uint8_t* keys = qe + kIdxMaxSpan * 4 * H;              // [4][128][16]
+  uint8_t* ke = keys + 4 * kIdxChunk * 16;               // [4][128]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  pdl_wait();
+  int lead, span, ch0, ch1;
+  if (a.reindex) {
+    const int per = max(1, (int)gridDim.x / a.rows);
+    const int row = blockIdx.x / per, i = blockIdx.x % per;
+    if (row >= a.rows) return;
+    lead = row;
+    span = 1;
+    ch0 = i * a.reindex_chunks / per;
+    ch1 = (i + 1) * a.reindex_chunks / per;
+  } else {
+    lead = a.plan[4 * blockIdx.x];
+    span = a.plan[4 * blockIdx.x + 1];
+    ch0 = a.plan[4 * blockIdx.x + 2];
+    ch1 = a.plan[4 * blockIdx.x + 3];
+  }
+  if (span <= 0 || ch0 >= ch1) return;
+  const int owner = a.owners[lead];
+  int piece_bound = 0;
+  for (int r = 0; r < span; ++r) piece_bound = max(piece_bound, a.bounds[lead + r]);
+  // the piece's queries: raw E2M1 bytes (rows padded to 68 B: conflict-free lane reads)
+  for (int i = tid; i < span * H * 16; i += blockDim.x) {
+    const int r = i / (H * 16), rem = i % (H * 16), h = rem / 16, wd = rem % 16;
+    *reinterpret_cast<uint32_t*>(qraw + (r * H + h) * 68 + 4 * wd) =
+        *reinterpret_cast<const uint32_t*>(a.q + ((size_t)(lead + r) * H + h) * 64 + 4 * wd);
+  }
+  for (int i = tid; i < span * 4 * H; i += blockDim.x) {
+    const int r = i / (4 * H), c = (i / H) % 4, h = i % H;
+    qe[i] = a.qscale[(size_t)(lead + r) * 256 + c * 64 + (h % 16) * 4 + h / 16];
+  }
+  for (int ch = ch0; ch < ch1 && ch * kIdxChunk < piece_bound; ++ch) {
+    __syncthreads();  // the previous chunk's readers are done
+    // the chunk's keys: 128 columns x 4 chunks x 16 B, zero past the piece's bound
+    for (int i = tid; i < 4 * kIdxChunk; i += blockDim.x) {
+      const int c = i / kIdxChunk, cl = i % kIdxChunk, col = ch * kIdxChunk + cl;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      uint8_t s = 127;
+      if (col < piece_bound && col / a.entry_rows < a.itab_len) {
+        const int entry = a.itab[(size_t)owner * a.itab_stride + col / a.entry_rows];
+        const long vrow = (long)entry * a.entry_rows + col % a.entry_rows;
+        const long page = vrow / kPlaneRows;
+        const int slot = (int)(vrow % kPlaneRows);
+        v = ldg16(a.payload + ((page * 4 + c) * kPlaneRows + slot) * 16);
+        s = a.kscale[(page * 4 + c) * kPlaneRows + (slot % 16) * 4 + slot / 16];
+      }
+      *reinterpret_cast<uint4*>(keys + (c * kIdxChunk + cl) * 16) = v;
+      ke[c * kIdxChunk + cl] = s;
+    }
+    __syncthreads();
+    for (int r = 0; r < span; ++r) {
+      const int row = lead + r, bound = a.bounds[row];
+#pragma unroll
+      for (int nn = 0; nn < 2; ++nn) {
+        const int nt = 2 * warp + nn;  // this warp's n-tile: columns 8 nt .. 8 nt + 7
+        const int col_g = 8 * nt + g;  // the B-fragment column of this lane
+        double s[2] = {0.0, 0.0};
+        for (int mt = 0; mt < mtiles; ++mt) {
+          double x[4] = {0.0, 0.0, 0.0, 0.0};
+          const uint8_t* qa = qraw + (r * H + 16 * mt + g) * 68;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int ks = 0; ks < 2; ++ks) {
+              const int qb = 16 * c + 8 * ks + t;
+              const uint32_t a0 = e2m1x2_f16(qa[qb]), a1 = e2m1x2_f16(qa[8 * 68 + qb]);
+              const uint32_t a2 = e2m1x2_f16(qa[qb + 4]), a3 = e2m1x2_f16(qa[8 * 68 + qb + 4]);
+              const uint8_t* kb = keys + (c * kIdxChunk + col_g) * 16 + 8 * ks + t;
+              const uint32_t b0 = e2m1x2_f16(kb[0]), b1 = e2m1x2_f16(kb[4]);
+              mma_f16(acc, a0, a1, a2, a3, b0, b1);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int h = 16 * mt + g + 8 * (q >> 1);
+              const int cl = 8 * nt + 2 * t + (q & 1);
+              const int e = (int)qe[(r * 4 + c) * H + h] + (int)ke[c * kIdxChunk + cl] - 254;
+              const double f = __longlong_as_double((long long)(e + 1023) << 52);
+              x[q] = __dadd_rn(x[q], __dmul_rn((double)acc[q], f));
+            }
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int h = 16 * mt + g + 8 * (q >> 1);
+            const double wv = (double)bf2f(a.w[(size_t)row * H + h]);
+            // heads g + 16 mt (q = 0, 1), then g + 8 + 16 mt (q = 2, 3): the tree's order
+            s[q & 1] = __dadd_rn(s[q & 1], __dmul_rn(wv, fmax(x[q], 0.0)));
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          double v = s[j];
+          v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 16));
+          v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 8));
+          v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
+          const int col = ch * kIdxChunk + 8 * nt + 2 * t + j;
+          if (g == 0 && col < bound && col < a.lstride) a.logits[(size_t)row * a.lstride + col] = (float)v;
+        }
+      }
+    }
+  }
+  pdl_launch();
+}
+
+// ------------------------------------------------------------------ top-k
+// The k largest of each row's first n values, ties to the lower position, written as
+// positions in ascending order (-1 padded); every position when n <= k. Radix select on an
+// order-preserving 32-bit key (NaN lowest, -0 equal to +0), then an ordered compaction.
+__device__ __forceinline__ uint32_t order_key(float v) {
+  if (isnan(v)) return 0u;
+  const uint32_t b = v == 0.f ? 0u : __float_as_uint(v);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+struct TopkArgs {
+  int rows, k;
+  const float* vals;       // [rows, vstride]
+  int vstride;
+  const int32_t* n;        // [rows] values a row considers
+  int group;               // 1: values as is; G > 1: a candidate's score is the max of G values
+  int32_t* out;            // [rows, k] positions (or groups)
+  // optional paged outputs: page_out[t][j] = table[owner][pos / page] * page + pos % page
+  int32_t* page_out;
+  const int32_t* table;
+  int table_stride, page;
+  const int32_t* owners;
+};
+
+__global__ void __launch_bounds__(1024) topk_kernel(const TopkArgs a) {
+  __shared__ int hist[256];
+  __shared__ uint32_t s_prefix;
+  __shared__ int s_need, s_gt;
+  __shared__ int warp_cnt[32], warp_tie[32];
+  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_wait();
+  const int nval = a.n[row];
+  const int n = a.group > 1 ? (nval + a.group - 1) / a.group : nval;
+  int32_t* out = a.out + (size_t)row * a.k;
+  auto key_at = [&](int i) -> uint32_t {
+    if (a.group <= 1) return order_key(a.vals[(size_t)row * a.vstride + i]);
+    uint32_t m = 0;
+    for (int j = 0; j < a.group; ++j) {
+      const int p = i * a.group + j;
+      if (p < nval) m = max(m, order_key(a.vals[(size_t)row * a.vstride + p]));
+    }
+    return m;
+  };
+  auto emit = [&](int j, int pos) {
+    out[j] = pos;
+    if (a.page_out) {
+      int32_t slot = -1;
+      if (pos >= 0)
+        slot = a.table[(size_t)a.owners[row] * a.table_stride + pos / a.page] * a.page + pos % a.page;
+      a.page_out[(size_t)row * a.k + j] = slot;
+    }
+  };
+  if (n <= a.k) {
+    for (int j = tid; j < a.k; j += blockDim.x) emit(j, j < n ? j : -1);
+    return;
+  }
+  // ---- radix select: the threshold key T, count(key > T) < k <= count(key >= T)
+  if (tid == 0) {
+    s_prefix = 0;
+    s_need = a.k;
+  }
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    const uint32_t prefix = s_prefix;
+    const uint32_t pmask = pass == 0 ? 0u : (0xFFFFFFFFu << (shift + 8));
+    for (int i = tid; i < n; i += blockDim.x) {
+      const uint32_t kk = key_at(i);
+      if ((kk & pmask) == prefix) atomicAdd(&hist[(kk >> shift) & 0xFF], 1);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int need = s_need, d = 255;
+      for (; d > 0; --d) {
+        if (hist[d] >= need) break;
+        need -= hist[d];
+      }
+      s_need = need;
+      s_prefix = prefix | ((uint32_t)d << shift);
+    }
+    __syncthreads();
+  }
+  const uint32_t T = s_prefix;
+  const int ties_taken = s_need;  // how many keys equal to T are selected (lowest positions)
+  // ---- ordered compaction: thread i handles positions [i c, i c + c)
+  const int per = (n + blockDim.x - 1) / blockDim.x;
+  const int p0 = min(n, tid * per), p1 = min(n, p0 + per);
+  int cnt_gt = 0, cnt_eq = 0;
+  for (int p = p0; p < p1; ++p) {
+    const uint32_t kk = key_at(p);
+    cnt_gt += kk > T;
+    cnt_eq += kk == T;
+  }
+  // exclusive scans of the ties (for the tie budget) and of the selections
+  auto block_excl_scan = [&](int v, int* buf, int& total) {
+    int incl = v;
+    for (int d = 1; d < 32; d <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += o;
+    }
+    if (lane == 31) buf[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int w = lane < (int)(blockDim.x >> 5) ? buf[lane] : 0;
+      for (int d = 1; d < 32; d <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, w, d);
+        if (lane >= d) w += o;
+      }
+      buf[lane] = w;  // inclusive warp totals
+    }
+    __syncthreads();
+    total = buf[(blockDim.x >> 5) - 1];
+    const int before = (warp > 0 ? buf[warp - 1] : 0) + incl - v;
+    __syncthreads();
+    return before;
+  };
+  int tot;
+  const int eq_before = block_excl_scan(cnt_eq, warp_tie, tot);
+  const int eq_mine = max(0, min(cnt_eq, ties_taken - eq_before));
+  const int sel = cnt_gt + eq_mine;
+  const int sel_before = block_excl_scan(sel, warp_cnt, tot);
+  int j = sel_before, eq_seen = 0;
+  for (int p = p0; p < p1; ++p) {
+    const uint32_t kk = key_at(p);
+    bool take = kk > T;
+    if (kk == T) {
+      take = eq_seen < eq_mine;
+      ++eq_seen;
+    }
+    if (take) emit(j++, p);
+  }
+  for (int q = tot + tid; q < a.k; q += blockDim.x) emit(q, -1);
+  pdl_launch();
+}
+
+// ------------------------------------------------------------------ candidate tables
+struct ReindexArgs {
+  int rows, topk_blocks, units, block_rows;  // units: 8-row blocks a 64-row page
+  const int32_t* ids;       // [rows, ids_stride] candidate blocks, -1 after the kept ones
+  int ids_stride;
+  const int32_t* page_table;  // [owner][page_stride]
+  int page_stride;
+  const int32_t* owners;
+  const int32_t* visible;   // [rows] bounds
+  int32_t* ids_out;         // [rows, ids_stride]
+  int32_t* table;           // [rows, ids_stride] virtual 8-row pages
+  int32_t* context;         // [rows]
+};
+
+// candidate_table.py:19-66 restated: the newest block (holding position visible - 1) moved to
+// the last kept slot; each kept block's virtual 8-row page; the context.
+__global__ void reindex_kernel(const ReindexArgs a) {
+  pdl_wait();
+  const int t = blockIdx.x;
+  if (threadIdx.x != 0) return;
+  const int32_t* ids = a.ids + (size_t)t * a.ids_stride;
+  int32_t* io = a.ids_out + (size_t)t * a.ids_stride;
+  int32_t* tb = a.table + (size_t)t * a.ids_stride;
+  int kept = 0;
+  for (int s = 0; s < a.topk_blocks; ++s) kept += ids[s] >= 0;
+  const int seen = a.visible[t];
+  const int newest = seen >= 1 ? (seen - 1) / a.block_rows : -1;  // floor division
+  int at = -1;
+  for (int s = 0; s < a.topk_blocks; ++s)
+    if (ids[s] >= 0 && ids[s] == newest) at = s;
+  const int last = kept - 1;
+  const int moved = last >= 0 ? ids[last] : 0;
+  for (int s = 0; s < a.topk_blocks; ++s) {
+    int c = ids[s];
+    if (at >= 0 && s == at) c = moved;
+    else if (at >= 0 && s == last) c = newest;
+    io[s] = c;
+    const bool live = c >= 0;
+    const int cc = live ? c : 0;
+    tb[s] = live ? a.page_table[(size_t)a.owners[t] * a.page_stride + cc / a.units] * a.units + cc % a.units : 0;
+  }
+  const int tail = last >= 0 ? io[last] : 0;
+  const int span = min(max(seen - tail * a.block_rows, 0), a.block_rows);
+  a.context[t] = kept > 0 ? (kept - 1) * a.block_rows + span : 0;
+  pdl_launch();
+}
+
+struct MapCompactArgs {
+  int rows, topk, block_rows, page;
+  const int32_t* compact;   // [rows, topk]
+  const int32_t* ids;       // [rows, ids_stride] (reindex_kernel's ids_out)
+  int ids_stride;
+  const int32_t* page_table;
+  int table_stride;
+  const int32_t* owners;
+  int32_t* raw_out;         // [rows, out_stride]
+  int32_t* page_out;
+  int out_stride;
+};
+
+// candidate_table.py:103-134 restated: compact column c -> position ids[c / 8] * 8 + c % 8
+// -> pool slot page_table[pos / 64] * 64 + pos % 64; -1 stays -1.
+__global__ void map_compact_kernel(const MapCompactArgs a) {
+  pdl_wait();
+  const int t = blockIdx.x;
+  for (int j = threadIdx.x; j < a.topk; j += blockDim.x) {
+    const int c = a.compact[(size_t)t * a.topk + j];
+    int raw = -1, pg = -1;
+    if (c >= 0) {
+      raw = a.ids[(size_t)t * a.ids_stride + c / a.block_rows] * a.block_rows + c % a.block_rows;
+      pg = a.page_table[(size_t)a.owners[t] * a.table_stride + raw / a.page] * a.page + raw % a.page;
+    }
+    a.raw_out[(size_t)t * a.out_stride + j] = raw;
+    a.page_out[(size_t)t * a.out_stride + j] = pg;
+  }
+  pdl_launch();
+}
+
+}  // namespace dsv41
