@@ -2,8 +2,9 @@
  *
  * Every entry point takes a POD argument struct whose fields are all 64-bit (device
  * pointers as int64, sizes and flags as int64), plus a cudaStream_t passed as void*, and
- * returns 0 or a negative DSV41_E* status. Nothing throws across the boundary; nothing
- * allocates device memory: scratch is caller-owned, sized by the *_scratch_bytes queries.
+ * returns 0 or a negative DSV41_E* status. Nothing throws across the boundary; nothing but
+ * dsv41_peer_alloc (the TP exchange regions) allocates device memory: scratch is
+ * caller-owned, sized by the *_scratch_bytes queries.
  * Launches go on the given stream only, so every call is CUDA-graph capturable.
  *
  * The reference (omirosh/sgl-amd-mono) binds the same launches through its FlyDSL JIT
@@ -100,8 +101,17 @@ int dsv41_k1(const Dsv41K1Args* a, void* stream);
  * routing, the shared and routed experts and the MoE all-reduce of one layer
  * (gfx950/layer.py:773-1072, launch args layer.py:802-854; host runner.py:624-728).
  * route_softmax = 1: softmax top-k routing; 0: sqrtsoftplus + bias, renormalized x 1.5.
- * tp > 1: peer_parts / peer_moe point at device tables of tp pointers (each rank's
- * symmetric bf16 [M, hidden] buffer) and the all-reduces go through peer memory. */
+ * heads, o_groups, inter and shared_inter are this rank's (local) widths.
+ * tp > 1: peers is a device array of tp int64 -- each rank's exchange region
+ * (dsv41_peer_alloc / dsv41_peer_open) as mapped in this process -- whose data slots hold
+ * peer_cap bf16 elements (>= M * hidden); both all-reduces run in-kernel through it, with
+ * waits that give up after deadline_ns (0: 5 s) and leave the failure in the guard words
+ * (dsv41_peer_status). phase 0: the whole layer; phase 1: stop at this rank's attention
+ * partial (attn_part); phase 2: start from the reduced attention output in attn and stop at
+ * this rank's MoE partial (moe_part) -- the caller reduces in between (the NCCL variant:
+ * an all-gather, then dsv41_rank_sum). inject = s (1 attention, 2 MoE): skip this rank's
+ * push at site s (the reference's SGLANG_AMD_MONO_FAULT_INJECT test hook, guard.py:80-100),
+ * so the peers' waits run out. */
 typedef struct {
   int64_t M, hidden, nope, rope, heads, o_groups, o_rank;
   int64_t experts, topk, inter, shared_inter, route_softmax, tp, rank, keys_ld;
@@ -116,7 +126,7 @@ typedef struct {
   /* outputs (xo, x8b, x8bs, attn_part, attn, logits: optional inspection copies) */
   int64_t out, ids, wts, xo, x8b, x8bs, attn_part, attn, logits, moe_part;
   /* tensor parallelism */
-  int64_t peer_attn, peer_moe, peer_flags, epoch, deadline_ns;
+  int64_t peers, peer_cap, deadline_ns, phase, inject;
   /* optional host array of DSV41_K2_STAGES + 1 cudaEvent_t recorded at stage boundaries
    * (attention, wo_a + wo_b, all-reduce + FFN seam, router + routing, shared expert,
    * routed experts, combine + all-reduce); 0 = none */
@@ -172,6 +182,44 @@ typedef struct {
   int64_t owners, raw_out, page_out, out_stride;
 } Dsv41MapCompactArgs;
 int dsv41_map_compact(const Dsv41MapCompactArgs* a, void* stream);
+
+/* ---------------------------------------------------------------- TP exchange regions
+ * One region a rank (guard words, failure flags, per-CTA arrival flags, two parities of
+ * tp data slots of cap bf16 elements); replaces common/peer.py:114-156 (PeerBuffer) and the
+ * guard block of common/guard.py:20-40. Construction is collective in the caller: every
+ * rank allocates its region, the 64-byte IPC handles are exchanged, and every rank opens the
+ * others'. dsv41_peer_region_bytes: the size of a region for tp ranks and cap elements. */
+#define DSV41_IPC_HANDLE_BYTES 64
+#define DSV41_PEER_MAX_TP 8
+#define DSV41_GUARD_WORDS 8
+int64_t dsv41_peer_region_bytes(int64_t tp, int64_t cap);
+/* cudaMalloc + zero fill + cudaIpcGetMemHandle on the current device: *region and the
+ * handle's DSV41_IPC_HANDLE_BYTES bytes. */
+int dsv41_peer_alloc(int64_t bytes, int64_t* region, uint8_t* handle);
+/* Map another rank's region (cudaIpcOpenMemHandle, lazy peer access). */
+int dsv41_peer_open(const uint8_t* handle, int64_t* region);
+int dsv41_peer_close(int64_t region);
+int dsv41_peer_free(int64_t region);
+/* Synchronous read of a region's DSV41_GUARD_WORDS guard words (0 sequence, 1 CTAs done,
+ * 3 deadline site, 4 peer failure seen, 5 fault injected); DSV41_EDEVICE when one of the
+ * error words is set. */
+int dsv41_peer_status(int64_t region, int32_t* words);
+
+/* One in-kernel TP all-reduce (seam.py:391-408, moe.py:1247-1268): dst = bf16(rank-order
+ * fp32 sum of every rank's src), n bf16 elements (a multiple of 8, <= cap). site: the
+ * 1-based number a timed-out wait records; skip_push: the fault-injection hook. */
+typedef struct {
+  int64_t n, tp, rank, peers, cap, src, dst, deadline_ns, site, skip_push;
+} Dsv41AllReduceArgs;
+int dsv41_allreduce(const Dsv41AllReduceArgs* a, void* stream);
+
+/* out = bf16(rank-order fp32 sum of parts[r]), parts [tp][n] bf16 contiguous: the reduction
+ * step of the NCCL variant (all-gather, then this); bit-identical to dsv41_allreduce.
+ * No counterpart kernel in the reference (its comparison path is NCCL's all_reduce). */
+typedef struct {
+  int64_t n, tp, parts, out;
+} Dsv41RankSumArgs;
+int dsv41_rank_sum(const Dsv41RankSumArgs* a, void* stream);
 
 /* Kernels this library has launched in this process (all entry points): for profiling. */
 int64_t dsv41_launch_count(void);

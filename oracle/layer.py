@@ -401,3 +401,44 @@ def moe_partial(normed, w, route_kind, topk, block=128):
     routed = routed_experts(x8r, x8rs, ids, wts, w["w13"], w["s13"], w["w2"], w["s2"])
     shared = shared_expert(x8, x8s, w["sgu"], w["sgu_s"], w["sw2"], w["sw2_s"], block)
     return bf(routed + shared), ids, wts, logits
+
+
+# ---------------------------------------------------------------- the whole layer over tp ranks
+def decode_layer(ws, S, shape, cache=None):
+    """One decode layer of M rows over ``len(ws)`` TP ranks (``ws[r]``: rank r's weight shards;
+    replicated tensors are read from ws[0]), from a step ``S`` (``synth.make_step``'s keys):
+    the attention seam, wqkv_a, the q path and KV record (written into ``cache``, a copy of
+    S["cache"] unless given), then per rank its heads' attention, wo_a and wo_b partial; the
+    attention all-reduce; the FFN seam; per rank its expert-slice MoE partial; the MoE
+    all-reduce (``layer.py:773-1072``). Returns a dict of the intermediate and final tensors."""
+    W = ws[0]
+    M = S["res"].shape[0]
+    cs = W["cos_sin"][S["pos"]]
+    cosv, sinv = cs[:, :32], cs[:, 32:]
+    QL, D, nope = shape.q_lora, shape.head_dim, shape.nope
+    cache = S["cache"].clone() if cache is None else cache
+    rn, normed, pre, post, comb = seam(S["res"].float(), S["x"].float(), S["post"], S["comb"], S["pre"],
+                                       W["hc_attn_fn"], W["hc_attn_scale"], W["hc_attn_base"], W["attn_norm"])
+    x8, x8s = N.mxfp8_quant(normed, "vllm")
+    qkv = gemv_x8_fp8(x8, x8s, W["wqkv"], W["wqkv_s"])
+    _, qx8, qx8s = q_path(qkv[:, :QL], W["q_norm"])
+    nb, rb, codes = kv_record(qkv[:, QL:], W["kv_norm"], cosv, sinv, nope)
+    data, sc = record_bytes(nb, rb, codes, 8)
+    write_records(cache, S["slot"], data, sc, S["blk"])
+    kt, klen = key_table(S["slot"], S["swa_idx"], S["swa_lens"], None, torch.zeros(M, dtype=torch.int32),
+                         S["swa_idx"].shape[1], 0)
+    attn_parts = []
+    for w in ws:
+        q = rope_q(bf(gemv_x8_fp8(qx8, qx8s, w["wqb"], w["wqb_s"])).view(M, -1, D), cosv, sinv, nope)
+        xo = attention(q, kt, klen, cache, S["blk"], None, 1, w["sink"], cosv, sinv, nope, shape.rope, 8)
+        _, x8b, x8bs = wo_a(xo, w["woa"], w["woa_s"], shape.groups_local, shape.o_rank)
+        attn_parts.append(wo_b(x8b, x8bs, w["wob"], w["wob_s"]))
+    attn = all_reduce(attn_parts)
+    rn2, normed2, *_ = seam(rn, attn, post, comb, pre, W["hc_ffn_fn"], W["hc_ffn_scale"], W["hc_ffn_base"],
+                            W["ffn_norm"])
+    moe_parts, ids = [], None
+    for w in ws:
+        part, ids, _, _ = moe_partial(normed2, w, shape.route, shape.topk)
+        moe_parts.append(part)
+    return dict(cache=cache, attn_parts=attn_parts, attn=attn, res2=rn2, normed2=normed2,
+                moe_parts=moe_parts, out=all_reduce(moe_parts), ids=ids)

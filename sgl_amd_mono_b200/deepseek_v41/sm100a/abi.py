@@ -34,7 +34,7 @@ K2Args = struct("Dsv41K2Args", [
     "res_out", "post_out", "comb_out", "pre_out", "normed",
     "gate_w", "bias", "w13", "w13_codes", "w2", "w2_codes", "sgu", "sgu_codes", "sw2", "sw2_codes",
     "out", "ids", "wts", "xo", "x8b", "x8bs", "attn_part", "attn", "logits", "moe_part",
-    "peer_attn", "peer_moe", "peer_flags", "epoch", "deadline_ns", "events",
+    "peers", "peer_cap", "deadline_ns", "phase", "inject", "events",
     "scratch", "scratch_bytes",
 ])
 K2_STAGES = ("attention", "wo_a+wo_b", "reduce+ffn seam", "router", "shared expert", "routed experts",
@@ -63,6 +63,12 @@ MapCompactArgs = struct("Dsv41MapCompactArgs", [
     "owners", "raw_out", "page_out", "out_stride",
 ])
 
+AllReduceArgs = struct("Dsv41AllReduceArgs", [
+    "n", "tp", "rank", "peers", "cap", "src", "dst", "deadline_ns", "site", "skip_push",
+])
+
+RankSumArgs = struct("Dsv41RankSumArgs", ["n", "tp", "parts", "out"])
+
 STRUCTS = {
     "Dsv41GemvArgs": GemvArgs,
     "Dsv41RelayoutArgs": RelayoutArgs,
@@ -73,4 +79,6 @@ STRUCTS = {
     "Dsv41TopkArgs": TopkArgs,
     "Dsv41ReindexArgs": ReindexArgs,
     "Dsv41MapCompactArgs": MapCompactArgs,
+    "Dsv41AllReduceArgs": AllReduceArgs,
+    "Dsv41RankSumArgs": RankSumArgs,
 }

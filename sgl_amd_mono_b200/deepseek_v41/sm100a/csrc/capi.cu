@@ -4,6 +4,7 @@
 // while the previous kernel drains; each kernel waits (griddepcontrol.wait) before reading
 // what the previous one wrote.
 #include <cstdio>
+#include <cstring>
 #include <algorithm>
 #include <atomic>
 #include <cmath>
@@ -19,6 +20,7 @@
 #include "gemv.cuh"
 #include "k2i.cuh"
 #include "moe.cuh"
+#include "peer.cuh"
 #include "seam.cuh"
 
 using namespace dsv41;
@@ -258,13 +260,34 @@ bool k2_ok(const Dsv41K2Args* a) {
   if (a->o_groups < 1 || a->o_rank % 128 || a->heads % a->o_groups) return false;
   if (((a->heads / a->o_groups) * (a->nope + a->rope)) % 128) return false;
   if (a->experts < 1 || a->experts > 512 || a->topk < 1 || a->topk > 32) return false;
-  if (a->inter % 128 || a->shared_inter % 128 || a->tp != 1) return false;
+  if (a->inter % 128 || a->shared_inter % 128 || a->tp < 1 || a->tp > kPeerMaxTp) return false;
+  if (a->rank < 0 || a->rank >= a->tp || a->phase < 0 || a->phase > 2 || a->inject < 0 || a->inject > 2)
+    return false;
+  if (a->tp > 1 && a->phase == 0 && (!a->peers || a->peer_cap < a->M * a->hidden || a->peer_cap % 8))
+    return false;
+  if (a->phase == 2 && (!a->attn || !a->moe_part)) return false;
+  if (a->phase == 1 && !a->attn_part) return false;
   if (!a->q || !a->kt || !a->klen || !a->swa || !a->sink || !a->woa || !a->wob) return false;
   if (!a->res_in || !a->post_in || !a->comb_in || !a->pre_in || !a->hc_fn || !a->norm_w) return false;
   if (!a->gate_w || !a->w13 || !a->w2 || !a->sgu || !a->sw2 || !a->out || !a->ids || !a->wts) return false;
   if (!a->route_softmax && !a->bias) return false;
   if (a->hidden % 1024 && a->hidden > 1024) return false;
   return true;
+}
+
+int64_t deadline_or_default(int64_t ns) { return ns > 0 ? ns : 5000000000LL; }
+
+// One in-kernel exchange: CTAs of 256 threads, a thread a 16-byte vector, at most kArBlocks
+// (every CTA resident, so each CTA's wait only needs the same CTA on the other ranks).
+cudaError_t allreduce_go(int n, int tp, int rank, int64_t peers, int64_t cap, const void* src, void* dst,
+                         int64_t deadline_ns, int site, int skip, cudaStream_t st) {
+  AllReduceArgs r = {};
+  r.n = n; r.tp = tp; r.rank = rank;
+  r.nblk = std::max(1, std::min(kArBlocks, cdiv(n / 8, 256)));
+  r.peers = ptr<const int64_t>(peers); r.cap = cap;
+  r.src = reinterpret_cast<const __nv_bfloat16*>(src); r.dst = reinterpret_cast<__nv_bfloat16*>(dst);
+  r.deadline_ns = deadline_or_default(deadline_ns); r.site = site; r.skip_push = skip;
+  return launch(allreduce_kernel, dim3(r.nblk), dim3(256), 0, st, r);
 }
 
 struct K2Plan {
@@ -351,6 +374,9 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   if (!a->scratch || a->scratch_bytes < c.off) return DSV41_ESCRATCH;
   if (eu.ks_len % 128 || ed.ks_len % 128 || H % eu.ks_len || I % ed.ks_len) return DSV41_EINVAL;
 
+  const int phase = (int)a->phase, tp = (int)a->tp, rank = (int)a->rank;
+  const __nv_bfloat16* reduced = attn;
+  if (phase != 2) {
   // ---- attention
   AttnArgs at = {};
   at.M = M; at.heads = heads; at.D = D; at.nope = nope; at.rope = rope; at.keys_ld = keys;
@@ -376,11 +402,17 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   FinalizeArgs fb = {M, H, gb.kslices, gb.out, attn_part, nullptr, nullptr};
   DSV41_TRY(launch(finalize_kernel, dim3(grid_for((int64_t)M * H / 8, 256)), dim3(256), 0, st, fb));
   mark(a->events, 2, st);
-  // tp == 1: the all-reduce of one rank's bf16 partial is the partial itself
-  const __nv_bfloat16* reduced = attn_part;
-  if (attn != attn_part) {
+  if (phase == 1) return launch_status();
+  if (tp > 1) {
+    // the attention all-reduce (site 1)
+    DSV41_TRY(allreduce_go(M * H, tp, rank, a->peers, a->peer_cap, attn_part, attn, a->deadline_ns, 1,
+                           a->inject == 1, st));
+  } else if (attn != attn_part) {
+    // tp == 1: the all-reduce of one rank's bf16 partial is the partial itself
     DSV41_TRY(cudaMemcpyAsync(attn, attn_part, (size_t)M * H * 2, cudaMemcpyDeviceToDevice, st));
-    reduced = attn;
+  } else {
+    reduced = attn_part;
+  }
   }
   // ---- FFN seam
   SeamArgs s = {};
@@ -422,9 +454,15 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   CombineMoeArgs cm = {M, H, TK, ed.kslices, gd.kslices, ed.out, ptr<const float>(a->wts), gd.out, moe_part};
   mark(a->events, 6, st);
   DSV41_TRY(launch(moe_combine_kernel, dim3(grid_for((int64_t)M * H, 256)), dim3(256), 0, st, cm));
-  // tp == 1: the MoE all-reduce of one partial is the partial
-  if (ptr<__nv_bfloat16>(a->out) != moe_part)
+  if (phase == 2) return launch_status();
+  if (tp > 1) {
+    // the MoE all-reduce (site 2)
+    DSV41_TRY(allreduce_go(M * H, tp, rank, a->peers, a->peer_cap, moe_part, ptr<void>(a->out), a->deadline_ns,
+                           2, a->inject == 2, st));
+  } else if (ptr<__nv_bfloat16>(a->out) != moe_part) {
+    // tp == 1: the MoE all-reduce of one partial is the partial
     DSV41_TRY(cudaMemcpyAsync(ptr<void>(a->out), moe_part, (size_t)M * H * 2, cudaMemcpyDeviceToDevice, st));
+  }
   mark(a->events, 7, st);
   return launch_status();
 }
@@ -523,6 +561,76 @@ int dsv41_map_compact(const Dsv41MapCompactArgs* a, void* stream) {
                       ptr<const int32_t>(a->page_table), (int)a->table_stride, ptr<const int32_t>(a->owners),
                       ptr<int32_t>(a->raw_out), ptr<int32_t>(a->page_out), (int)a->out_stride};
   DSV41_TRY(launch(map_compact_kernel, dim3((int)a->rows), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), m));
+  return launch_status();
+}
+
+int64_t dsv41_peer_region_bytes(int64_t tp, int64_t cap) {
+  if (tp < 1 || tp > kPeerMaxTp || cap < 8 || cap % 8) return DSV41_EINVAL;
+  return peer_region_bytes((int)tp, cap);
+}
+
+int dsv41_peer_alloc(int64_t bytes, int64_t* region, uint8_t* handle) {
+  if (bytes < kPeerDataOff || !region || !handle) return DSV41_EINVAL;
+  void* p = nullptr;
+  if (cudaMalloc(&p, (size_t)bytes) != cudaSuccess) return launch_status();
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, (size_t)bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return launch_status();
+  }
+  static_assert(sizeof(h) == DSV41_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  *region = reinterpret_cast<int64_t>(p);
+  return DSV41_OK;
+}
+
+int dsv41_peer_open(const uint8_t* handle, int64_t* region) {
+  if (!handle || !region) return DSV41_EINVAL;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return launch_status();
+  *region = reinterpret_cast<int64_t>(p);
+  return DSV41_OK;
+}
+
+int dsv41_peer_close(int64_t region) {
+  if (!region) return DSV41_EINVAL;
+  if (cudaIpcCloseMemHandle(reinterpret_cast<void*>(region)) != cudaSuccess) return launch_status();
+  return DSV41_OK;
+}
+
+int dsv41_peer_free(int64_t region) {
+  if (!region) return DSV41_EINVAL;
+  if (cudaFree(reinterpret_cast<void*>(region)) != cudaSuccess) return launch_status();
+  return DSV41_OK;
+}
+
+int dsv41_peer_status(int64_t region, int32_t* words) {
+  if (!region || !words) return DSV41_EINVAL;
+  if (cudaMemcpy(words, reinterpret_cast<const void*>(region), DSV41_GUARD_WORDS * 4, cudaMemcpyDeviceToHost) !=
+      cudaSuccess)
+    return launch_status();
+  return (words[kErrDeadline] | words[kErrPeer] | words[kErrFault]) ? DSV41_EDEVICE : DSV41_OK;
+}
+
+int dsv41_allreduce(const Dsv41AllReduceArgs* a, void* stream) {
+  if (!a || a->tp < 1 || a->tp > kPeerMaxTp || a->rank < 0 || a->rank >= a->tp || !a->peers || !a->src ||
+      !a->dst || a->n < 8 || a->n % 8 || a->cap < a->n || a->cap % 8 || a->n > (1LL << 30) || a->src % 16 ||
+      a->dst % 16)
+    return DSV41_EINVAL;
+  DSV41_TRY(allreduce_go((int)a->n, (int)a->tp, (int)a->rank, a->peers, a->cap, ptr<const void>(a->src),
+                         ptr<void>(a->dst), a->deadline_ns, (int)a->site, (int)a->skip_push,
+                         reinterpret_cast<cudaStream_t>(stream)));
+  return launch_status();
+}
+
+int dsv41_rank_sum(const Dsv41RankSumArgs* a, void* stream) {
+  if (!a || a->n < 1 || a->tp < 1 || a->tp > kPeerMaxTp || !a->parts || !a->out || a->n > (1LL << 30))
+    return DSV41_EINVAL;
+  RankSumArgs r = {(int)a->n, (int)a->tp, ptr<const __nv_bfloat16>(a->parts), ptr<__nv_bfloat16>(a->out)};
+  DSV41_TRY(launch(rank_sum_kernel, dim3(grid_for(a->n, 256)), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
+                   r));
   return launch_status();
 }
 

@@ -58,23 +58,6 @@ __global__ void finalize_kernel(const FinalizeArgs a) {
   pdl_launch();
 }
 
-// out = bf16(sum over ranks in rank order of the bf16 partials), fp32 accumulation.
-struct RankSumArgs {
-  int n, tp;
-  const __nv_bfloat16* const* parts;  // tp pointers (device-visible table)
-  __nv_bfloat16* out;
-};
-
-__global__ void rank_sum_kernel(const RankSumArgs a) {
-  pdl_wait();
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += gridDim.x * blockDim.x) {
-    float s = 0.f;
-    for (int r = 0; r < a.tp; ++r) s += bf2f(a.parts[r][i]);
-    a.out[i] = __float2bfloat16_rn(s);
-  }
-  pdl_launch();
-}
-
 // MXFP4 weight [E][N][K/2] (even K in the low nibble) + E8M0 [E][N][K/32] -> fragment order:
 // tile (e, rt, kc) of 16 rows x 128 K is 1024 bytes; byte 16 L + q of half h (h = 0, 1) of
 // lane L = 4 g + t holds, for jj = q / 4 (block b = 2 h + jj / 2, half j = jj % 2) and

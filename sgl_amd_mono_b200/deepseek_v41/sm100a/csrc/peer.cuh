@@ -1,0 +1,189 @@
+// The TP all-reduce over peer memory: every rank pushes its bf16 partial into a slot of every
+// rank's exchange region (NVLink stores through CUDA IPC mappings), raises a per-CTA arrival
+// flag there, waits for every rank's flag in its own region, and sums the slots in rank order
+// in fp32 before one rounding to bf16 -- the reference's one-shot push and fixed-order sum
+// (seam.py:391-408, moe.py:1247-1268, ops.py:269-277), with its mailbox / guard / epoch roles
+// (sync.py:29-197, guard.py:103-224, epoch.py:52-85) done by this layout:
+//
+//   [0, 256)      guard words (uint32): 0 the exchange sequence (epoch), 1 CTAs done with the
+//                 current exchange, 3 the site (1-based) of the first wait on this GPU that ran
+//                 past its deadline, 4 set when a wait saw another rank's failure flag, 5 set
+//                 by the fault-injection hook (this rank stalled: no push, no flag)
+//   [256, 288)    failure flags: rank r writes word r of every rank's region when it fails
+//   [512, +4 * kPeerMaxTp * kArBlocks)   arrival flags [src rank][CTA], the sequence number
+//   [kPeerDataOff, ...)  data slots [parity][src rank][cap] bf16
+//
+// Sequence numbers only grow, so a waiter accepts any flag >= its own; the data of exchange e
+// lives in parity e & 1, which no rank can overwrite before every rank has finished reading it
+// (a rank reaches exchange e + 2 only after every rank raised its flag for e + 1, which each
+// does after finishing e). A wait gives up after ``deadline_ns`` of %globaltimer: it records
+// its site, raises this rank's failure flag in every region and returns -- a device-side
+// failure is a status the host reads (dsv41_peer_status), never a fault. Failures are sticky:
+// an exchange that starts on a failed region (any error word, or any rank's failure flag
+// raised in it) does nothing.
+#pragma once
+
+#include "common.cuh"
+
+namespace dsv41 {
+
+constexpr int kPeerMaxTp = 8;
+constexpr int kArBlocks = 128;     // CTAs an exchange at most (all resident: one an SM)
+constexpr int kGuardSeq = 0, kGuardDone = 1, kErrDeadline = 3, kErrPeer = 4, kErrFault = 5;
+constexpr int kFailOff = 256;
+constexpr int kArriveOff = 512;
+constexpr int kPeerDataOff = 8192;
+
+__host__ __device__ inline int64_t peer_region_bytes(int tp, int64_t cap) {
+  return kPeerDataOff + 2LL * tp * cap * 2;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+struct AllReduceArgs {
+  int n, tp, rank, nblk;        // n bf16 elements (a multiple of 8)
+  const int64_t* peers;         // [tp] each rank's region as mapped in this process
+  int64_t cap;                  // elements a data slot holds (a multiple of 8, >= n)
+  const __nv_bfloat16* src;     // this rank's partial [n]
+  __nv_bfloat16* dst;           // the reduced [n]
+  int64_t deadline_ns;
+  int site, skip_push;          // skip_push: the fault-injection hook (publish nothing)
+};
+
+__device__ __forceinline__ uint32_t* peer_words(int64_t base) { return reinterpret_cast<uint32_t*>(base); }
+__device__ __forceinline__ uint32_t* arrive_flag(int64_t base, int src, int b) {
+  return reinterpret_cast<uint32_t*>(base + kArriveOff) + src * kArBlocks + b;
+}
+__device__ __forceinline__ uint4* peer_slot(int64_t base, int par, int tp, int src, int64_t cap) {
+  return reinterpret_cast<uint4*>(base + kPeerDataOff + ((int64_t)(par * tp + src) * cap) * 2);
+}
+
+// Wait until ``flag`` reaches epoch e, another rank fails, or the deadline passes (every
+// 64 polls the failure flags and the clock are checked). Returns true on arrival.
+__device__ inline bool wait_arrival(const AllReduceArgs& a, const uint32_t* flag, uint32_t e) {
+  const int64_t me = a.peers[a.rank];
+  uint64_t t0 = 0;
+  for (uint32_t it = 1; it != 0; ++it) {
+    if ((int)(ld_acquire_sys(flag) - e) >= 0) return true;
+    if ((it & 63) != 0) continue;
+    bool failed = false;
+    for (int r = 0; r < a.tp; ++r)
+      if (r != a.rank) failed |= ld_acquire_sys(peer_words(me + kFailOff) + r) != 0;
+    if (failed) {
+      atomicExch(peer_words(me) + kErrPeer, 1u);
+      return false;
+    }
+    const uint64_t now = global_ns();
+    if (t0 == 0) {
+      t0 = now;
+    } else if (now - t0 > (uint64_t)a.deadline_ns) {
+      atomicCAS(peer_words(me) + kErrDeadline, 0u, (uint32_t)a.site);
+      for (int r = 0; r < a.tp; ++r) st_release_sys(peer_words(a.peers[r] + kFailOff) + a.rank, 1u);
+      return false;
+    }
+  }
+  atomicCAS(peer_words(me) + kErrDeadline, 0u, (uint32_t)a.site);  // 2^32 polls: give up too
+  return false;
+}
+
+__global__ void __launch_bounds__(256) allreduce_kernel(const AllReduceArgs a) {
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_fail;
+  pdl_wait();
+  const int tid = threadIdx.x, b = blockIdx.x;
+  const int64_t me = a.peers[a.rank];
+  uint32_t* words = peer_words(me);
+  if (tid == 0) {
+    s_epoch = __ldcg(words + kGuardSeq) + 1u;
+    // sticky: this rank's earlier failure, or a failure flag another rank raised here
+    uint32_t f = __ldcg(words + kErrDeadline) | __ldcg(words + kErrPeer) | __ldcg(words + kErrFault);
+    for (int r = 0; r < a.tp; ++r) f |= __ldcg(peer_words(me + kFailOff) + r);
+    s_fail = f != 0;
+  }
+  __syncthreads();
+  const uint32_t e = s_epoch;
+  const int par = (int)(e & 1u);
+  const int nv = a.n / 8;
+  const int per = (nv + a.nblk - 1) / a.nblk;
+  const int v0 = min(nv, b * per), v1 = min(nv, v0 + per);
+  if (!s_fail && a.skip_push) {
+    // the fault-injection hook: this rank stalls -- it publishes nothing and raises no flag,
+    // so the other ranks' waits run out -- and its exchange fails
+    if (tid == 0) atomicExch(words + kErrFault, 1u);
+  } else if (!s_fail) {
+    const uint4* src = reinterpret_cast<const uint4*>(a.src);
+    for (int v = v0 + tid; v < v1; v += blockDim.x) {
+      const uint4 x = src[v];
+      for (int r = 0; r < a.tp; ++r) peer_slot(a.peers[r], par, a.tp, a.rank, a.cap)[v] = x;
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (tid < a.tp) st_release_sys(arrive_flag(a.peers[tid], a.rank, b), e);
+    if (tid < a.tp && !wait_arrival(a, arrive_flag(me, tid, b), e)) atomicOr(&s_fail, 1);
+    __syncthreads();
+    if (!s_fail) {
+      uint4* dst = reinterpret_cast<uint4*>(a.dst);
+      for (int v = v0 + tid; v < v1; v += blockDim.x) {
+        float acc[8];
+        for (int r = 0; r < a.tp; ++r) {
+          const uint4 x = __ldcg(peer_slot(me, par, a.tp, r, a.cap) + v);
+          const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float lo = __uint_as_float(w[q] << 16), hi = __uint_as_float(w[q] & 0xFFFF0000u);
+            acc[2 * q] = r ? acc[2 * q] + lo : lo;
+            acc[2 * q + 1] = r ? acc[2 * q + 1] + hi : hi;
+          }
+        }
+        uint32_t o[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) o[q] = pack_bf16x2(acc[2 * q], acc[2 * q + 1]);
+        dst[v] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+  // the exchange's end: the last CTA advances the sequence
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(words + kGuardDone, 1u) == (uint32_t)(a.nblk - 1)) {
+      atomicExch(words + kGuardDone, 0u);
+      __threadfence();
+      atomicExch(words + kGuardSeq, e);
+    }
+  }
+  pdl_launch();
+}
+
+// out = bf16(sum over ranks in rank order of parts[r]), fp32 accumulation: the reduction step
+// of the NCCL variant (an all-gather of the partials, then this), bit-identical to the
+// in-kernel exchange.
+struct RankSumArgs {
+  int n, tp;
+  const __nv_bfloat16* parts;  // [tp][n]
+  __nv_bfloat16* out;
+};
+
+__global__ void rank_sum_kernel(const RankSumArgs a) {
+  pdl_wait();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += gridDim.x * blockDim.x) {
+    float s = bf2f(a.parts[i]);
+    for (int r = 1; r < a.tp; ++r) s += bf2f(a.parts[(size_t)r * a.n + i]);
+    a.out[i] = __float2bfloat16_rn(s);
+  }
+  pdl_launch();
+}
+
+}  // namespace dsv41

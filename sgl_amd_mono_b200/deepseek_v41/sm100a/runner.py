@@ -7,13 +7,21 @@ scratch belong to the runner and are allocated per width outside graph capture
 (``buffers``); every launch goes on the current stream, so a step can be captured in a CUDA
 graph and replayed. Host-side argument errors raise ``RuntimeError``; a launch's negative
 status raises ``ExtError``.
+
+Tensor parallelism (tp > 1): the weights are this rank's shards (``synth.make_layer`` with
+``rank``), and K2's two all-reduces run either in-kernel through a ``PeerBuffer`` (the
+default, ``allreduce="peer"``) or as the NCCL variant (``allreduce="nccl"``: K2 in two
+phases around an all-gather of the bf16 partials and the same rank-order fp32 sum, so both
+give identical bits). ``check()`` raises if a device-side guard fired.
 """
 
 from __future__ import annotations
 
 import torch
+import torch.distributed as dist
 
 from ...common import ext
+from ...common.peer import MIN_DEADLINE_S, PeerBuffer, fault_injection
 from ..shapes import LayerShape
 from . import abi
 
@@ -51,8 +59,22 @@ class Layer:
 class MonoRunner:
     MAX_ROWS = 48
 
-    def __init__(self, shape: LayerShape, device: torch.device, copies: dict | None = None):
+    def __init__(self, shape: LayerShape, device: torch.device, copies: dict | None = None, *,
+                 rank: int = 0, peers: PeerBuffer | None = None, group=None, allreduce: str = "peer",
+                 deadline_s: float = 5.0):
         shape.check()
+        if not 0 <= rank < shape.tp:
+            raise RuntimeError(f"rank {rank} outside tp {shape.tp}")
+        if allreduce not in ("peer", "nccl"):
+            raise RuntimeError(f"allreduce {allreduce!r}: 'peer' or 'nccl'")
+        if shape.tp > 1 and allreduce == "peer" and peers is None:
+            raise RuntimeError("tp > 1 with the in-kernel all-reduce needs a PeerBuffer")
+        if deadline_s < MIN_DEADLINE_S:
+            raise RuntimeError(f"deadline {deadline_s} s under {MIN_DEADLINE_S} s")
+        self.rank, self.peers, self.group, self.allreduce = rank, peers, group, allreduce
+        self.deadline_ns = int(deadline_s * 1e9)
+        self._inject = fault_injection(rank) if shape.tp > 1 else None
+        self._k2_count = 0
         self.s = shape
         dev = torch.device(device)
         if dev.type == "cuda" and dev.index is None:
@@ -118,6 +140,10 @@ class MonoRunner:
             # one rank: the reduced attention output is the partial, the MoE output its partial
             b["attn"] = b["attn_part"] if s.tp == 1 else z(M, H, dt=bf)
             b["moe_part"] = b["out"] if s.tp == 1 else z(M, H, dt=bf)
+            if s.tp > 1:
+                if self.peers is not None and self.peers.cap < M * H:
+                    raise RuntimeError(f"peer slots of {self.peers.cap} elements < {M} x {H}")
+                b["gathered"] = z(s.tp, M, H, dt=bf)  # the NCCL variant's all-gather
         return self._bufs[key]
 
     def _scratch_for(self, kind: str, M: int, need: int) -> torch.Tensor:
@@ -165,13 +191,14 @@ class MonoRunner:
 
     # ------------------------------------------------------------ K2
     def k2_args(self, L: Layer, step: dict, M: int, b: dict, *, comp=None, comp_stride=0, comp_blk=0,
-                events=0):
+                events=0, phase=0, inject=0):
         s = self.s
         w = L
+        peers = self.peers if s.tp > 1 else None
         a = abi.K2Args(
             M=M, hidden=s.hidden, nope=s.nope, rope=s.rope, heads=s.heads_local, o_groups=s.groups_local,
             o_rank=s.o_rank, experts=s.experts, topk=s.topk, inter=s.inter_local,
-            shared_inter=s.shared_local, route_softmax=int(s.route == "softmax"), tp=s.tp, rank=0,
+            shared_inter=s.shared_local, route_softmax=int(s.route == "softmax"), tp=s.tp, rank=self.rank,
             keys_ld=b["kt"].shape[1],
             q=_p(b["q"]), kt=_p(b["kt"]), klen=_p(b["klen"]), swa=_p(step["cache"]),
             swa_stride=step["page_stride"], swa_blk=step["blk"], comp=_p(comp), comp_stride=comp_stride,
@@ -187,7 +214,8 @@ class MonoRunner:
             sw2=_p(w["sw2"]), sw2_codes=_p(w["sw2_s"]),
             out=_p(b["out"]), ids=_p(b["ids"]), wts=_p(b["wts"]), xo=_p(b["xo"]), x8b=_p(b["x8b"]),
             x8bs=_p(b["x8bs"]), attn_part=_p(b["attn_part"]), attn=_p(b["attn"]), logits=_p(b["logits"]),
-            moe_part=_p(b["moe_part"]), peer_attn=0, peer_moe=0, peer_flags=0, epoch=0, deadline_ns=0,
+            moe_part=_p(b["moe_part"]), peers=_p(peers.table) if peers else 0,
+            peer_cap=peers.cap if peers else 0, deadline_ns=self.deadline_ns, phase=phase, inject=inject,
             events=events,
             scratch=0, scratch_bytes=0,
         )
@@ -197,6 +225,28 @@ class MonoRunner:
         return a
 
     def k2(self, L: Layer, step: dict, M: int, b: dict, **kw) -> dict:
-        a = self.k2_args(L, step, M, b, **kw)
+        s = self.s
+        if s.tp > 1 and self.allreduce == "nccl":
+            for phase, part, dst in ((1, "attn_part", "attn"), (2, "moe_part", "out")):
+                ext.call("dsv41_k2", self.k2_args(L, step, M, b, phase=phase, **kw), _stream())
+                self._nccl_reduce(b[part], b["gathered"], b[dst])
+            return b
+        inject = 0
+        if self._inject is not None and self._k2_count == self._inject[1]:
+            inject = self._inject[0]
+        self._k2_count += 1
+        a = self.k2_args(L, step, M, b, inject=inject, **kw)
         ext.call("dsv41_k2", a, _stream())
         return b
+
+    def _nccl_reduce(self, part: torch.Tensor, gathered: torch.Tensor, out: torch.Tensor) -> None:
+        """The NCCL variant of an all-reduce: all-gather the bf16 partials, then the rank-order
+        fp32 sum (``dsv41_rank_sum``)."""
+        dist.all_gather_into_tensor(gathered, part, group=self.group)
+        a = abi.RankSumArgs(n=part.numel(), tp=self.s.tp, parts=_p(gathered), out=_p(out))
+        ext.call("dsv41_rank_sum", a, _stream())
+
+    def check(self) -> None:
+        """Raise ``DeviceGuardError`` if a device-side guard fired on this rank (synchronizes)."""
+        if self.peers is not None:
+            self.peers.check()
