@@ -11,8 +11,12 @@ in L2 (each step also reads more than L2 holds). ``value`` = decode tokens/s of 
 (M rows / layer time, summed over ranks); the sweep over M = 1, 4, 16, 48 and the per-M
 fraction of the HBM weight-streaming roofline are in ``config``.
 
-With N > 1 (torchrun), each rank runs its own replica of the layer (weak scaling: no data-path
-collective in this mode); ``value`` sums the ranks' rows over the max-over-ranks time.
+With N > 1 (torchrun), the same layer runs tensor-parallel over the N ranks (TP = N: heads,
+wo_a groups, expert and shared-expert intermediates sharded; wqkv_a, the router and the KV
+cache replicated), with both all-reduces in-kernel through CUDA IPC peer regions (strong
+scaling: the same M rows at every N; ``value`` = M / the max-over-ranks layer time). The
+NCCL variant of the all-reduces (all-gather + rank-order sum) and the exchanges alone are
+timed beside it, at the headline M.
 
 ``--impl reference`` times the reference path's CPU restatement (the repository's oracle:
 torch fp32/fp64 on the host cores, all threads) on a bounded sample of the same workload.
@@ -202,8 +206,11 @@ def run_ours(args, world, rank, local):
     from sgl_amd_mono_b200.deepseek_v41.sm100a import abi
     from sgl_amd_mono_b200.deepseek_v41.sm100a.runner import MonoRunner
 
+    from sgl_amd_mono_b200.common.peer import PeerBuffer
+
     dev = torch.device("cuda", local if world > 1 else 0)
-    shape = CONFIG2
+    tp = world
+    shape = CONFIG2.sharded(tp) if tp > 1 else CONFIG2
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
@@ -212,16 +219,17 @@ def run_ours(args, world, rank, local):
         pass
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
-    runner = MonoRunner(shape, dev)
-    layers = [runner.bind(synth.make_layer(shape, args.seed + 7919 * i + rank, dev, positions=args.ctx + 8),
-                          tag=f"layer{i}") for i in range(args.layers)]
     sweep = sorted({int(x) for x in args.sweep.split(",") if x} | {args.rows})
+    peers = PeerBuffer(max(sweep) * shape.hidden, None, rank, world, dev) if tp > 1 else None
+    runner = MonoRunner(shape, dev, rank=rank, peers=peers)
+    # every rank draws the same full layer and keeps its shard
+    layers = [runner.bind(synth.make_layer(shape, args.seed + 7919 * i, dev, positions=args.ctx + 8, rank=rank),
+                          tag=f"layer{i}") for i in range(args.layers)]
     stream = torch.cuda.current_stream()
     results, graphs_by_m, steps_by_m, bufs_by_m = {}, {}, {}, {}
     launches_per_step = None
     for M in sweep:
-        steps = [synth.make_step(shape, M, args.ctx, args.seed + 100 * i + M + 1000 * rank, dev)
-                 for i in range(args.layers)]
+        steps = [synth.make_step(shape, M, args.ctx, args.seed + 100 * i + M, dev) for i in range(args.layers)]
         graphs, bufs = [], []
         for L, st in zip(layers, steps):
             b = runner.k1(L, st, M)  # eager: allocates buffers and scratch outside capture
@@ -260,7 +268,7 @@ def run_ours(args, world, rank, local):
         lb = [roofline.layer_bytes(shape, u, k)["total"] for u, k in zip(unions, keys)]
         avg_bytes = sum(lb) / len(lb)
         gbs = avg_bytes / (ms * 1e-3) / 1e9
-        results[M] = {"us_per_layer": round(ms * 1e3, 2), "tokens_s": round(world * M / (ms * 1e-3), 1),
+        results[M] = {"us_per_layer": round(ms * 1e3, 2), "tokens_s": round(M / (ms * 1e-3), 1),
                       "algorithmic_MB": round(avg_bytes / 1e6, 1), "union": unions,
                       "GBs": round(gbs, 1), "frac_hbm": round(gbs / hbm_peak, 4)}
         if clk is not None:
@@ -269,7 +277,9 @@ def run_ours(args, world, rank, local):
 
     M = args.rows
     ms = results[M]["us_per_layer"] / 1e3
-    value = world * M / (ms * 1e-3)
+    value = M / (ms * 1e-3)
+    runner.check()  # no device-side guard fired during the timed steps
+    tp_extra = tp_comparison(args, runner, layers, steps_by_m[M], bufs_by_m[M], M, world, stream) if tp > 1 else None
 
     # ---- stage timelines (eager launches, CUDA events at stage boundaries on the stream)
     n1, n2 = len(abi.K1_STAGES), len(abi.K2_STAGES)
@@ -348,10 +358,12 @@ def run_ours(args, world, rank, local):
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "fp8/mxfp4 weights, bf16 activations",
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp8/mxfp4 weights, bf16 activations",
             "data": "synthetic (random-init, seeded)",
             "config": {"workload": f"config2: one MoE decode layer (K1 + K2), {M} rows, ctx {args.ctx}",
-                       "rows": M, "ctx": args.ctx, "tp": 1, "parallelism": f"replicas x{world}",
+                       "rows": M, "ctx": args.ctx, "tp": tp, "parallelism": f"tp{tp}",
+                       "allreduce": "in-kernel peer push, rank-order fp32 sum" if tp > 1 else "none (tp1)",
+                       "tp_comparison": tp_extra,
                        "l2": f"steps alternate {args.layers} layer copies; a step reads "
                              f"{results[M]['algorithmic_MB']} MB (> 126 MB L2)",
                        "layer_roofline": {"GBs": results[M]["GBs"], "frac": results[M]["frac_hbm"],
@@ -364,12 +376,75 @@ def run_ours(args, world, rank, local):
                          "frac": round(achieved / hbm_peak, 4), "traffic": None,
                          "algorithmic_bytes": int(exp_bytes), "peak_source": peak_src},
             "cpu_baseline": cpu,
-            "e2e": {"value": round(world * M / (e2e_ms * 1e-3), 1), "unit": UNIT,
+            "e2e": {"value": round(M / (e2e_ms * 1e-3), 1), "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
+    del graphs_by_m, graphs
+    torch.cuda.synchronize()
+    barrier(world)
+    if peers is not None:
+        peers.close()
+
+
+def tp_comparison(args, runner, layers, steps, bufs, M, world, stream):
+    """At TP > 1: the layer with the NCCL variant of its all-reduces (all-gather + the same
+    rank-order sum, CUDA-graph captured like ours), and one exchange of M x hidden bf16 alone
+    (ours, the NCCL variant, NCCL's own all_reduce), device-timed, max over ranks."""
+    import torch.distributed as dist
+
+    from sgl_amd_mono_b200.common import ext
+    from sgl_amd_mono_b200.deepseek_v41.sm100a import abi
+    from sgl_amd_mono_b200.deepseek_v41.sm100a.runner import MonoRunner
+
+    def timed(fn, reps):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1) / reps, world) * 1e3
+
+    s = runner.s
+    nccl = MonoRunner(s, runner.dev, rank=runner.rank, group=None, allreduce="nccl")
+    graphs = []
+    for L, st in zip(layers, steps):
+        b = nccl.k1(L, st, M)
+        nccl.k2(L, st, M, b)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            nccl.k1(L, st, M)
+            nccl.k2(L, st, M, b)
+        graphs.append(g)
+    it = iter(range(1 << 30))
+    us_nccl = timed(lambda: graphs[next(it) % len(graphs)].replay(), args.steps)
+    del graphs
+    torch.cuda.synchronize()
+    n = M * s.hidden
+    src = torch.randn(n, device=runner.dev).to(torch.bfloat16)
+    dst = torch.empty_like(src)
+    gathered = torch.empty(world, n, dtype=torch.bfloat16, device=runner.dev)
+    pa = abi.AllReduceArgs(n=n, tp=world, rank=runner.rank, peers=runner.peers.table.data_ptr(), cap=runner.peers.cap,
+                           src=src.data_ptr(), dst=dst.data_ptr(), deadline_ns=runner.deadline_ns, site=3,
+                           skip_push=0)
+    ra = abi.RankSumArgs(n=n, tp=world, parts=gathered.data_ptr(), out=dst.data_ptr())
+    us_peer = timed(lambda: ext.call("dsv41_allreduce", pa, stream.cuda_stream), 200)
+    us_gather = timed(lambda: (dist.all_gather_into_tensor(gathered, src),
+                               ext.call("dsv41_rank_sum", ra, stream.cuda_stream)), 200)
+    us_ar = timed(lambda: dist.all_reduce(dst), 200)
+    runner.check()
+    return {"layer_us_nccl_variant": round(us_nccl, 2),
+            "exchange_bytes": 2 * n, "nvlink_bytes_out_per_exchange": 2 * n * (world - 1),
+            "exchange_us": {"in_kernel_peer": round(us_peer, 2), "nccl_allgather_rank_sum": round(us_gather, 2),
+                            "nccl_all_reduce_bf16": round(us_ar, 2)}}
 
 
 class ctypes_events:
