@@ -221,6 +221,29 @@ typedef struct {
 } Dsv41RankSumArgs;
 int dsv41_rank_sum(const Dsv41RankSumArgs* a, void* stream);
 
+/* ---------------------------------------------------------------- LM head and greedy selection
+ * logits = x . W^T for this rank's vocab rows W [V, K] bf16 (row-major, read in place; vocab
+ * row i is global token vbase + i) and x [M, K] bf16, M <= 48, K a multiple of 128; the
+ * argmax of each row (ties to the lower token id) as int64 keys in best [M] (init = 1:
+ * reset first; 0: max-merge into best, e.g. a second vocab shard); optional fp32 logits
+ * [M, V]. Vocab-parallel ranks max-reduce best (int64 MAX) and decode with
+ * dsv41_argmax_decode. Replaces SGLang's logits processor + greedy sampling on the verify
+ * path (reference spec.py:807-833, draft.py:173-195); the fused argmax has no kernel
+ * counterpart in the reference. */
+typedef struct {
+  int64_t M, V, K, vbase, w, x, logits, best, init;
+} Dsv41LmHeadArgs;
+int dsv41_lmhead_argmax(const Dsv41LmHeadArgs* a, void* stream);
+
+/* best [M] keys -> ids [M] int32 and vals [M] fp32 (each optional); with draft [M] int32 (the
+ * verify rows' input tokens, per_req rows a request): accept [M / per_req] = the accepted
+ * draft tokens of each request (draft[j + 1] accepted while it equals row j's argmax) and
+ * next_tok [M / per_req] = the target's token after them. */
+typedef struct {
+  int64_t M, best, ids, vals, draft, per_req, accept, next_tok;
+} Dsv41ArgmaxArgs;
+int dsv41_argmax_decode(const Dsv41ArgmaxArgs* a, void* stream);
+
 /* Kernels this library has launched in this process (all entry points): for profiling. */
 int64_t dsv41_launch_count(void);
 int64_t dsv41_k2_scratch_bytes(const Dsv41K2Args* a);

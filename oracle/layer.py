@@ -442,3 +442,25 @@ def decode_layer(ws, S, shape, cache=None):
         moe_parts.append(part)
     return dict(cache=cache, attn_parts=attn_parts, attn=attn, res2=rn2, normed2=normed2,
                 moe_parts=moe_parts, out=all_reduce(moe_parts), ids=ids)
+
+
+# ---------------------------------------------------------------- LM head and greedy selection
+def lm_head_argmax(x, w):
+    """fp32 logits x . W^T (exact bf16 products summed in fp64, rounded once) and each row's
+    greedy id, ties to the lower id (the north star's rule for SGLang's greedy sampling)."""
+    logits = (f32(x).double() @ f32(w).double().T).float()
+    return logits, _topk_ids(logits, 1)[:, 0]
+
+
+def greedy_accept(ids, draft, per_req):
+    """DSpark's greedy verify of blocks of ``per_req`` rows: row j of a request scored the token
+    after draft[j]; draft[j + 1] is accepted while it equals row j's greedy id. Returns
+    (accepted count, the target's next token) per request."""
+    acc, nxt = [], []
+    for r0 in range(0, ids.numel(), per_req):
+        n = 0
+        while n + 1 < per_req and int(ids[r0 + n]) == int(draft[r0 + n + 1]):
+            n += 1
+        acc.append(n)
+        nxt.append(int(ids[r0 + n]))
+    return torch.tensor(acc, dtype=torch.int32), torch.tensor(nxt, dtype=torch.int32)

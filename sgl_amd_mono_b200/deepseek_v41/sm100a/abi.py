@@ -69,6 +69,10 @@ AllReduceArgs = struct("Dsv41AllReduceArgs", [
 
 RankSumArgs = struct("Dsv41RankSumArgs", ["n", "tp", "parts", "out"])
 
+LmHeadArgs = struct("Dsv41LmHeadArgs", ["M", "V", "K", "vbase", "w", "x", "logits", "best", "init"])
+
+ArgmaxArgs = struct("Dsv41ArgmaxArgs", ["M", "best", "ids", "vals", "draft", "per_req", "accept", "next_tok"])
+
 STRUCTS = {
     "Dsv41GemvArgs": GemvArgs,
     "Dsv41RelayoutArgs": RelayoutArgs,
@@ -81,4 +85,6 @@ STRUCTS = {
     "Dsv41MapCompactArgs": MapCompactArgs,
     "Dsv41AllReduceArgs": AllReduceArgs,
     "Dsv41RankSumArgs": RankSumArgs,
+    "Dsv41LmHeadArgs": LmHeadArgs,
+    "Dsv41ArgmaxArgs": ArgmaxArgs,
 }

@@ -19,6 +19,7 @@
 #include "front.cuh"
 #include "gemv.cuh"
 #include "k2i.cuh"
+#include "lmhead.cuh"
 #include "moe.cuh"
 #include "peer.cuh"
 #include "seam.cuh"
@@ -631,6 +632,38 @@ int dsv41_rank_sum(const Dsv41RankSumArgs* a, void* stream) {
   RankSumArgs r = {(int)a->n, (int)a->tp, ptr<const __nv_bfloat16>(a->parts), ptr<__nv_bfloat16>(a->out)};
   DSV41_TRY(launch(rank_sum_kernel, dim3(grid_for(a->n, 256)), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
                    r));
+  return launch_status();
+}
+
+int dsv41_lmhead_argmax(const Dsv41LmHeadArgs* a, void* stream) {
+  if (!a || a->M < 1 || a->M > 48 || a->V < 1 || a->V > (1LL << 30) || a->K < kLmChunk || a->K % kLmChunk ||
+      a->vbase < 0 || a->vbase + a->V > (1LL << 31) || !a->w || !a->x || !a->best || a->w % 16 || a->x % 16)
+    return DSV41_EINVAL;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  LmHeadArgs l = {ptr<const __nv_bfloat16>(a->w), ptr<const __nv_bfloat16>(a->x), ptr<float>(a->logits),
+                  ptr<long long>(a->best), (int)a->M, (int)a->V, (int)a->K, (int)a->vbase};
+  if (a->init) DSV41_TRY(launch(argmax_init_kernel, dim3(1), dim3(64), 0, st, l));
+  const dim3 grid(cdiv(l.V, kLmRows));
+  const int nt = cdiv(l.M, 8);
+  const int smem = 2 * 8 * nt * kLmLd * 2;
+  switch (nt) {
+    case 1: DSV41_TRY(launch(lmhead_kernel<1>, grid, dim3(256), smem, st, l)); break;
+    case 2: DSV41_TRY(launch(lmhead_kernel<2>, grid, dim3(256), smem, st, l)); break;
+    case 3: DSV41_TRY(launch(lmhead_kernel<3>, grid, dim3(256), smem, st, l)); break;
+    case 4: DSV41_TRY(launch(lmhead_kernel<4>, grid, dim3(256), smem, st, l)); break;
+    case 5: DSV41_TRY(launch(lmhead_kernel<5>, grid, dim3(256), smem, st, l)); break;
+    default: DSV41_TRY(launch(lmhead_kernel<6>, grid, dim3(256), smem, st, l)); break;
+  }
+  return launch_status();
+}
+
+int dsv41_argmax_decode(const Dsv41ArgmaxArgs* a, void* stream) {
+  if (!a || a->M < 1 || a->M > 4096 || !a->best ||
+      (a->draft && (a->per_req < 1 || a->M % a->per_req || !a->accept || !a->next_tok)))
+    return DSV41_EINVAL;
+  ArgmaxArgs d = {ptr<const long long>(a->best), (int)a->M, ptr<int32_t>(a->ids), ptr<float>(a->vals),
+                  ptr<const int32_t>(a->draft), (int)a->per_req, ptr<int32_t>(a->accept), ptr<int32_t>(a->next_tok)};
+  DSV41_TRY(launch(argmax_decode_kernel, dim3(1), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), d));
   return launch_status();
 }
 
