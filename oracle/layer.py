@@ -32,6 +32,18 @@ def f32(x):
 
 
 # ---------------------------------------------------------------- mHC seam
+def fold_post(res, x, post, comb):
+    """The pending post folded into the residual (``seam.py:137-157``): R_new[o] =
+    bf16(fma(c3 r3, ((post x + r0 c0) + c1 r1) + c2 r2)), res [M, HC, H], x [M, H]."""
+    res, x, c = f32(res), f32(x), f32(comb)
+    v = f32(post)[:, :, None] * x[:, None, :] + res[:, 0:1, :] * c[:, 0, :, None]
+    v = v + c[:, 1, :, None] * res[:, 1:2, :]
+    v = v + c[:, 2, :, None] * res[:, 2:3, :]
+    # the last term as one fused multiply-add: the exact product plus v, rounded once
+    v = (c[:, 3, :, None].double() * res[:, 3:4, :].double() + v.double()).float()
+    return bf(v)
+
+
 def seam(res, x, post, comb, pre_prev, hc_fn, hc_scale, hc_base, norm_w, *, fold=True,
          first=False):
     """One hyper-connection boundary (``seam.py:137-378``).
@@ -45,17 +57,7 @@ def seam(res, x, post, comb, pre_prev, hc_fn, hc_scale, hc_base, norm_w, *, fold
     ``seam.py:260-321``); RMSNorm of the layer input (``seam.py:325-378``).
     Returns (res_out, normed, pre, post, comb)."""
     M, _, H = res.shape
-    res, x = f32(res), f32(x)
-    if fold:
-        c = f32(comb)
-        v = f32(post)[:, :, None] * x[:, None, :] + res[:, 0:1, :] * c[:, 0, :, None]
-        v = v + c[:, 1, :, None] * res[:, 1:2, :]
-        v = v + c[:, 2, :, None] * res[:, 2:3, :]
-        # the last term as one fused multiply-add: the exact product plus v, rounded once
-        v = (c[:, 3, :, None].double() * res[:, 3:4, :].double() + v.double()).float()
-        rn = bf(v)
-    else:
-        rn = res.clone()
+    rn = fold_post(res, x, post, comb) if fold else f32(res).clone()
     if first:
         lin = rn[:, 0, :].clone()
     else:
@@ -404,7 +406,7 @@ def moe_partial(normed, w, route_kind, topk, block=128):
 
 
 # ---------------------------------------------------------------- the whole layer over tp ranks
-def decode_layer(ws, S, shape, cache=None):
+def decode_layer(ws, S, shape, cache=None, fold=True, first=False):
     """One decode layer of M rows over ``len(ws)`` TP ranks (``ws[r]``: rank r's weight shards;
     replicated tensors are read from ws[0]), from a step ``S`` (``synth.make_step``'s keys):
     the attention seam, wqkv_a, the q path and KV record (written into ``cache``, a copy of
@@ -418,7 +420,8 @@ def decode_layer(ws, S, shape, cache=None):
     QL, D, nope = shape.q_lora, shape.head_dim, shape.nope
     cache = S["cache"].clone() if cache is None else cache
     rn, normed, pre, post, comb = seam(S["res"].float(), S["x"].float(), S["post"], S["comb"], S["pre"],
-                                       W["hc_attn_fn"], W["hc_attn_scale"], W["hc_attn_base"], W["attn_norm"])
+                                       W["hc_attn_fn"], W["hc_attn_scale"], W["hc_attn_base"], W["attn_norm"],
+                                       fold=fold, first=first)
     x8, x8s = N.mxfp8_quant(normed, "vllm")
     qkv = gemv_x8_fp8(x8, x8s, W["wqkv"], W["wqkv_s"])
     _, qx8, qx8s = q_path(qkv[:, :QL], W["q_norm"])
@@ -434,14 +437,14 @@ def decode_layer(ws, S, shape, cache=None):
         _, x8b, x8bs = wo_a(xo, w["woa"], w["woa_s"], shape.groups_local, shape.o_rank)
         attn_parts.append(wo_b(x8b, x8bs, w["wob"], w["wob_s"]))
     attn = all_reduce(attn_parts)
-    rn2, normed2, *_ = seam(rn, attn, post, comb, pre, W["hc_ffn_fn"], W["hc_ffn_scale"], W["hc_ffn_base"],
-                            W["ffn_norm"])
+    rn2, normed2, pre2, post2, comb2 = seam(rn, attn, post, comb, pre, W["hc_ffn_fn"], W["hc_ffn_scale"],
+                                            W["hc_ffn_base"], W["ffn_norm"])
     moe_parts, ids = [], None
     for w in ws:
         part, ids, _, _ = moe_partial(normed2, w, shape.route, shape.topk)
         moe_parts.append(part)
-    return dict(cache=cache, attn_parts=attn_parts, attn=attn, res2=rn2, normed2=normed2,
-                moe_parts=moe_parts, out=all_reduce(moe_parts), ids=ids)
+    return dict(cache=cache, attn_parts=attn_parts, attn=attn, res2=rn2, normed2=normed2, pre2=pre2,
+                post2=post2, comb2=comb2, moe_parts=moe_parts, out=all_reduce(moe_parts), ids=ids)
 
 
 # ---------------------------------------------------------------- LM head and greedy selection

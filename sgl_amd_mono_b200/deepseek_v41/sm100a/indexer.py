@@ -125,6 +125,12 @@ class K2iRunner:
                          table_stride=0 if table is None else table.stride(0), page=page, owners=_p(owners))
         ext.call("dsv41_topk", a, _stream())
 
+    def identity(self, *, rows, bounds, page_table, raw_out, page_out, owners=None):
+        """Rows that see at most ``topk`` columns: every position in order, -1 padded, and its
+        pool slot (SGLang's topk_transform_paged on such rows)."""
+        owners = self.owners[0] if owners is None else owners
+        self.topk_of(self.ilog, bounds, self.topk, raw_out, page_out=page_out, table=page_table, owners=owners)
+
     def select(self, *, kind, rows, per_req, ratio, query, plane, page_table, bounds, raw_out, page_out,
                candidates=None):
         """An index source's top-k of each row into raw_out / page_out [rows, topk] (positions

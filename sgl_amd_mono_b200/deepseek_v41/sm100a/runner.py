@@ -83,6 +83,8 @@ class MonoRunner:
         self.copies = copies if copies is not None else {}
         self._bufs: dict[int, dict] = {}
         self._scratch: dict[tuple, torch.Tensor] = {}
+        self._pending_zeros: dict[int, dict] = {}
+        self.k2i = None  # an indexer's K2iRunner (a model with index sources)
 
     # ------------------------------------------------------------ weights
     def bind(self, w: dict, tag: str = "layer") -> Layer:
@@ -145,6 +147,16 @@ class MonoRunner:
                     raise RuntimeError(f"peer slots of {self.peers.cap} elements < {M} x {H}")
                 b["gathered"] = z(s.tp, M, H, dt=bf)  # the NCCL variant's all-gather
         return self._bufs[key]
+
+    def zeros_like_pending(self, M: int) -> dict:
+        """Stand-ins for a pending post that is not owed (K1 with fold = 0 reads none of them;
+        with first = 1 it reads no pre)."""
+        if M not in self._pending_zeros:
+            H, d = self.s.hidden, self.dev
+            self._pending_zeros[M] = dict(
+                x=torch.zeros(M, H, dtype=torch.bfloat16, device=d), post=torch.zeros(M, 4, device=d),
+                comb=torch.zeros(M, 4, 4, device=d), pre=torch.zeros(M, 4, device=d))
+        return self._pending_zeros[M]
 
     def _scratch_for(self, kind: str, M: int, need: int) -> torch.Tensor:
         k = (kind, M)
