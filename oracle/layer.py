@@ -406,7 +406,8 @@ def moe_partial(normed, w, route_kind, topk, block=128):
 
 
 # ---------------------------------------------------------------- the whole layer over tp ranks
-def decode_layer(ws, S, shape, cache=None, fold=True, first=False):
+def decode_layer(ws, S, shape, cache=None, fold=True, first=False, topk=None, topk_lens=None, comp=None,
+                 comp_blk=1):
     """One decode layer of M rows over ``len(ws)`` TP ranks (``ws[r]``: rank r's weight shards;
     replicated tensors are read from ws[0]), from a step ``S`` (``synth.make_step``'s keys):
     the attention seam, wqkv_a, the q path and KV record (written into ``cache``, a copy of
@@ -428,12 +429,16 @@ def decode_layer(ws, S, shape, cache=None, fold=True, first=False):
     nb, rb, codes = kv_record(qkv[:, QL:], W["kv_norm"], cosv, sinv, nope)
     data, sc = record_bytes(nb, rb, codes, 8)
     write_records(cache, S["slot"], data, sc, S["blk"])
-    kt, klen = key_table(S["slot"], S["swa_idx"], S["swa_lens"], None, torch.zeros(M, dtype=torch.int32),
-                         S["swa_idx"].shape[1], 0)
+    if topk is None:
+        kt, klen = key_table(S["slot"], S["swa_idx"], S["swa_lens"], None, torch.zeros(M, dtype=torch.int32),
+                             S["swa_idx"].shape[1], 0)
+    else:
+        kt, klen = key_table(S["slot"], S["swa_idx"], S["swa_lens"], topk, topk_lens, S["swa_idx"].shape[1],
+                             topk.shape[1])
     attn_parts = []
     for w in ws:
         q = rope_q(bf(gemv_x8_fp8(qx8, qx8s, w["wqb"], w["wqb_s"])).view(M, -1, D), cosv, sinv, nope)
-        xo = attention(q, kt, klen, cache, S["blk"], None, 1, w["sink"], cosv, sinv, nope, shape.rope, 8)
+        xo = attention(q, kt, klen, cache, S["blk"], comp, comp_blk, w["sink"], cosv, sinv, nope, shape.rope, 8)
         _, x8b, x8bs = wo_a(xo, w["woa"], w["woa_s"], shape.groups_local, shape.o_rank)
         attn_parts.append(wo_b(x8b, x8bs, w["wob"], w["wob_s"]))
     attn = all_reduce(attn_parts)

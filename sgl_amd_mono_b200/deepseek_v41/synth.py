@@ -139,3 +139,40 @@ def make_step(s: LayerShape, M: int, ctx: int, seed: int, device, blk: int = 64)
         swa_idx=slots.contiguous(), swa_lens=torch.full((M,), ctx, dtype=torch.int32, device=device),
         cache=cache, blk=blk, page_stride=page_stride, ctx=ctx,
     )
+
+
+def make_sparse(s: LayerShape, M: int, ctx: int, seed: int, device, index_heads: int = 64, blk: int = 64) -> dict:
+    """BASELINE config 3's compressed side of a decode step, every row its own request with
+    ``ctx`` compressed keys: the compressed KV cache (records of N(0, 1) rows in ``blk``-slot
+    pages scattered by the request's page table), the FP4 index plane on the same page table
+    (N(0, 1) keys of 128 dims as E2M1 + E8M0 per 32, SGLang's split layout), and the rows' FP4
+    index queries (N(0, 1), ``index_heads`` heads) with N(0, 0.05) bf16 head weights."""
+    g = _rng(seed, device)
+    ppr = -(-ctx // blk)
+    pages = M * ppr
+    pt = torch.randperm(pages, generator=g, device=device).to(torch.int32).view(M, ppr).contiguous()
+    data_b = s.record_data
+    page_stride = -(-blk * (data_b + 8) // 16) * 16
+    comp = torch.zeros(pages, page_stride, dtype=torch.uint8, device=device)
+    posn = torch.arange(ctx, device=device)
+    for t in range(M):
+        data, sc = quant.kv_records(torch.randn(ctx, s.head_dim, generator=g, device=device), s.nope)
+        sl = pt[t, posn // blk].long() * blk + posn % blk
+        p, o = sl // blk, sl % blk
+        col = o[:, None] * data_b + torch.arange(data_b, device=device)
+        comp[p[:, None].expand_as(col), col] = data
+        scol = blk * data_b + o[:, None] * 8 + torch.arange(8, device=device)
+        comp[p[:, None].expand_as(scol), scol] = sc
+    packed, codes = quant.quant_mxfp4(torch.randn(pages * blk, 128, generator=g, device=device))
+    payload = packed.view(pages, blk, 4, 16).permute(0, 2, 1, 3).contiguous().view(pages, 1, 4, blk, 16)
+    slot = torch.arange(blk, device=device)
+    kscale = torch.empty(pages, 1, 4, blk, dtype=torch.uint8, device=device)
+    kscale[:, 0, :, (slot % 16) * 4 + slot // 16] = codes.view(pages, blk, 4).permute(0, 2, 1)
+    qp, qc = quant.quant_mxfp4(torch.randn(M * index_heads, 128, generator=g, device=device))
+    qs = torch.zeros(M, 1, 4, 16, 4, dtype=torch.uint8, device=device)
+    h = torch.arange(index_heads, device=device)
+    qs[:, 0, :, h % 16, h // 16] = qc.view(M, index_heads, 4).permute(0, 2, 1)
+    w = (torch.randn(M, index_heads, generator=g, device=device) * 0.05).to(torch.bfloat16)
+    return dict(comp=comp, comp_blk=blk, page_table=pt, payload=payload, kscale=kscale,
+                q=qp.view(M, index_heads, 64).contiguous(), qscale=qs, w=w,
+                bounds=torch.full((M,), ctx, dtype=torch.int32, device=device))
