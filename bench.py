@@ -54,6 +54,7 @@ def parse():
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--skip-configs", action="store_true", help="skip the config-3 / config-5 sections")
     return ap.parse_args()
 
 
@@ -91,7 +92,7 @@ def max_over_ranks(v: float, world: int) -> float:
 
 # ---------------------------------------------------------------- clocks during the timed region
 class Clocks:
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -104,8 +105,23 @@ class Clocks:
                                       stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
+        # nvidia-smi takes a while to start: wait (at most 3 s) for its first sample, so the
+        # samples cover the timed region that follows
+        t0 = time.time()
+        while self.p is not None and time.time() - t0 < 3.0:
+            self.f.flush()
+            if os.path.getsize(self.f.name) > 0:
+                break
+            time.sleep(0.02)
+
+    def mark(self) -> None:
+        """The timed region starts: samples before this are dropped."""
+        import datetime
+        self.t0 = datetime.datetime.now()
 
     def stop(self) -> dict:
+        import datetime
+        t1 = datetime.datetime.now()
         if self.p is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.p.terminate()
@@ -114,13 +130,21 @@ class Clocks:
         except subprocess.TimeoutExpired:
             self.p.kill()
         self.f.flush()
-        rows = []
+        rows, timed = [], []
         with open(self.f.name) as fh:
             for line in fh:
                 parts = [x.strip() for x in line.split(",")]
-                if len(parts) >= 9:
-                    rows.append(parts)
+                if len(parts) >= 10:
+                    rows.append(parts[1:])
+                    try:
+                        ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f")
+                    except ValueError:
+                        continue
+                    if getattr(self, "t0", None) is not None and self.t0 <= ts <= t1:
+                        timed.append(parts[1:])
         os.unlink(self.f.name)
+        window = "timed region" if timed else "whole sampler run (no sample fell inside the timed region)"
+        rows = timed or rows
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
@@ -128,7 +152,7 @@ class Clocks:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "window": window}
 
 
 # ---------------------------------------------------------------- the CPU reference path
@@ -223,7 +247,8 @@ def run_ours(args, world, rank, local):
     peers = PeerBuffer(max(sweep) * shape.hidden, None, rank, world, dev) if tp > 1 else None
     runner = MonoRunner(shape, dev, rank=rank, peers=peers)
     # every rank draws the same full layer and keeps its shard
-    layers = [runner.bind(synth.make_layer(shape, args.seed + 7919 * i, dev, positions=args.ctx + 8, rank=rank),
+    positions = max(args.ctx, 32768) + 8  # config 5's verify rows sit at positions up to 32767
+    layers = [runner.bind(synth.make_layer(shape, args.seed + 7919 * i, dev, positions=positions, rank=rank),
                           tag=f"layer{i}") for i in range(args.layers)]
     stream = torch.cuda.current_stream()
     results, graphs_by_m, steps_by_m, bufs_by_m = {}, {}, {}, {}
@@ -246,13 +271,15 @@ def run_ours(args, world, rank, local):
                 runner.k2(L, st, M, b)
             graphs.append(g)
             bufs.append(b)
+        clocks = Clocks(local if world > 1 else 0) if M == args.rows else None
         for i in range(args.warmup):
             graphs[i % len(graphs)].replay()
         torch.cuda.synchronize()
         barrier(world)
-        clocks = Clocks(local if world > 1 else 0) if M == args.rows else None
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
+        if clocks:
+            clocks.mark()
         e0.record(stream)
         for i in range(args.steps):
             graphs[i % len(graphs)].replay()
@@ -279,6 +306,11 @@ def run_ours(args, world, rank, local):
     ms = results[M]["us_per_layer"] / 1e3
     value = M / (ms * 1e-3)
     runner.check()  # no device-side guard fired during the timed steps
+    other = {}
+    if not args.skip_configs:
+        other["3"] = run_config3(args, runner, layers, world, stream, hbm_peak)
+        other["5"] = run_config5(args, runner, layers, world, rank, stream, hbm_peak)
+        runner.check()
     tp_extra = tp_comparison(args, runner, layers, steps_by_m[M], bufs_by_m[M], M, world, stream) if tp > 1 else None
 
     # ---- stage timelines (eager launches, CUDA events at stage boundaries on the stream)
@@ -364,6 +396,7 @@ def run_ours(args, world, rank, local):
                        "rows": M, "ctx": args.ctx, "tp": tp, "parallelism": f"tp{tp}",
                        "allreduce": "in-kernel peer push, rank-order fp32 sum" if tp > 1 else "none (tp1)",
                        "tp_comparison": tp_extra,
+                       "configs": other,
                        "l2": f"steps alternate {args.layers} layer copies; a step reads "
                              f"{results[M]['algorithmic_MB']} MB (> 126 MB L2)",
                        "layer_roofline": {"GBs": results[M]["GBs"], "frac": results[M]["frac_hbm"],
@@ -387,6 +420,145 @@ def run_ours(args, world, rank, local):
     barrier(world)
     if peers is not None:
         peers.close()
+
+
+def _graph_time(args, fns, world, stream, reps=None):
+    """Capture each callable in a CUDA graph, replay them round-robin after the warm-up, and
+    return the max-over-ranks device time of one replay (ms)."""
+    graphs = []
+    for fn in fns:
+        fn()  # eager: buffers and scratch outside the capture
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        graphs.append(g)
+    for i in range(args.warmup):
+        graphs[i % len(graphs)].replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    reps = reps or args.steps
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(reps):
+        graphs[i % len(graphs)].replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / reps, world)
+    del graphs
+    return ms
+
+
+def run_config3(args, runner, layers, world, stream, hbm_peak):
+    """the indexer layer -- K2i over 16 rows' FP4 index keys of a 32768-token
+    compressed context (64 index heads), the top-2048, then K1 + K2 with the SWA window (128
+    keys) and the 2048 selected compressed keys. Timed as one CUDA graph (K2i's walk plan,
+    scoring and top-k, K1, K2), and K2i alone; two copies of the step's data alternate."""
+    from sgl_amd_mono_b200.deepseek_v41 import roofline, synth
+    from sgl_amd_mono_b200.deepseek_v41.sm100a.indexer import K2iRunner
+
+    M, ctx, topk, window, heads = 16, 32768, 2048, 128, 64
+    s, dev = runner.s, runner.dev
+    k2i = K2iRunner(dev, ctx, topk=topk)
+    copies = []
+    for i in range(2):
+        st = synth.make_step(s, M, window, args.seed + 300 + i, dev)
+        sp = synth.make_sparse(s, M, ctx, args.seed + 310 + i, dev, index_heads=heads)
+        raw = torch.empty(M, topk, dtype=torch.int32, device=dev)
+        page = torch.empty_like(raw)
+        lens = torch.clamp(sp["bounds"], max=topk).to(torch.int32)
+        copies.append((st, sp, raw, page, lens))
+
+    def select(c):
+        st, sp, raw, page, lens = c
+        k2i.walk_plan(ratio=1, bounds=sp["bounds"], rows=M, per_req=1)
+        k2i.select(kind="full", rows=M, per_req=1, ratio=1, query=(sp["q"], sp["qscale"], sp["w"]),
+                   plane=(sp["payload"], sp["kscale"]), page_table=sp["page_table"], bounds=sp["bounds"],
+                   raw_out=raw, page_out=page)
+
+    def layer(i):
+        c = copies[i]
+        st, sp, raw, page, lens = c
+        L = layers[i % len(layers)]
+        select(c)
+        b = runner.k1(L, st, M, topk_width=topk, topk_idx=page, topk_lens=lens)
+        runner.k2(L, st, M, b, comp=sp["comp"], comp_stride=sp["comp"].stride(0), comp_blk=sp["comp_blk"])
+        return b
+
+    ms_sel = _graph_time(args, [lambda c=c: select(c) for c in copies], world, stream)
+    ms_layer = _graph_time(args, [lambda i=i: layer(i) for i in range(2)], world, stream)
+    b = layer(0)
+    torch.cuda.synchronize()
+    union = int(torch.unique(b["ids"][:M]).numel())
+    keys = int(b["klen"][:M].sum().item())
+    index_bytes = M * ctx * 68  # 64 B of E2M1 + 4 E8M0 codes a key
+    lb = roofline.layer_bytes(s, union, keys)["total"] + index_bytes
+    return {"workload": f"config3: K2i (64 heads, ctx {ctx}) -> top-{topk} -> K1 + K2 (window {window} + "
+                        f"{topk} compressed keys), {M} rows, tp{runner.s.tp}",
+            "rows": M, "us_per_layer": round(ms_layer * 1e3, 2), "tokens_s": round(M / (ms_layer * 1e-3), 1),
+            "k2i_select_us": round(ms_sel * 1e3, 2),
+            "k2i_index_GBs": round(index_bytes / (ms_sel * 1e-3) / 1e9, 1),
+            "k2i_frac_hbm": round(index_bytes / (ms_sel * 1e-3) / 1e9 / hbm_peak, 4),
+            "algorithmic_MB": round(lb / 1e6, 1), "frac_hbm": round(lb / (ms_layer * 1e-3) / 1e9 / hbm_peak, 4),
+            "union": union}
+
+
+def run_config5(args, runner, layers, world, rank, stream, hbm_peak):
+    """a speculative-verify step's pieces -- 48 verify rows (8 requests x 6,
+    row j of a block seeing its causal prefix of a 32768-token context) through one target
+    layer and the one-layer draft (config-2 shapes, their own weights), then the LM head
+    (129280 x 4096 bf16, vocab-parallel over the ranks) with the fused argmax and the greedy
+    acceptance of each block. Each piece is CUDA-graph timed; the step line sums one target
+    layer, the draft and the head."""
+    import torch.distributed as dist
+
+    from sgl_amd_mono_b200.common import ext
+    from sgl_amd_mono_b200.deepseek_v41 import synth
+    from sgl_amd_mono_b200.deepseek_v41.sm100a import abi
+
+    M, P, ctx, V = 48, 6, 32768, 129280
+    s, dev = runner.s, runner.dev
+    steps = [synth.make_step(s, M, ctx, args.seed + 500 + i, dev, per_req=P) for i in range(2)]
+
+    def layer(i):
+        L, st = layers[i % len(layers)], steps[i]
+        b = runner.k1(L, st, M)
+        runner.k2(L, st, M, b)
+
+    ms_layer = _graph_time(args, [lambda i=i: layer(i) for i in range(2)], world, stream, reps=20)
+    vl = V // world
+    g = torch.Generator(device=dev).manual_seed(args.seed + 600)
+    heads = [(torch.randn(vl, s.hidden, generator=g, device=dev) * 0.02).to(torch.bfloat16) for _ in range(2)]
+    x = torch.randn(M, s.hidden, generator=g, device=dev).to(torch.bfloat16)
+    best = torch.empty(M, dtype=torch.int64, device=dev)
+    ids = torch.empty(M, dtype=torch.int32, device=dev)
+    draft_tok = torch.randint(0, V, (M,), generator=g, device=dev, dtype=torch.int32)
+    acc = torch.empty(M // P, dtype=torch.int32, device=dev)
+    nxt = torch.empty_like(acc)
+
+    def head(i):
+        a = abi.LmHeadArgs(M=M, V=vl, K=s.hidden, vbase=rank * vl, w=heads[i].data_ptr(), x=x.data_ptr(), logits=0,
+                           best=best.data_ptr(), init=1)
+        cur = torch.cuda.current_stream().cuda_stream  # the capturing stream under graph capture
+        ext.call("dsv41_lmhead_argmax", a, cur)
+        if world > 1:
+            dist.all_reduce(best, op=dist.ReduceOp.MAX)
+        d = abi.ArgmaxArgs(M=M, best=best.data_ptr(), ids=ids.data_ptr(), vals=0, draft=draft_tok.data_ptr(),
+                           per_req=P, accept=acc.data_ptr(), next_tok=nxt.data_ptr())
+        ext.call("dsv41_argmax_decode", d, cur)
+
+    ms_head = _graph_time(args, [lambda i=i: head(i) for i in range(2)], world, stream)
+    head_bytes = vl * s.hidden * 2
+    step_ms = 2 * ms_layer + ms_head  # one target layer + the one-layer draft + the head
+    return {"workload": f"config5: verify step pieces, {M} rows (8 x {P}), ctx {ctx} causal blocks, "
+                        f"LM head {V} x {s.hidden} bf16, tp{runner.s.tp}",
+            "rows": M, "layer_us": round(ms_layer * 1e3, 2), "draft_us": round(ms_layer * 1e3, 2),
+            "lm_head_argmax_accept_us": round(ms_head * 1e3, 2),
+            "lm_head_GBs": round(head_bytes / (ms_head * 1e-3) / 1e9, 1),
+            "lm_head_frac_hbm": round(head_bytes / (ms_head * 1e-3) / 1e9 / hbm_peak, 4),
+            "step_us_target_layer_draft_head": round(step_ms * 1e3, 2),
+            "note": "the draft layer has the target layer's shapes and cost (config 5's 1-layer draft); "
+                    "a 40-layer target adds 39 more layer_us"}
 
 
 def tp_comparison(args, runner, layers, steps, bufs, M, world, stream):

@@ -80,7 +80,7 @@ typedef struct {
   int64_t res_in, x_in, post_in, comb_in, pre_in, hc_fn, hc_scale, hc_base, norm_w;
   int64_t res_out, post_out, comb_out, pre_out, normed, x8, x8s;
   /* projections, norms, positions */
-  int64_t wqkv, wqkv_codes, q_norm, kv_norm, cos_sin, pos;
+  int64_t wqkv, wqkv_codes, q_norm, kv_norm, cos_sin, pos, rope_rows;
   /* KV store */
   int64_t slot, cache, page_stride, blk;
   /* key table */
@@ -116,7 +116,7 @@ typedef struct {
   int64_t M, hidden, nope, rope, heads, o_groups, o_rank;
   int64_t experts, topk, inter, shared_inter, route_softmax, tp, rank, keys_ld;
   /* attention */
-  int64_t q, kt, klen, swa, swa_stride, swa_blk, comp, comp_stride, comp_blk, sink, cos_sin, pos;
+  int64_t q, kt, klen, swa, swa_stride, swa_blk, comp, comp_stride, comp_blk, sink, cos_sin, pos, rope_rows;
   int64_t woa, woa_codes, wob, wob_codes;
   /* FFN seam */
   int64_t res_in, post_in, comb_in, pre_in, hc_fn, hc_scale, hc_base, norm_w;

@@ -16,7 +16,7 @@ K1Args = struct("Dsv41K1Args", [
     "fold", "first", "index", "build_kt",
     "res_in", "x_in", "post_in", "comb_in", "pre_in", "hc_fn", "hc_scale", "hc_base", "norm_w",
     "res_out", "post_out", "comb_out", "pre_out", "normed", "x8", "x8s",
-    "wqkv", "wqkv_codes", "q_norm", "kv_norm", "cos_sin", "pos",
+    "wqkv", "wqkv_codes", "q_norm", "kv_norm", "cos_sin", "pos", "rope_rows",
     "slot", "cache", "page_stride", "blk",
     "swa_idx", "swa_lens", "topk_idx", "topk_lens", "kt", "klen",
     "wqb", "wqb_codes", "q", "qr", "qx8", "qx8s", "qkv_out", "events",
@@ -28,7 +28,7 @@ K2Args = struct("Dsv41K2Args", [
     "M", "hidden", "nope", "rope", "heads", "o_groups", "o_rank",
     "experts", "topk", "inter", "shared_inter", "route_softmax", "tp", "rank", "keys_ld",
     "q", "kt", "klen", "swa", "swa_stride", "swa_blk", "comp", "comp_stride", "comp_blk", "sink",
-    "cos_sin", "pos",
+    "cos_sin", "pos", "rope_rows",
     "woa", "woa_codes", "wob", "wob_codes",
     "res_in", "post_in", "comb_in", "pre_in", "hc_fn", "hc_scale", "hc_base", "norm_w",
     "res_out", "post_out", "comb_out", "pre_out", "normed",

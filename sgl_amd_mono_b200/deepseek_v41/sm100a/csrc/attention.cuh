@@ -342,6 +342,7 @@ struct CombineArgs {
   const float* sink;       // [heads] (this rank's)
   const float* cos_sin;    // [positions, rope]
   const int64_t* pos;      // [M]
+  int64_t rope_rows;       // the table's positions (0: unchecked)
   __nv_bfloat16* xo;       // [M, heads * D]
 };
 
@@ -357,7 +358,7 @@ __global__ void attn_combine_kernel(const CombineArgs a) {
     if (ml[0] != -INFINITY) l += ml[1] * exp2f(ml[0] - m);
   }
   const float inv = 1.0f / l;
-  const int64_t p = a.pos[t];
+  const int64_t p = rope_row(a.pos[t], a.rope_rows);
   for (int d2 = threadIdx.x; d2 < a.D / 2; d2 += blockDim.x) {
     const int d = 2 * d2;
     float v0 = 0.f, v1 = 0.f;

@@ -226,7 +226,7 @@ int k1_run(const Dsv41K1Args* a, cudaStream_t st, bool go, int64_t* need) {
   f.M = M; f.QL = QL; f.KVD = D; f.nope = nope; f.rope = rope; f.kslices = g1.kslices;
   f.index = (int)a->index; f.qkv_part = g1.out;
   f.q_norm_w = ptr<const __nv_bfloat16>(a->q_norm); f.kv_norm_w = ptr<const __nv_bfloat16>(a->kv_norm);
-  f.cos_sin = ptr<const float>(a->cos_sin); f.pos = ptr<const int64_t>(a->pos);
+  f.cos_sin = ptr<const float>(a->cos_sin); f.pos = ptr<const int64_t>(a->pos); f.rope_rows = a->rope_rows;
   f.slot = ptr<const int64_t>(a->slot); f.cache = ptr<uint8_t>(a->cache);
   f.page_stride = a->page_stride; f.blk = (int)a->blk;
   f.qr = ptr<__nv_bfloat16>(a->qr); f.qx8 = qx8; f.qx8s = qx8s; f.qxq = qxq;
@@ -248,6 +248,7 @@ int k1_run(const Dsv41K1Args* a, cudaStream_t st, bool go, int64_t* need) {
   QRopeArgs qr = {};
   qr.M = M; qr.heads = heads; qr.D = D; qr.nope = nope; qr.rope = rope; qr.kslices = g2.kslices;
   qr.part = g2.out; qr.cos_sin = ptr<const float>(a->cos_sin); qr.pos = ptr<const int64_t>(a->pos);
+  qr.rope_rows = a->rope_rows;
   qr.q = ptr<__nv_bfloat16>(a->q);
   DSV41_TRY(launch(q_rope_kernel, dim3(cdiv(heads * D / 2, 256), M), dim3(256), 0, st, qr));
   mark(a->events, 4, st);
@@ -393,6 +394,7 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   cb.M = M; cb.heads = heads; cb.D = D; cb.nope = nope; cb.rope = rope; cb.nchunks = nchunks;
   cb.part_o = part_o; cb.part_ml = part_ml; cb.sink = ptr<const float>(a->sink);
   cb.cos_sin = ptr<const float>(a->cos_sin); cb.pos = ptr<const int64_t>(a->pos); cb.xo = xo;
+  cb.rope_rows = a->rope_rows;
   DSV41_TRY(launch(attn_combine_kernel, dim3(M * heads), dim3(128), 0, st, cb));
   // ---- wo_a -> X8B -> wo_b -> partial -> reduce
   mark(a->events, 1, st);

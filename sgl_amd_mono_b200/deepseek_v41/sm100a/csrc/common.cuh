@@ -215,6 +215,12 @@ __device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.laun
 
 __host__ __device__ __forceinline__ int cdiv(int a, int b) { return (a + b - 1) / b; }
 
+// A RoPE table row for position p: clamped into the table's rows (rows = 0: unchecked), so a
+// position past the table reads its last row instead of memory past it.
+__device__ __forceinline__ int64_t rope_row(int64_t p, int64_t rows) {
+  return rows > 0 ? min(max(p, (int64_t)0), rows - 1) : p;
+}
+
 // Raise a kernel's dynamic shared-memory limit once per (kernel, device) -- not on every
 // launch, so launches captured into a CUDA graph make no attribute calls after the first.
 cudaError_t ensure_smem(const void* kernel, int bytes);

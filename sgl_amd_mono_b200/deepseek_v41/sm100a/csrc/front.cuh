@@ -15,6 +15,7 @@ struct FrontArgs {
   const __nv_bfloat16* kv_norm_w;  // [KVD]
   const float* cos_sin;        // [positions, rope]: rope/2 cos, then rope/2 sin
   const int64_t* pos;          // [M]
+  int64_t rope_rows;           // the table's positions (0: unchecked)
   const int64_t* slot;         // [M] KV slot (< 0: a pad row, nothing stored)
   uint8_t* cache;              // paged KV cache
   int64_t page_stride;         // bytes a page
@@ -106,7 +107,7 @@ __global__ void __launch_bounds__(256) front_qkv_kernel(const FrontArgs a) {
     for (int q = 0; q < R; ++q) e[q] = __fmul_rn(__fmul_rn(xk[q], r), bf2f(a.kv_norm_w[tid + 64 * q]));
     // GPT-J RoPE of the dims past nope: pair (2j, 2j + 1) sits on threads 2j, 2j + 1 (r = R - 1)
     const int half = a.rope / 2;
-    const int64_t p = a.pos[t];
+    const int64_t p = rope_row(a.pos[t], a.rope_rows);
     for (int q = 0; q < R; ++q) {
       const int d = tid + 64 * q;
       if (d >= a.nope) {
@@ -154,6 +155,7 @@ struct QRopeArgs {
   const float* part;       // [kslices][M][heads * D]
   const float* cos_sin;    // [positions, rope]
   const int64_t* pos;      // [M]
+  int64_t rope_rows;       // the table's positions (0: unchecked)
   __nv_bfloat16* q;        // [M, heads, D]
 };
 
@@ -174,7 +176,7 @@ __global__ void q_rope_kernel(const QRopeArgs a) {
     const int d = n % a.D;
     if (d >= a.nope) {
       const int j = (d - a.nope) >> 1;
-      const int64_t p = a.pos[t];
+      const int64_t p = rope_row(a.pos[t], a.rope_rows);
       const float c = a.cos_sin[p * a.rope + j], s = a.cos_sin[p * a.rope + a.rope / 2 + j];
       const float e0 = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, s));
       const float e1 = __fadd_rn(__fmul_rn(v0, s), __fmul_rn(v1, c));

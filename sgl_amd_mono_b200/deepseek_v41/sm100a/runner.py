@@ -183,7 +183,7 @@ class MonoRunner:
             res_out=_p(b["res1"]), post_out=_p(b["post_a"]), comb_out=_p(b["comb_a"]), pre_out=_p(b["pre_a"]),
             normed=_p(b["normed_a"]), x8=_p(b["x8"]), x8s=_p(b["x8s"]),
             wqkv=_p(w["wqkv"]), wqkv_codes=_p(w["wqkv_s"]), q_norm=_p(w["q_norm"]), kv_norm=_p(w["kv_norm"]),
-            cos_sin=_p(w["cos_sin"]), pos=_p(step["pos"]),
+            cos_sin=_p(w["cos_sin"]), pos=_p(step["pos"]), rope_rows=w["cos_sin"].shape[0],
             slot=_p(step["slot"]), cache=_p(step["cache"]), page_stride=step["page_stride"], blk=step["blk"],
             swa_idx=_p(step["swa_idx"]), swa_lens=_p(step["swa_lens"]), topk_idx=_p(topk_idx),
             topk_lens=_p(topk_lens), kt=_p(b["kt"]), klen=_p(b["klen"]),
@@ -215,6 +215,7 @@ class MonoRunner:
             q=_p(b["q"]), kt=_p(b["kt"]), klen=_p(b["klen"]), swa=_p(step["cache"]),
             swa_stride=step["page_stride"], swa_blk=step["blk"], comp=_p(comp), comp_stride=comp_stride,
             comp_blk=comp_blk, sink=_p(w["sink"]), cos_sin=_p(w["cos_sin"]), pos=_p(step["pos"]),
+            rope_rows=w["cos_sin"].shape[0],
             woa=_p(w["woa"]), woa_codes=_p(w["woa_s"]), wob=_p(w["wob"]), wob_codes=_p(w["wob_s"]),
             res_in=_p(b["res1"]), post_in=_p(b["post_a"]), comb_in=_p(b["comb_a"]), pre_in=_p(b["pre_a"]),
             hc_fn=_p(w["hc_ffn_fn"]), hc_scale=_p(w["hc_ffn_scale"]), hc_base=_p(w["hc_ffn_base"]),

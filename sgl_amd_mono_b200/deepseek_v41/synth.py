@@ -98,10 +98,14 @@ def _cols(q, codes, c0, n):
     return q[:, c0:c0 + n].contiguous(), codes[:, c0 // 128:(c0 + n) // 128].contiguous()
 
 
-def make_step(s: LayerShape, M: int, ctx: int, seed: int, device, blk: int = 64) -> dict:
+def make_step(s: LayerShape, M: int, ctx: int, seed: int, device, blk: int = 64, per_req: int = 1) -> dict:
     """A decode step of M rows, each its own request with ``ctx`` keys (the row's own token
     last), over a paged SWA-layout cache of ``blk``-slot pages scattered by a page table.
-    The key table is the rows' window of ``ctx`` slots (K1 builds it)."""
+    The key table is the rows' window of ``ctx`` slots (K1 builds it). With ``per_req`` > 1,
+    rows come in verify blocks: the per_req rows of a request share its cache and row j of the
+    block sees the causal prefix ending at its own token, ctx - per_req + j + 1 keys."""
+    if per_req > 1:
+        return _make_verify_step(s, M, ctx, seed, device, blk, per_req)
     g = _rng(seed, device)
     H = s.hidden
     res = torch.randn(M, HC, H, generator=g, device=device)
@@ -138,6 +142,46 @@ def make_step(s: LayerShape, M: int, ctx: int, seed: int, device, blk: int = 64)
         slot=slots[:, ctx - 1].long().contiguous(),
         swa_idx=slots.contiguous(), swa_lens=torch.full((M,), ctx, dtype=torch.int32, device=device),
         cache=cache, blk=blk, page_stride=page_stride, ctx=ctx,
+    )
+
+
+def _make_verify_step(s: LayerShape, M: int, ctx: int, seed: int, device, blk: int, per_req: int) -> dict:
+    g = _rng(seed, device)
+    H, R = s.hidden, M // per_req
+    assert M % per_req == 0 and ctx >= per_req
+    res = torch.randn(M, HC, H, generator=g, device=device)
+    res = (res * torch.rsqrt(res.pow(2).mean(-1, keepdim=True))).to(torch.bfloat16)
+    x = torch.randn(M, H, generator=g, device=device).to(torch.bfloat16)
+    comb = torch.rand(M, HC, HC, generator=g, device=device) + 0.1
+    for _ in range(20):
+        comb = comb / comb.sum(-1, keepdim=True)
+        comb = comb / comb.sum(-2, keepdim=True)
+    post = torch.sigmoid(torch.randn(M, HC, generator=g, device=device)) * 2
+    pre = torch.sigmoid(torch.randn(M, HC, generator=g, device=device)) + 1e-6
+    ppr = -(-ctx // blk)
+    page_table = torch.randperm(R * ppr, generator=g, device=device).view(R, ppr)
+    posn = torch.arange(ctx, device=device)
+    req_slots = (page_table[:, posn // blk] * blk + posn % blk).to(torch.int32)  # [R, ctx]
+    slots = req_slots.repeat_interleave(per_req, 0)  # [M, ctx]
+    j = torch.arange(M, device=device) % per_req
+    lens = (ctx - per_req + j + 1).to(torch.int32)
+    data_b = s.record_data
+    page_stride = -(-blk * (data_b + 8) // 16) * 16
+    cache = torch.zeros(R * ppr, page_stride, dtype=torch.uint8, device=device)
+    # prefill every key before the block (K1 writes the block's own)
+    for r in range(R):
+        data, sc = quant.kv_records(torch.randn(ctx - per_req, s.head_dim, generator=g, device=device), s.nope)
+        sl = req_slots[r, : ctx - per_req].long()
+        p, o = sl // blk, sl % blk
+        col = o[:, None] * data_b + torch.arange(data_b, device=device)
+        cache[p[:, None].expand_as(col), col] = data
+        scol = blk * data_b + o[:, None] * 8 + torch.arange(8, device=device)
+        cache[p[:, None].expand_as(scol), scol] = sc
+    pos = (lens - 1).long()
+    return dict(
+        res=res, x=x.contiguous(), post=post.contiguous(), comb=comb.contiguous(), pre=pre.contiguous(),
+        pos=pos, slot=slots.gather(1, pos[:, None])[:, 0].long().contiguous(),
+        swa_idx=slots.contiguous(), swa_lens=lens, cache=cache, blk=blk, page_stride=page_stride, ctx=ctx,
     )
 
 

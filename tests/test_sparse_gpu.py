@@ -64,3 +64,27 @@ def test_k2i_topk_sparse_attention_layer(M, ctx, topk):
     _close(b["attn"], ref["attn"])
     _close(b["out"], ref["out"])
     assert torch.equal(b["ids"].cpu(), ref["ids"])
+
+
+def test_verify_blocks_causal_layer():
+    """BASELINE config 5's rows: verify blocks of 6 rows a request sharing its cache, row j
+    seeing the causal prefix up to its own token (written by the same K1 launch)."""
+    from sgl_amd_mono_b200.deepseek_v41 import synth
+    from sgl_amd_mono_b200.deepseek_v41.shapes import LayerShape
+    from sgl_amd_mono_b200.deepseek_v41.sm100a.runner import MonoRunner
+    s = LayerShape(**SMALL)
+    M, P, ctx = 12, 6, 700
+    w = synth.make_layer(s, 81, "cpu", positions=ctx + 8)
+    S = synth.make_step(s, M, ctx, 82, "cpu", per_req=P)
+    gpu = lambda d: {k: (v.to(DEV) if torch.is_tensor(v) else v) for k, v in d.items()}  # noqa: E731
+    Sd = gpu(S)
+    runner = MonoRunner(s, DEV)
+    L = runner.bind(gpu(w))
+    b = runner.k1(L, Sd, M)
+    runner.k2(L, Sd, M, b)
+    torch.cuda.synchronize()
+    ref = OL.decode_layer([w], S, s)
+    assert torch.equal(Sd["cache"].cpu(), ref["cache"])
+    assert b["klen"][:M].tolist() == S["swa_lens"].tolist()
+    _close(b["attn"], ref["attn"])
+    _close(b["out"], ref["out"])
