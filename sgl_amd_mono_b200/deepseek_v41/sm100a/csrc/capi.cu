@@ -14,6 +14,7 @@
 
 #include "../../../../include/dsv41_b200.h"
 #include "attention.cuh"
+#include "attn_tc.cuh"
 #include "common.cuh"
 #include "epilogue.cuh"
 #include "front.cuh"
@@ -53,6 +54,16 @@ int sm_count() {
     cached[dev] = n;
   }
   return cached[dev];
+}
+
+// The attention core: tcgen05 (default) or the mma.sync split kernel (DSV41_ATTN=mma).
+bool use_tc_attention() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("DSV41_ATTN");
+    v = (e && e[0] == 'm') ? 0 : 1;
+  }
+  return v == 1;
 }
 
 bool use_pdl() {
@@ -306,9 +317,12 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   const int P = M * TK, keys = (int)a->keys_ld;
   const int sms = sm_count();
   Carver c{go ? ptr<uint8_t>(a->scratch) : nullptr};
-  // attention split plan
-  const int head_tiles = cdiv(heads, 16);
-  int nchunks = cdiv(2 * sms, M * head_tiles);
+  // attention split plan: the tcgen05 kernel takes every head of a row (one CTA an SM in
+  // total), the mma.sync kernel 16-head tiles (two CTAs an SM)
+  const bool tc = use_tc_attention() && (nope == 512 || nope == 448);
+  const int head_tiles = tc ? cdiv(heads, 32) : cdiv(heads, 16);
+  const int units = M * head_tiles;
+  int nchunks = tc ? std::max(1, (sms + units / 2) / units) : cdiv(2 * sms, units);
   nchunks = std::max(1, std::min(nchunks, cdiv(keys, kSub)));
   const int chunk_keys = cdiv(cdiv(keys, nchunks), kSub) * kSub;
   nchunks = cdiv(keys, chunk_keys);
@@ -389,7 +403,17 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   at.scale_log2 = (float)(1.0 / sqrt((double)D) * 1.4426950408889634);
   at.part_o = part_o; at.part_ml = part_ml;
   mark(a->events, 0, st);
-  DSV41_TRY(launch(attn_split_kernel, dim3(M * nchunks * head_tiles), dim3(256), attn_smem_bytes(D), st, at));
+  if (tc) {
+    AttnTcArgs ta = {at, heads >= 32 ? 32 : std::max(16, cdiv(heads, 16) * 16), head_tiles};
+    if (nope == 512)
+      DSV41_TRY(launch(attn_tc_kernel<512>, dim3(M * nchunks * head_tiles), dim3(kTcThreads), TcSmem<576>::kBytes,
+                       st, ta));
+    else
+      DSV41_TRY(launch(attn_tc_kernel<448>, dim3(M * nchunks * head_tiles), dim3(kTcThreads), TcSmem<512>::kBytes,
+                       st, ta));
+  } else {
+    DSV41_TRY(launch(attn_split_kernel, dim3(M * nchunks * head_tiles), dim3(256), attn_smem_bytes(D), st, at));
+  }
   CombineArgs cb = {};
   cb.M = M; cb.heads = heads; cb.D = D; cb.nope = nope; cb.rope = rope; cb.nchunks = nchunks;
   cb.part_o = part_o; cb.part_ml = part_ml; cb.sink = ptr<const float>(a->sink);
@@ -475,6 +499,12 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
 extern "C" {
 
 int64_t dsv41_launch_count(void) { return g_launches.load(); }
+
+int dsv41_device_error(void) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, dsv41::g_tc_error, sizeof(v)) != cudaSuccess) return launch_status();
+  return v ? DSV41_EDEVICE : DSV41_OK;
+}
 
 int dsv41_version(void) { return 1; }
 int dsv41_arch(void) { return 100; }

@@ -6,7 +6,15 @@ floating-point outputs within the reference's bounds (``deepseek_v41/spec.py:287
 the reference: k1.q.cosine 0.99999, k1.q.rel 5e-3, k2.attn_out.cosine 0.9998, k2.wo_a.rel
 5e-3, k2.wo_b.rel 1e-3, ffn.moe.cosine 0.9999, ffn.moe.rel 0.015, ffn.mix.rel 1e-4). The
 whole layer is then checked end to end: every element within 2e-2 x RMS(oracle) plus one
-bf16 rounding step of the oracle's element (``e2e_excess``), and rel-norm error below 1e-2.
+bf16 rounding step of the oracle's element (``e2e_excess``) once the oracle continues from
+the GPU's own attention output, and, from the oracle's own attention, rel-norm error within
+the reference's ffn.moe.rel bound (1.5e-2). Why the split: the attention output is bf16 and
+is requantized to MXFP8 (wo_a's input) and again before the experts; an attention that agrees
+with the exact oracle to ~1e-6 still lands a handful of its 10^4-10^5 bf16 outputs one step
+apart (any kernel but a bit-identical one does), each such step can flip an e4m3 code of the
+requantized activation, and one flipped code moves its row's MoE output by several percent of
+the RMS. Element-wise bounds therefore hold from the same attention output, and the exact
+attention is bounded separately (rel 1e-3, cos >= 0.9998, the reference's k2.attn_out bound).
 """
 
 import pytest
@@ -159,14 +167,33 @@ def test_layer_end_to_end(shape_kw, M, ctx):
     kt, klen = OL.key_table(S["slot"], S["swa_idx"], S["swa_lens"], None, torch.zeros(M, dtype=torch.int32),
                             S["swa_idx"].shape[1], 0)
     xo = OL.attention(q, kt, klen, cache, S["blk"], None, 1, W["sink"], cosv, sinv, nope, s.rope, 8)
-    _, x8b, x8bs = OL.wo_a(xo, W["woa"], W["woa_s"], s.groups_local, s.o_rank)
-    attn = OL.all_reduce([OL.wo_b(x8b, x8bs, W["wob"], W["wob_s"])])
-    rn2, normed2, *_ = OL.seam(rn, attn, post, comb, pre, W["hc_ffn_fn"], W["hc_ffn_scale"],
-                               W["hc_ffn_base"], W["ffn_norm"])
-    out, ids, _, _ = OL.moe_partial(normed2, W, s.route, s.topk)
+    # the step's KV records are the oracle's; the attention of the GPU's own q against the exact
+    # oracle attention of that q (q itself sums wq_b in another order: the reference's 5e-3)
+    assert torch.equal(step["cache"].cpu(), cache)
+    assert rel(b["q"].cpu().float(), q) < 5e-3
+    gx = b["xo"].cpu().float()
+    xo_g = OL.attention(b["q"].cpu().float(), kt, klen, cache, S["blk"], None, 1, W["sink"], cosv, sinv, nope,
+                        s.rope, 8)
+    assert rel(gx, xo_g) < 1e-3 and cos(gx, xo_g) >= 0.9998, (rel(gx, xo_g), cos(gx, xo_g))
+
+    def rest(xo_in):
+        _, x8b, x8bs = OL.wo_a(xo_in, W["woa"], W["woa_s"], s.groups_local, s.o_rank)
+        attn = OL.all_reduce([OL.wo_b(x8b, x8bs, W["wob"], W["wob_s"])])
+        rn2, normed2, *_ = OL.seam(rn, attn, post, comb, pre, W["hc_ffn_fn"], W["hc_ffn_scale"],
+                                   W["hc_ffn_base"], W["ffn_norm"])
+        out, ids, _, _ = OL.moe_partial(normed2, W, s.route, s.topk)
+        return out, rn2, ids
+
+    # element-wise: the oracle continued from the GPU's attention output
+    out, rn2, ids = rest(gx)
+    assert torch.equal(b["ids"].cpu(), ids)
     for got, ref in ((b["out"].float().cpu(), out), (b["res2"].float().cpu(), rn2)):
         excess, rms = e2e_excess(got, ref)
         assert excess <= 2e-2 * rms, (excess, rms)
         assert rel(got, ref) < 1e-2
-    same = (b["ids"].cpu().sort(1).values == ids.sort(1).values).all(1).float().mean().item()
+    # the whole layer against the oracle's own attention: the reference's MoE bound
+    out_x, rn2_x, ids_x = rest(xo)
+    for got, ref in ((b["out"].float().cpu(), out_x), (b["res2"].float().cpu(), rn2_x)):
+        assert rel(got, ref) < 1.5e-2, rel(got, ref)
+    same = (b["ids"].cpu().sort(1).values == ids_x.sort(1).values).all(1).float().mean().item()
     assert same >= 0.9

@@ -1,8 +1,10 @@
 """BASELINE config 3's pipeline on the GPU (at test size): K2i scores every row's compressed
 keys from the FP4 index plane, the top-2048 (ties to the lower position) become the pool slots
 K1 writes into K2's key table beside the SWA window, and K2 attends over both caches. Against
-the oracle: the selection bit-exact, the step's KV record bytes exact, the attention output and
-the layer output within the layer tolerance (2e-2 x RMS + one bf16 step)."""
+the oracle: the selection bit-exact, the step's KV record bytes exact, the reduced attention
+output within 2e-2 x RMS + one bf16 step element-wise, and the MoE output within the reference's
+ffn.moe.rel bound (1.5e-2) with identical routing (element-wise bounds stop at the MXFP8
+requantization of the attention's bf16 output, where a one-step difference flips e4m3 codes)."""
 
 import pytest
 import torch
@@ -14,6 +16,11 @@ pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0)
 SMALL = dict(hidden=1024, heads=8, nope=512, rope=64, q_lora=256, o_groups=1, o_rank=1024, experts=16, topk=4,
              inter=512, shared_inter=512)
+
+
+def _rel(got, ref, tol):
+    got, ref = got.float().cpu(), ref.float()
+    assert (got - ref).norm() / ref.norm() < tol
 
 
 def _close(got, ref, tol=2e-2):
@@ -62,7 +69,7 @@ def test_k2i_topk_sparse_attention_layer(M, ctx, topk):
     assert torch.equal(Sd["cache"].cpu(), ref["cache"])
     assert int(b["klen"][:M].sum()) == int((lens + 128).sum())
     _close(b["attn"], ref["attn"])
-    _close(b["out"], ref["out"])
+    _rel(b["out"], ref["out"], 1.5e-2)
     assert torch.equal(b["ids"].cpu(), ref["ids"])
 
 
@@ -87,4 +94,4 @@ def test_verify_blocks_causal_layer():
     assert torch.equal(Sd["cache"].cpu(), ref["cache"])
     assert b["klen"][:M].tolist() == S["swa_lens"].tolist()
     _close(b["attn"], ref["attn"])
-    _close(b["out"], ref["out"])
+    _rel(b["out"], ref["out"], 1.5e-2)
