@@ -5,7 +5,8 @@
 //   warps 0-3  softmax + epilogue (each owns the TMEM lane quarter of its warp index),
 //   warp  4    TMEM allocation and the MMA issue (one elected thread),
 //   warps 5-11 producers: 64-key sub-blocks of FP8 records -> an f16 tile in shared memory.
-// Per sub-block j (tile buffer j & 1, S buffer j & 1):
+// Per sub-block j (tile, P and O_sub buffers j & 1; one S buffer, released as soon as the
+// softmax threads hold it in registers):
 //   S^T[64 keys x NH heads]  = K_tile . Q^T      tcgen05.mma M=64 (keys), N=NH, K=D: A = the tile
 //                                                (K-major), B = Q (K-major), D in TMEM;
 //   softmax over keys (the threads holding keys 16 w + lane, lane < 16, of warp w) with the
@@ -13,19 +14,20 @@
 //   O_sub^T[D dims x NH heads] = V_tile^T . P^T  M=128 (dims, in 128-dim blocks), N=NH, K=64
 //                                                keys: A = the same tile read MN-major, B = P^T
 //                                                (MN-major, written by the softmax threads) --
-//                                                twice: P's f16 head, then its f16 tail (two
-//                                                buffers; p keeps ~22 bits, as the averages over
-//                                                thousands of keys need);
-//   O_acc = O_acc * alpha + O_sub by the softmax threads (one fp32 FMA an element): the
-//   tensor core's accumulation into TMEM truncates, so a chunk's thousands of keys are summed
-//   8 MMA steps at a time in hardware and across sub-blocks in round-to-nearest fp32.
+//                                                twice into the same accumulator: P's f16 head,
+//                                                then its f16 tail (p keeps ~22 bits, as the
+//                                                averages over thousands of keys need);
+//   O_acc = O_acc * alpha + O_sub by the softmax threads two sub-blocks later (one fp32 FMA an
+//   element), so the softmax never waits for the PV just issued: the tensor core's
+//   accumulation into TMEM truncates, so a chunk's thousands of keys are summed 8 MMA steps at
+//   a time in hardware and across sub-blocks in round-to-nearest fp32.
 // The tile is stored as 8 x 16-byte core matrices: element (key, d) at
 //   (key / 8) * (D / 8) * 128 + (d / 8) * 128 + (key % 8) * 16 + (d % 8) * 2,
 // which is the K-major layout of the QK operand (leading offset 128 B, stride (D / 8) * 128 B)
 // and the MN-major layout of the PV operand (dims contiguous: stride 128 B, leading (D / 8)
 // * 128 B); Q likewise ([head][d]), P^T as [key group][head group][8 keys][8 heads].
 // Synchronization: mbarriers (producer -> MMA: tile full; MMA -> producer: tile free;
-// MMA -> softmax: S ready, PV done; softmax -> MMA: P ready), tcgen05.commit for MMA
+// MMA -> softmax: S ready, PV done; softmax -> MMA: S consumed, P ready), tcgen05.commit for MMA
 // completion; every wait is bounded and a timeout sets an error word and unwinds.
 #pragma once
 
@@ -38,18 +40,37 @@ constexpr int kTcKeys = 64;                // keys a sub-block
 constexpr int kTcThreads = 384;            // 12 warps
 constexpr int kTcProducers = 7 * 32;       // warps 5..11
 constexpr uint32_t kTcWaitPolls = 1u << 24;
+constexpr float kTcSlack = 8.f;            // log2 headroom of p over the reference max
 
 __device__ int g_tc_error;  // set when a bounded wait gave up (a kernel bug, never a peer)
 
 // Build-time role timeline of CTA 0 (clock64 at each role's milestones of each sub-block), for
 // pipeline tuning: compiled only with -DDSV41_TC_TRACE.
 #ifdef DSV41_TC_TRACE
-__device__ long long g_tc_trace[64 * 8];
+__device__ long long g_tc_trace[64 * 16];
 #define TC_TRACE(j, slot)                                                  \
   do {                                                                     \
-    if (blockIdx.x == 0 && (j) < 64) g_tc_trace[(j) * 8 + (slot)] = clock64(); \
+    if (blockIdx.x == 0 && (j) < 64) g_tc_trace[(j) * 16 + (slot)] = clock64(); \
+  } while (0)
+// every CTA's [start, end) in %globaltimer ns and its SM
+__device__ long long g_tc_span[4096 * 3];
+#define TC_SPAN(slot)                                                                       \
+  do {                                                                                      \
+    if (threadIdx.x == 0 && blockIdx.x < 4096) {                                            \
+      unsigned long long ns;                                                                \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(ns));                                \
+      g_tc_span[blockIdx.x * 3 + (slot)] = (long long)ns;                                   \
+      if ((slot) == 0) {                                                                    \
+        unsigned sm;                                                                        \
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));                                     \
+        g_tc_span[blockIdx.x * 3 + 2] = sm;                                                 \
+      }                                                                                     \
+    }                                                                                       \
   } while (0)
 #else
+#define TC_SPAN(slot) \
+  do {                \
+  } while (0)
 #define TC_TRACE(j, slot) \
   do {                    \
   } while (0)
@@ -70,12 +91,12 @@ struct TcSmem {
   static constexpr int kTile1 = kTileBytes;
   static constexpr int kQ = 2 * kTileBytes;
   static constexpr int kP = kQ + kQBytes;
-  static constexpr int kRed = kP + 2 * kPBytes;      // float [4 warps][64 heads]
+  static constexpr int kRed = kP + 4 * kPBytes;      // float [4 warps][64 heads]
   static constexpr int kM = kRed + 4 * 64 * 4;       // float [64]: the used max of each head
-  static constexpr int kAlpha = kM + 64 * 4;         // float [64]: this sub-block's rescale
+  static constexpr int kAlpha = kM + 64 * 4;         // float [64]: the rescale of the reference max
   static constexpr int kMeta = kAlpha + 64 * 4;      // [2 stages][64 keys]: record pointer, then 8 codes
   static constexpr int kBar = kMeta + 2 * 64 * 16;   // uint64 mbarriers
-  static constexpr int kNumBars = 9;
+  static constexpr int kNumBars = 13;
   static constexpr int kMisc = kBar + kNumBars * 8;  // tmem base, abort flag
   static constexpr int kBytes = kMisc + 16;
 };
@@ -125,6 +146,14 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   atomicExch(&g_tc_error, 1);
   return false;
 }
+// AND of a predicate over the 224 producer threads (named barrier 2), for the same reason.
+__device__ __forceinline__ bool producers_all(bool v) {
+  uint32_t r;
+  asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbarrier.red.and.pred q, 2, %2, p;\n\t"
+               "selp.u32 %0, 1, 0, q;\n\t}\n"
+               : "=r"(r) : "r"((uint32_t)v), "n"(kTcProducers) : "memory");
+  return r != 0;
+}
 // AND / OR of a predicate over the 128 softmax threads (named barrier 1): keeps their control
 // flow uniform, so no thread leaves while the others wait at the barrier.
 __device__ __forceinline__ bool softmax_all(bool v) {
@@ -166,6 +195,20 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// 2^x by the SFU's ex2 instruction (PTX ex2.approx.ftz.f32: about 2 ulp; results below 2^-126
+// flush to 0, far under what the f16 head/tail of p can hold).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+// {lo, hi} -> f16x2 bits (round to nearest), one instruction.
+__device__ __forceinline__ uint32_t cvt_f16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
 // Core-matrix byte offset of element (row r, column c) of a [rows][C] tile.
 template <int C>
 __device__ __forceinline__ int core_off(int r, int c) {
@@ -188,7 +231,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
   const int h0 = 32 * ht;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
-  // bars: 0,1 tile full; 2,3 tile free; 4 S ready; 5 S consumed; 6 P ready; 7 PV done; 8 MMA drain
+  // bars: 0,1 tile full; 2,3 tile free; 4,5 S ready; 6,7 S consumed; 8,9 P ready; 10,11 PV
+  // done; 12 MMA drain (pairs by the sub-block's parity)
   auto bar = [&](int i) { return smem_u32(bars + i); };
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
   uint32_t* tmem_base = reinterpret_cast<uint32_t*>(smem + L::kMisc);
@@ -199,6 +243,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
   const uint32_t s_q = smem_u32(smem + L::kQ), s_p = smem_u32(smem + L::kP);
 
   pdl_wait();
+  TC_SPAN(0);
   const int kv = a.klen[t];
   const int k0 = ch * a.chunk_keys, k1 = min(k0 + a.chunk_keys, kv);
   const int nsub = k1 > k0 ? (k1 - k0 + kTcKeys - 1) / kTcKeys : 0;
@@ -219,10 +264,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
     mbar_init(bar(2), 1);
     mbar_init(bar(3), 1);
     mbar_init(bar(4), 1);
-    mbar_init(bar(5), 4);
+    mbar_init(bar(5), 1);
     mbar_init(bar(6), 4);
-    mbar_init(bar(7), 1);
-    mbar_init(bar(8), 1);
+    mbar_init(bar(7), 4);
+    mbar_init(bar(8), 4);
+    mbar_init(bar(9), 4);
+    mbar_init(bar(10), 1);
+    mbar_init(bar(11), 1);
+    mbar_init(bar(12), 1);
     *abort = 0;
   }
   if (tid < 64) {
@@ -239,17 +288,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_base;
-  // TMEM columns: S^T at 0 (NH); O_acc block b at 32 + 32 b (NH); O_sub block b at 192 + 64 b
+  // TMEM columns: S^T[s] at 32 s (NH), s = the sub-block's parity; O^T block b at 64 + 64 b
   // (2 NH: the head pass's columns, then the tail pass's)
-  const uint32_t tm_s0 = tmem, tm_o = tmem + 32, tm_sub = tmem + 192;
+  const uint32_t tm_s = tmem, tm_o = tmem + 64;
 
   if (warp >= 5) {
     // ================= producers
-    // Per tile: producer threads 0..63 resolve their key (record pointer, the 8 scale codes;
+    // Per tile: producer threads 0..63 publish their key (record pointer, the 8 scale codes;
     // null = masked) into shared memory; then each producer warp converts units of 8 keys x 4
     // consecutive 16-byte chunks (lane: key 8 g + lane % 8, chunk 4 q + lane / 8), so a warp's
-    // loads are whole 64-byte runs of 8 records. The next tile's record loads are issued before
-    // this tile's conversion.
+    // loads are whole 64-byte runs of 8 records. Loads run ahead of use: while tile j converts,
+    // tile j + 1's record chunks, tile j + 2's scale codes and tile j + 3's key-table entries
+    // are in flight.
     static_assert(CHUNKS % 4 == 0, "records are whole 64-byte runs");
     const int ptid = tid - 5 * 32, wp = warp - 5;
     const int data_bytes = NOPE + 128;
@@ -263,25 +313,29 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
       c = 4 * (u / 8) + (lane >> 3);
       return u < kUnits;
     };
-    auto resolve = [&](int j) {
-      // thread ptid < 64: key ptid of tile j into stage j & 1
+    // key lookahead (threads ptid < 64, key ptid of a tile)
+    auto kt_load = [&](int j) {  // the key-table entry; -1 past the chunk
       const int k = k0 + j * kTcKeys + ptid;
-      const uint8_t* dp = nullptr;
-      uint64_t cw = 0;
-      if (k < k1) {
-        const int v = a.kt[(size_t)t * a.keys_ld + k];
-        const bool comp = v < 0 && v != -1 && a.comp != nullptr;
-        if (v >= 0 || comp) {
-          const int sl = v & 0x7fffffff;
-          const int blk = comp ? a.comp_blk : a.swa_blk;
-          const uint8_t* page = (comp ? a.comp : a.swa) + (int64_t)(sl / blk) * (comp ? a.comp_stride : a.swa_stride);
-          const int off = sl % blk;
-          dp = page + (size_t)off * data_bytes;
-          cw = *reinterpret_cast<const uint64_t*>(page + (size_t)blk * data_bytes + (size_t)off * 8);
-        }
+      return k < k1 ? a.kt[(size_t)t * a.keys_ld + k] : -1;
+    };
+    const uint8_t* la_p = nullptr;  // tile j + 2's record and scale-code word (load in flight)
+    uint64_t la_c = 0;
+    auto locate = [&](int v) {
+      la_p = nullptr;
+      la_c = 0;
+      const bool comp = v < 0 && v != -1 && a.comp != nullptr;
+      if (v >= 0 || comp) {
+        const int sl = v & 0x7fffffff;
+        const int blk = comp ? a.comp_blk : a.swa_blk;
+        const uint8_t* page = (comp ? a.comp : a.swa) + (int64_t)(sl / blk) * (comp ? a.comp_stride : a.swa_stride);
+        const int off = sl % blk;
+        la_p = page + (size_t)off * data_bytes;
+        la_c = *reinterpret_cast<const uint64_t*>(page + (size_t)blk * data_bytes + (size_t)off * 8);
       }
-      meta_p[(j & 1) * 64 + ptid] = dp;
-      meta_c[(j & 1) * 64 + ptid] = cw;
+    };
+    auto publish = [&](int j) {
+      meta_p[(j & 1) * 64 + ptid] = la_p;
+      meta_c[(j & 1) * 64 + ptid] = la_c;
     };
     auto issue = [&](int j, uint4 (&raw)[kItems]) {
       const int s = j & 1;
@@ -295,24 +349,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
         }
       }
     };
-    uint4 cur[kItems], nxt[kItems];
-    if (nsub > 0) {
-      if (ptid < 64) resolve(0);
-      asm volatile("bar.sync 2, %0;" ::"n"(kTcProducers) : "memory");
-      issue(0, cur);
-    }
-    for (int j = 0; j < nsub; ++j) {
+    auto convert = [&](int j, const uint4 (&raw)[kItems]) {
       const int s = j & 1;
-      if (j >= 2 && !mbar_wait(bar(2 + s), ((j >> 1) - 1) & 1, abort)) break;
-      if (ptid == 0) TC_TRACE(j, 0);
-      // the next tile's keys and record loads (its stage's metadata was last read two tiles ago)
-      if (j + 1 < nsub) {
-        // every producer is past tile j - 1's conversion (the metadata stage being rewritten)
-        asm volatile("bar.sync 2, %0;" ::"n"(kTcProducers) : "memory");
-        if (ptid < 64) resolve(j + 1);
-        asm volatile("bar.sync 2, %0;" ::"n"(kTcProducers) : "memory");
-        issue(j + 1, nxt);
-      }
       uint8_t* tile = smem + (s ? L::kTile1 : L::kTile0);
 #pragma unroll
       for (int i = 0; i < kItems; ++i) {
@@ -324,7 +362,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
           uint4 o0 = make_uint4(0, 0, 0, 0), o1 = o0;
           if (live) {
             const int cd = (int)((meta_c[s * 64 + key] >> (8 * (b0 / 64))) & 0xff);
-            const uint32_t w[4] = {cur[i].x, cur[i].y, cur[i].z, cur[i].w};
+            const uint32_t w[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
             uint32_t r[8];
             if (cd >= 113 && cd <= 134) {
               const uint32_t s1 = (uint32_t)(cd - 112) << 10;
@@ -351,44 +389,87 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
         } else {
           uint4 o0 = make_uint4(0, 0, 0, 0);
           if (live)
-            o0 = make_uint4(bf16x2_to_f16x2(cur[i].x), bf16x2_to_f16x2(cur[i].y), bf16x2_to_f16x2(cur[i].z),
-                            bf16x2_to_f16x2(cur[i].w));
+            o0 = make_uint4(bf16x2_to_f16x2(raw[i].x), bf16x2_to_f16x2(raw[i].y), bf16x2_to_f16x2(raw[i].z),
+                            bf16x2_to_f16x2(raw[i].w));
           *reinterpret_cast<uint4*>(tile + core_off<D>(key, NOPE + (b0 - NOPE) / 2)) = o0;
         }
       }
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(s));
+    };
+    // one tile: free its stage, publish and issue the next tile, convert this one (cur holds its
+    // chunks; nxt receives the next tile's)
+    int la_v = -1;  // tile j + 3's key-table entry (load in flight)
+    auto step = [&](int j, const uint4 (&cur)[kItems], uint4 (&nxt)[kItems]) {
+      const int s = j & 1;
+      // the stage is free (PV(j - 2) done), for every producer alike; and every producer is past
+      // tile j - 1's conversion (its metadata stage is rewritten next)
+      if (!producers_all(j < 2 || mbar_wait(bar(2 + s), ((j >> 1) - 1) & 1, abort))) return false;
+      if (ptid == 0) TC_TRACE(j, 0);
+      if (j + 1 < nsub) {
+        if (ptid < 64) publish(j + 1);
+        asm volatile("bar.sync 2, %0;" ::"n"(kTcProducers) : "memory");
+        if (ptid == 0) TC_TRACE(j, 14);
+        issue(j + 1, nxt);
+        if (ptid == 0) TC_TRACE(j, 15);
+      }
+      if (ptid < 64) {
+        locate(la_v);
+        la_v = kt_load(j + 3);
+      }
+      if (ptid == 0) TC_TRACE(j, 4);
+      convert(j, cur);
       if (ptid == 0) TC_TRACE(j, 1);
-#pragma unroll
-      for (int i = 0; i < kItems; ++i) cur[i] = nxt[i];
+      return true;
+    };
+    uint4 buf0[kItems], buf1[kItems];
+    if (nsub > 0) {
+      if (ptid < 64) {
+        locate(kt_load(0));
+        publish(0);
+        const int v1 = kt_load(1);
+        la_v = kt_load(2);
+        locate(v1);
+      }
+      asm volatile("bar.sync 2, %0;" ::"n"(kTcProducers) : "memory");
+      issue(0, buf0);
+    }
+    for (int j = 0; j < nsub; j += 2) {
+      if (!step(j, buf0, buf1)) break;
+      if (j + 1 < nsub && !step(j + 1, buf1, buf0)) break;
     }
   } else if (warp == 4) {
     // ================= MMA issue (one elected thread)
-    // QK(j) needs tile j and the S buffer consumed by softmax(j - 1); PV(j) needs P(j). QK(j + 1)
-    // goes out as soon as both are ready, so it runs under softmax(j).
+    // QK(j) needs tile j and S[j & 1] consumed by softmax(j - 2); PV(j) needs P(j) (written
+    // after softmax(j) rescaled O, when it had to). QK(j + 1) goes out as soon as its inputs are
+    // ready, so it runs under softmax(j).
     if (lane == 0) {
       const uint32_t id_qk = umma_idesc(64, NH, 0, 0);
       const uint32_t id_pv = umma_idesc(128, 2 * NH, 1, 1);
       auto issue_qk = [&](int j) {
         const uint32_t tile = s_tile0 + ((j & 1) ? L::kTileBytes : 0);
+        const uint32_t dst = tm_s + 32 * (j & 1);
 #pragma unroll 4
         for (int ks = 0; ks < D / 16; ++ks)
-          umma_f16(tm_s0, umma_sdesc(tile + 256 * ks, 128, DG * 128), umma_sdesc(s_q + 256 * ks, 128, DG * 128), id_qk,
+          umma_f16(dst, umma_sdesc(tile + 256 * ks, 128, DG * 128), umma_sdesc(s_q + 256 * ks, 128, DG * 128), id_qk,
                    ks > 0);
-        umma_commit(bar(4));
+        umma_commit(bar(4 + (j & 1)));
+        TC_TRACE(j, 11);
       };
-      auto qk_ready = [&](int j) {  // tile j loaded and S consumed by softmax(j - 1)
-        return mbar_try(bar(j & 1), (j >> 1) & 1) && (j == 0 || mbar_try(bar(5), (j - 1) & 1));
+      auto qk_ready = [&](int j) {  // tile j loaded and S[j & 1] consumed by softmax(j - 2)
+        return mbar_try(bar(j & 1), (j >> 1) & 1) && (j < 2 || mbar_try(bar(6 + (j & 1)), ((j - 2) >> 1) & 1));
       };
       auto wait_qk = [&](int j) {
-        return mbar_wait(bar(j & 1), (j >> 1) & 1, abort) && (j == 0 || mbar_wait(bar(5), (j - 1) & 1, abort));
+        return mbar_wait(bar(j & 1), (j >> 1) & 1, abort) &&
+               (j < 2 || mbar_wait(bar(6 + (j & 1)), ((j - 2) >> 1) & 1, abort));
       };
       bool ok = true;
       if (nsub > 0) ok = wait_qk(0);
       if (ok && nsub > 0) issue_qk(0);
       for (int j = 0; ok && j < nsub; ++j) {
         const int s = j & 1;
+        const uint32_t p_ready = bar(8 + s), p_par = (j >> 1) & 1;
         bool qk_done = j + 1 >= nsub;
         if (!qk_done && qk_ready(j + 1)) {
           issue_qk(j + 1);
@@ -397,7 +478,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
         if (!qk_done) {
           // wait for whichever comes first: P(j) (then PV), or QK(j + 1)'s inputs
           for (uint32_t it = 0; !qk_done && it < kTcWaitPolls; ++it) {
-            if (mbar_try(bar(6), j & 1)) break;
+            if (mbar_try(p_ready, p_par)) break;
             if (qk_ready(j + 1)) {
               issue_qk(j + 1);
               qk_done = true;
@@ -405,22 +486,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
           }
         }
         TC_TRACE(j, 2);
-        ok = mbar_wait(bar(6), j & 1, abort);
+        ok = mbar_wait(p_ready, p_par, abort);
         if (!ok) break;
         TC_TRACE(j, 3);
         tc_fence_after();
-        // PV: B = P^T with the f16 head of p in columns 0 .. NH - 1, its tail in NH .. 2 NH - 1
+        // PV: O += V^T P^T, P^T's columns the f16 head of p (0 .. NH - 1), then its tail
         const uint32_t tile = s_tile0 + (s ? L::kTileBytes : 0);
+        const uint32_t pt = s_p + 2 * s * L::kPBytes;
 #pragma unroll
         for (int b = 0; b < NBLK; ++b) {
           const int d0 = min(128 * b, D - 128);
 #pragma unroll
           for (int ks = 0; ks < kTcKeys / 16; ++ks)
-            umma_f16(tm_sub + 64 * b, umma_sdesc(tile + (d0 / 8) * 128 + 2 * ks * DG * 128, DG * 128, 128),
-                     umma_sdesc(s_p + 2 * ks * (2 * NH / 8) * 128, (2 * NH / 8) * 128, 128), id_pv, ks > 0);
+            umma_f16(tm_o + 64 * b, umma_sdesc(tile + (d0 / 8) * 128 + 2 * ks * DG * 128, DG * 128, 128),
+                     umma_sdesc(pt + 2 * ks * (2 * NH / 8) * 128, (2 * NH / 8) * 128, 128), id_pv, j > 0 || ks > 0);
         }
-        umma_commit(bar(2 + s));  // the tile is free
-        umma_commit(bar(7));      // P^T free; O_sub holds sub-block j
+        umma_commit(bar(2 + s));   // the tile is free
+        umma_commit(bar(10 + s));  // P[s] free; O holds sub-blocks 0 .. j
         if (!qk_done) {
           ok = wait_qk(j + 1);
           if (!ok) break;
@@ -428,15 +510,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
         }
       }
       // drain: every issued MMA complete before the TMEM is freed (also after an abort)
-      umma_commit(bar(8));
-      mbar_wait(bar(8), 0, abort);
+      umma_commit(bar(12));
+      mbar_wait(bar(12), 0, abort);
     }
   } else {
     // ================= softmax + epilogue (warps 0-3: TMEM lanes 32 w .. 32 w + 31)
     // Thread (warp w, lane < 16) holds key 16 w + lane of a sub-block (S^T rows of an M = 64
-    // MMA sit on the first 16 lanes of each 32-lane quarter). Heads go 16 at a time; the
-    // running max of each head and the rescale factors live in shared memory (the same for
-    // every thread); each key thread keeps its own partial sums of p.
+    // MMA sit on the first 16 lanes of each 32-lane quarter). p = 2^(s - m) against a per-head
+    // reference m that moves only when a sub-block's max passes it by more than 2^kTcSlack
+    // (p <= 2^kTcSlack stays well inside f16): then O and the partial sums are rescaled once.
+    // Each key thread keeps its own partial sums of p.
     const int key = 16 * warp + (lane & 15);
     const bool has_key = lane < 16;
     const uint32_t lane_addr = (uint32_t)(32 * warp) << 16;
@@ -445,60 +528,55 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
 #pragma unroll
     for (int h = 0; h < 32; ++h) l_part[h] = 0.f;
     bool ok = true;
-    // O_acc = O_acc * alpha + O_sub for this thread's lane (dim) in every block: sub-block
-    // jj's PV result joins the sum at jj's max (alpha: the rescale the sub-block made)
-    auto fold = [&](int jj) {
+    // O *= alpha (per head, head and tail columns) for this thread's lane (dim) in every block
+    auto rescale_o = [&]() {
 #pragma unroll 1
       for (int b = 0; b < NBLK; ++b) {
 #pragma unroll
         for (int g = 0; g < 2; ++g) {
           if (g >= ngroups) break;
-          uint32_t vh[16], vt[16], va[16];
-          const uint32_t sub = tm_sub + 64 * b + lane_addr + 16 * g, acc = tm_o + 32 * b + lane_addr + 16 * g;
-          tmem_ld16(sub, vh);
-          tmem_ld16(sub + NH, vt);
-          if (jj > 0) tmem_ld16(acc, va);
+          uint32_t vh[16], vt[16];
+          const uint32_t col = tm_o + 64 * b + lane_addr + 16 * g;
+          tmem_ld16(col, vh);
+          tmem_ld16(col + NH, vt);
           tmem_wait_ld();
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
-            const float x = __uint_as_float(vh[q]) + __uint_as_float(vt[q]);  // head + tail pass
-            va[q] = __float_as_uint(jj > 0 ? fmaf(__uint_as_float(va[q]), a_sm[16 * g + q], x) : x);
+            vh[q] = __float_as_uint(__uint_as_float(vh[q]) * a_sm[16 * g + q]);
+            vt[q] = __float_as_uint(__uint_as_float(vt[q]) * a_sm[16 * g + q]);
           }
-          tmem_st16(acc, va);
+          tmem_st16(col, vh);
+          tmem_st16(col + NH, vt);
         }
       }
       tmem_wait_st();
     };
+    // this thread's key-table entry, one sub-block ahead
+    auto kt_entry = [&](int j) {
+      const int k = k0 + j * kTcKeys + key;
+      return (has_key && k < k1) ? a.kt[(size_t)t * a.keys_ld + k] : -1;
+    };
+    int kt_next = nsub > 0 ? kt_entry(0) : -1;
     for (int j = 0; ok && j < nsub; ++j) {
-      bool w_ok = mbar_wait(bar(4), j & 1, abort);
-      ok = softmax_all(w_ok);
+      const int s = j & 1;
+      const int kv_ = kt_next;
+      kt_next = j + 1 < nsub ? kt_entry(j + 1) : -1;
+      const bool valid = kv_ != -1 && (kv_ >= 0 || a.comp != nullptr);
+      ok = softmax_all(mbar_wait(bar(4 + s), (j >> 1) & 1, abort));
       if (!ok) break;
       if (tid == 0) TC_TRACE(j, 5);
       tc_fence_after();
-      const uint32_t src = tm_s0 + lane_addr;
       float sv[32];
       {
         uint32_t v[32];
-        tmem_ld16(src, *reinterpret_cast<uint32_t(*)[16]>(v));
-        if (NH > 16) tmem_ld16(src + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
+        tmem_ld16(tm_s + 32 * s + lane_addr, *reinterpret_cast<uint32_t(*)[16]>(v));
+        if (NH > 16) tmem_ld16(tm_s + 32 * s + lane_addr + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
         tmem_wait_ld();
-        // S is in registers: QK(j + 1) may overwrite it
+        // S[s] is in registers: QK(j + 2) may overwrite it
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar(5));
-        // the previous sub-block's PV result joins O_acc (O_sub and P^T are then free)
-        if (j > 0) {
-          ok = softmax_all(mbar_wait(bar(7), (j - 1) & 1, abort));
-          if (!ok) break;
-          tc_fence_after();
-          fold(j - 1);
-        }
-        const int k = k0 + j * kTcKeys + key;
-        bool valid = has_key && k < k1;
-        if (valid) {
-          const int kv_ = a.kt[(size_t)t * a.keys_ld + k];
-          valid = kv_ != -1 && (kv_ >= 0 || a.comp != nullptr);
-        }
+        if (lane == 0) mbar_arrive(bar(6 + s));
+        if (tid == 0) TC_TRACE(j, 8);
 #pragma unroll
         for (int q = 0; q < 32; ++q) sv[q] = (valid && q < NH) ? __uint_as_float(v[q]) * a.scale_log2 : -INFINITY;
       }
@@ -512,54 +590,88 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
         x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 8));
         if (lane == 0) red[warp * 32 + q] = x;
       }
-      softmax_bar();  // red complete; every thread is past its fold (a_sm may change)
+      softmax_bar();  // red complete
       if (tid == 0) TC_TRACE(j, 6);
+      bool moved = false;  // a head's reference moved while O already holds its sums
       if (tid < NH) {
         const float bx = fmaxf(fmaxf(red[tid], red[32 + tid]), fmaxf(red[64 + tid], red[96 + tid]));
         const float mu = m_sm[tid];
-        const float mn = fmaxf(mu, bx);
-        a_sm[tid] = (mu == -INFINITY) ? 0.f : exp2f(mu - mn);
-        m_sm[tid] = mn;
+        float al = 1.f;
+        if (bx > mu + kTcSlack) {
+          al = (mu == -INFINITY) ? 0.f : exp2f(mu - bx);
+          moved = mu != -INFINITY;
+          m_sm[tid] = bx;
+        }
+        a_sm[tid] = al;
       }
-      softmax_bar();
-      // p = 2^(s - m) (<= 1) into P^T as an f16 head and its f16 tail (the two PV passes see
-      // ~22 bits of p); this thread's partial sums of p
+      const bool rescale = softmax_any(moved) && j > 0;  // also publishes m_sm / a_sm
+      if (tid == 0) TC_TRACE(j, 9);
+      if (rescale) {
+        // O must hold every issued PV before it is scaled
+        ok = softmax_all(mbar_wait(bar(10 + ((j - 1) & 1)), ((j - 1) >> 1) & 1, abort));
+        if (!ok) break;
+        tc_fence_after();
+        rescale_o();
+        tc_fence_before();
+#pragma unroll
+        for (int q = 0; q < 32; ++q) l_part[q] *= a_sm[q];
+        if (tid == 0) TC_TRACE(j, 10);
+      }
+      // p = 2^(s - m) into P^T[s] as an f16 head and its f16 tail (the PV sees ~22 bits of p);
+      // this thread's partial sums of p
+      // (the head keeps p's top 11 significant bits, exact in f16 for p >= 2^-14; the tail is
+      // the exact remainder, rounded to f16)
       uint32_t hi[16], lo[16];
 #pragma unroll
-      for (int q = 0; q < 32; q += 2) {
-        const float p0 = sv[q] == -INFINITY ? 0.f : exp2f(sv[q] - m_sm[q]);
-        const float p1 = sv[q + 1] == -INFINITY ? 0.f : exp2f(sv[q + 1] - m_sm[q + 1]);
-        l_part[q] = l_part[q] * a_sm[q] + p0;
-        l_part[q + 1] = l_part[q + 1] * a_sm[q + 1] + p1;
-        const __half ph0 = __float2half_rn(p0), ph1 = __float2half_rn(p1);
-        hi[q / 2] = pack_f16x2(p0, p1);
-        lo[q / 2] = pack_f16x2(p0 - __half2float(ph0), p1 - __half2float(ph1));
+      for (int q = 0; q < 32; q += 4) {
+        const float4 m4 = *reinterpret_cast<const float4*>(m_sm + q);
+        const float mq[4] = {m4.x, m4.y, m4.z, m4.w};
+        float pq[4], hq[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          pq[i] = sv[q + i] == -INFINITY ? 0.f : ex2_approx(sv[q + i] - mq[i]);
+          l_part[q + i] += pq[i];
+          hq[i] = __uint_as_float(__float_as_uint(pq[i]) & 0xffffe000u);
+        }
+        hi[q / 2] = cvt_f16x2(hq[0], hq[1]);
+        hi[q / 2 + 1] = cvt_f16x2(hq[2], hq[3]);
+        lo[q / 2] = cvt_f16x2(pq[0] - hq[0], pq[1] - hq[1]);
+        lo[q / 2 + 1] = cvt_f16x2(pq[2] - hq[2], pq[3] - hq[3]);
       }
+      if (tid == 0) TC_TRACE(j, 12);
+      // P^T[s] is free once PV(j - 2) is done
+      if (j >= 2) {
+        ok = softmax_all(mbar_wait(bar(10 + s), ((j - 2) >> 1) & 1, abort));
+        if (!ok) break;
+      }
+      if (tid == 0) TC_TRACE(j, 13);
       if (has_key) {
         // P^T [key group][column group][8 keys][8 columns]: head groups 0 .. NH / 8 - 1, then tail
+        uint8_t* pt = smem + L::kP + 2 * s * L::kPBytes;
+        const int row = (key >> 3) * (2 * NH / 8);
 #pragma unroll
         for (int hg = 0; hg < 4; ++hg) {
           if (8 * hg >= NH) break;
-          const int row = (key >> 3) * (2 * NH / 8);
-          *reinterpret_cast<uint4*>(smem + L::kP + (row + hg) * 128 + (key & 7) * 16) =
+          *reinterpret_cast<uint4*>(pt + (row + hg) * 128 + (key & 7) * 16) =
               make_uint4(hi[4 * hg], hi[4 * hg + 1], hi[4 * hg + 2], hi[4 * hg + 3]);
-          *reinterpret_cast<uint4*>(smem + L::kP + (row + NH / 8 + hg) * 128 + (key & 7) * 16) =
+          *reinterpret_cast<uint4*>(pt + (row + NH / 8 + hg) * 128 + (key & 7) * 16) =
               make_uint4(lo[4 * hg], lo[4 * hg + 1], lo[4 * hg + 2], lo[4 * hg + 3]);
         }
       }
       fence_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(6));
+      if (lane == 0) mbar_arrive(bar(8 + s));
       if (tid == 0) TC_TRACE(j, 7);
+      // (the next update of red, m_sm and a_sm comes after the next sub-block's first barrier,
+      // which every thread reaches only after this sub-block's reads)
     }
-    // ---- epilogue: the last sub-block folded in, then O_acc^T and (m, l) of the chunk
-    if (ok && nsub > 0) ok = softmax_all(mbar_wait(bar(7), (nsub - 1) & 1, abort));
+    // ---- epilogue: every PV done, then O^T (head + tail columns) and (m, l) of the chunk
+    if (ok && nsub > 0) ok = softmax_all(mbar_wait(bar(10 + ((nsub - 1) & 1)), ((nsub - 1) >> 1) & 1, abort));
     const size_t base = ((size_t)t * a.nchunks + ch) * a.heads + h0;
     const int nh_live = min(NH, a.heads - h0);
     if (ok && nsub > 0) {
       tc_fence_after();
-      fold(nsub - 1);
       // l: the partial sums of the 64 key threads (16 lanes x 4 warps)
 #pragma unroll
       for (int h = 0; h < 32; ++h) {
@@ -585,13 +697,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
 #pragma unroll
         for (int g = 0; g < 2; ++g) {
           if (g >= ngroups) break;
-          uint32_t v[16];
-          tmem_ld16(tm_o + 32 * b + lane_addr + 16 * g, v);
+          uint32_t vh[16], vt[16];
+          tmem_ld16(tm_o + 64 * b + lane_addr + 16 * g, vh);
+          tmem_ld16(tm_o + 64 * b + lane_addr + NH + 16 * g, vt);
           tmem_wait_ld();
           if (own)
 #pragma unroll
             for (int q = 0; q < 16; ++q)
-              if (16 * g + q < nh_live) a.part_o[(base + 16 * g + q) * D + d] = __uint_as_float(v[q]);
+              if (16 * g + q < nh_live)
+                a.part_o[(base + 16 * g + q) * D + d] = __uint_as_float(vh[q]) + __uint_as_float(vt[q]);
         }
       }
     } else if (nsub == 0 && tid < nh_live) {
@@ -606,6 +720,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
   }
+  TC_SPAN(1);
   pdl_launch();
 }
 

@@ -322,7 +322,16 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   const bool tc = use_tc_attention() && (nope == 512 || nope == 448);
   const int head_tiles = tc ? cdiv(heads, 32) : cdiv(heads, 16);
   const int units = M * head_tiles;
-  int nchunks = tc ? std::max(1, (sms + units / 2) / units) : cdiv(2 * sms, units);
+  int nchunks = cdiv(2 * sms, units);
+  if (tc) {
+    // one CTA an SM: the split with the fewest sub-block periods over all waves, a CTA's start
+    // and drain counted as 4 periods (ties: fewer chunks, so fewer partials for the combine)
+    int64_t best = INT64_MAX;
+    for (int c = 1; c <= cdiv(keys, kSub); ++c) {
+      const int64_t cost = (int64_t)cdiv(units * c, sms) * (cdiv(cdiv(keys, c), kSub) + 4);
+      if (cost < best) best = cost, nchunks = c;
+    }
+  }
   nchunks = std::max(1, std::min(nchunks, cdiv(keys, kSub)));
   const int chunk_keys = cdiv(cdiv(keys, nchunks), kSub) * kSub;
   nchunks = cdiv(keys, chunk_keys);
