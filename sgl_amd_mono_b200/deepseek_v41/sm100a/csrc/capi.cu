@@ -22,6 +22,7 @@
 #include "k2i.cuh"
 #include "lmhead.cuh"
 #include "moe.cuh"
+#include "moe_tc.cuh"
 #include "peer.cuh"
 #include "seam.cuh"
 
@@ -96,6 +97,37 @@ cudaError_t gemv_go(const GemvArgs& g, cudaStream_t st) {
   return gemv_launch(g, st, use_pdl());
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link-time libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  });
+  return fn;
+}
+
+// The tensor map of a relayout expert weight: `tiles` 128-row x 128-K tiles of packed e2m1 (8 KB
+// each), read as unpacked FP4 (16U4_ALIGN16B) with the 128-byte swizzle, one tile a copy.
+bool expert_weight_map(CUtensorMap* m, const void* w, int64_t tiles) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc || !w || reinterpret_cast<uintptr_t>(w) % 32) return false;
+  const cuuint64_t dims[3] = {128, 128, (cuuint64_t)tiles};
+  const cuuint64_t strides[2] = {64, 8192};
+  const cuuint32_t box[3] = {128, 128, 1};
+  const cuuint32_t es[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<void*>(w), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <typename Kern, typename Args>
 cudaError_t launch(Kern kernel, dim3 grid, dim3 block, int smem, cudaStream_t st, const Args& args) {
   g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -114,6 +146,27 @@ cudaError_t launch(Kern kernel, dim3 grid, dim3 block, int smem, cudaStream_t st
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, args);
+}
+
+// The same with two kernel parameters (a tensor map, then the arguments).
+template <typename Kern, typename A0, typename A1>
+cudaError_t launch2(Kern kernel, dim3 grid, dim3 block, int smem, cudaStream_t st, const A0& a0, const A1& a1) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  if (smem > 48 * 1024) {
+    cudaError_t e = ensure_smem(reinterpret_cast<const void*>(kernel), smem);
+    if (e != cudaSuccess) return e;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = use_pdl() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, a0, a1);
 }
 
 // y[m][n] = sum over K slices of partials p[ks][m][n], in slice order.
@@ -381,7 +434,7 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   const int max_units = std::min(E, P);
   ExpertArgs eu = {};
   eu.M = M; eu.topk = TK; eu.N = 2 * I; eu.K = H; eu.ks_len = std::min(H, 1024);
-  eu.kslices = cdiv(H, eu.ks_len); eu.row_groups = cdiv(2 * I / 16, 8); eu.max_units = max_units;
+  eu.kslices = cdiv(H, eu.ks_len); eu.row_groups = 2 * I / 128; eu.max_units = max_units;
   eu.w = ptr<const uint8_t>(a->w13); eu.ws = ptr<const uint8_t>(a->w13_codes);
   eu.x = x8r; eu.xs = x8rs; eu.x_by_pick = 0;
   eu.n_u = n_u; eu.u_expert = u_expert; eu.u_off = u_off; eu.picks = picks;
@@ -390,14 +443,16 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   auto* mids = c.take<uint8_t>((int64_t)P * I / 32);
   ExpertArgs ed = eu;
   ed.N = H; ed.K = I; ed.ks_len = std::min(I, 1024); ed.kslices = cdiv(I, ed.ks_len);
-  ed.row_groups = cdiv(H / 16, 8); ed.w = ptr<const uint8_t>(a->w2); ed.ws = ptr<const uint8_t>(a->w2_codes);
+  ed.row_groups = H / 128; ed.w = ptr<const uint8_t>(a->w2); ed.ws = ptr<const uint8_t>(a->w2_codes);
   ed.x = mid; ed.xs = mids; ed.x_by_pick = 1;
   ed.out = c.take<float>((int64_t)ed.kslices * P * H);
   auto* moe_part = a->moe_part ? ptr<__nv_bfloat16>(a->moe_part) : c.take<__nv_bfloat16>((int64_t)M * H);
   *need = c.off;
   if (!go) return DSV41_OK;
   if (!a->scratch || a->scratch_bytes < c.off) return DSV41_ESCRATCH;
-  if (eu.ks_len % 128 || ed.ks_len % 128 || H % eu.ks_len || I % ed.ks_len) return DSV41_EINVAL;
+  if (eu.ks_len % 128 || ed.ks_len % 128 || H % eu.ks_len || I % ed.ks_len || eu.ks_len > kMxKsMax ||
+      ed.ks_len > kMxKsMax)
+    return DSV41_EINVAL;
 
   const int phase = (int)a->phase, tp = (int)a->tp, rank = (int)a->rank;
   const __nv_bfloat16* reduced = attn;
@@ -479,14 +534,25 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   DSV41_TRY(launch(shared_act_kernel, dim3(grid_for((int64_t)M * SI / 8, 256)), dim3(256), 0, st, sa));
   DSV41_TRY(gemv_go(gd, st));
   mark(a->events, 5, st);
-  // ---- routed experts
-  // persistent: exactly the resident CTAs (two an SM), each looping over work items
-  DSV41_TRY(launch(expert_gemv_kernel, dim3(std::min(2 * sms, max_units * eu.row_groups * eu.kslices)), dim3(256),
-                   expert_smem_bytes(eu.ks_len), st, eu));
-  ExpertActArgs ea = {P, I, eu.kslices, eu.out, mid, mids};
-  DSV41_TRY(launch(expert_act_kernel, dim3(grid_for((int64_t)P * I / 8, 256)), dim3(256), 0, st, ea));
-  DSV41_TRY(launch(expert_gemv_kernel, dim3(std::min(2 * sms, max_units * ed.row_groups * ed.kslices)), dim3(256),
-                   expert_smem_bytes(ed.ks_len), st, ed));
+  // ---- routed experts: persistent tcgen05 grouped GEMMs, one CTA an SM
+  {
+    CUtensorMap m13, m2;
+    if (!expert_weight_map(&m13, ptr<const void>(a->w13), (int64_t)E * (2 * I / 128) * (H / 128)) ||
+        !expert_weight_map(&m2, ptr<const void>(a->w2), (int64_t)E * (H / 128) * (I / 128))) {
+      fprintf(stderr, "dsv41: expert weight tensor map failed (driver entry point or alignment)\n");
+      return DSV41_ELAUNCH;
+    }
+    const ExpertTcArgs tu = {M, TK, 2 * I, H, eu.kslices, eu.ks_len, 2 * I / 128, eu.ws, eu.x, eu.xs, 0,
+                             n_u, u_expert, u_off, picks, eu.out};
+    const ExpertTcArgs td = {M, TK, H, I, ed.kslices, ed.ks_len, H / 128, ed.ws, ed.x, ed.xs, 1,
+                             n_u, u_expert, u_off, picks, ed.out};
+    DSV41_TRY(launch2(expert_tc_kernel, dim3(std::min(sms, max_units * eu.kslices * eu.row_groups)),
+                      dim3(kMxThreads), MxSmem::kBytes, st, m13, tu));
+    ExpertActArgs ea = {P, I, eu.kslices, eu.out, mid, mids};
+    DSV41_TRY(launch(expert_act_kernel, dim3(grid_for((int64_t)P * I / 8, 256)), dim3(256), 0, st, ea));
+    DSV41_TRY(launch2(expert_tc_kernel, dim3(std::min(sms, max_units * ed.kslices * ed.row_groups)),
+                      dim3(kMxThreads), MxSmem::kBytes, st, m2, td));
+  }
   CombineMoeArgs cm = {M, H, TK, ed.kslices, gd.kslices, ed.out, ptr<const float>(a->wts), gd.out, moe_part};
   mark(a->events, 6, st);
   DSV41_TRY(launch(moe_combine_kernel, dim3(grid_for((int64_t)M * H, 256)), dim3(256), 0, st, cm));
@@ -710,7 +776,7 @@ int dsv41_argmax_decode(const Dsv41ArgmaxArgs* a, void* stream) {
 
 int dsv41_relayout_mxfp4(const Dsv41RelayoutArgs* a, void* stream) {
   if (!a || !a->src || !a->src_codes || !a->dst || !a->dst_codes || a->E < 1 || a->N % 16 ||
-      a->K % 128 || a->N < 16)
+      a->K % 128 || a->N < 16 || a->src % 16 || a->dst % 16 || a->src_codes % 4 || a->dst_codes % 4)
     return DSV41_EINVAL;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   relayout_mxfp4_kernel<<<4 * 148 * 4, 256, 0, st>>>(ptr<const uint8_t>(a->src), ptr<const uint8_t>(a->src_codes),

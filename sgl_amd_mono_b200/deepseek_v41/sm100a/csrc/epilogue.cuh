@@ -1,5 +1,5 @@
 // GEMV epilogues that need no stage-specific math: K-slice sums rounded to bf16, optionally
-// requantized to vLLM-rule MXFP8; the rank-order all-reduce sum; the MXFP4 fragment relayout.
+// requantized to vLLM-rule MXFP8; the rank-order all-reduce sum; the MXFP4 tensor-core tile relayout.
 #pragma once
 
 #include "common.cuh"
@@ -58,38 +58,40 @@ __global__ void finalize_kernel(const FinalizeArgs a) {
   pdl_launch();
 }
 
-// MXFP4 weight [E][N][K/2] (even K in the low nibble) + E8M0 [E][N][K/32] -> fragment order:
-// tile (e, rt, kc) of 16 rows x 128 K is 1024 bytes; byte 16 L + q of half h (h = 0, 1) of
-// lane L = 4 g + t holds, for jj = q / 4 (block b = 2 h + jj / 2, half j = jj % 2) and
-// e = q % 4, the source byte of row 16 rt + g + 8 (e & 1) at K index
-// 128 kc + 32 b + 16 j + 8 (e >> 1) + 2 t. Codes: 64 bytes a tile, 8 a row pair g:
-// (g, b0), (g + 8, b0), (g, b1), (g + 8, b1), ... (g + 8, b3).
+// MXFP4 weight [E][N][K/2] (even K in the low nibble) + E8M0 [E][N][K/32] -> the tensor-core
+// tiles of expert_tc_kernel: tile (e, rt, kt) = 128 rows x 128 K at ((e RT + rt) KT + kt) 8192,
+// RT = ceil(N / 128), KT = K / 128; its row r holds source row 128 rt + r, bytes 64 kt ..
+// 64 kt + 63 (zero past N). Codes: 512 bytes a tile, row r's code of K block 4 kt + b at
+// (r % 32) * 16 + (r / 32) * 4 + b (the TMEM scale-atom order). 16 bytes (4 code bytes) a step.
 __global__ void relayout_mxfp4_kernel(const uint8_t* __restrict__ src, const uint8_t* __restrict__ src_codes,
                                       uint8_t* __restrict__ dst, uint8_t* __restrict__ dst_codes,
                                       int64_t E, int N, int K) {
-  const int64_t tiles = (int64_t)E * (N / 16) * (K / 128);
-  const int64_t total = tiles * 1024;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t tile = i / 1024;
-    const int r = (int)(i % 1024);
-    const int h = r / 512, L = (r % 512) / 16, q = r % 16;
-    const int g = L / 4, t = L % 4, jj = q / 4, e = q % 4;
-    const int b = 2 * h + jj / 2, j = jj % 2;
-    const int kc = (int)(tile % (K / 128));
-    const int64_t rt_all = tile / (K / 128);  // e * (N / 16) + rt
-    const int64_t ex = rt_all / (N / 16);
-    const int rt = (int)(rt_all % (N / 16));
-    const int row = 16 * rt + g + 8 * (e & 1);
-    const int k = 128 * kc + 32 * b + 16 * j + 8 * (e >> 1) + 2 * t;
-    dst[i] = src[(ex * N + row) * (int64_t)(K / 2) + k / 2];
-    if (i % 16 == 0 && L < 8 && h == 0) {
-      // codes of row pair g = L (one writer a row pair)
-      const int gg = L;
-      for (int bb = 0; bb < 4; ++bb)
-        for (int ee = 0; ee < 2; ++ee)
-          dst_codes[tile * 64 + 8 * gg + 2 * bb + ee] =
-              src_codes[(ex * N + 16 * rt + gg + 8 * ee) * (int64_t)(K / 32) + 4 * kc + bb];
-    }
+  const int RT = (N + 127) / 128, KT = K / 128;
+  const int64_t tiles = E * RT * KT;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < tiles * 512; i += stride) {
+    const int64_t tile = i / 512;
+    const int within = (int)(i % 512) * 16;
+    const int r = within / 64, cb = within % 64;
+    const int kt = (int)(tile % KT);
+    const int rt = (int)((tile / KT) % RT);
+    const int64_t ex = tile / ((int64_t)KT * RT);
+    const int row = 128 * rt + r;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (row < N) v = *reinterpret_cast<const uint4*>(src + (ex * N + row) * (int64_t)(K / 2) + 64 * kt + cb);
+    *reinterpret_cast<uint4*>(dst + i * 16) = v;
+  }
+  for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < tiles * 128; j += stride) {
+    const int64_t tile = j / 128;
+    const int q = (int)(j % 128);  // (r % 32) * 4 + r / 32
+    const int r = q / 4 + 32 * (q % 4);
+    const int kt = (int)(tile % KT);
+    const int rt = (int)((tile / KT) % RT);
+    const int64_t ex = tile / ((int64_t)KT * RT);
+    const int row = 128 * rt + r;
+    uint32_t v = 0;
+    if (row < N) v = *reinterpret_cast<const uint32_t*>(src_codes + (ex * N + row) * (int64_t)(K / 32) + 4 * kt);
+    *reinterpret_cast<uint32_t*>(dst_codes + tile * 512 + 4 * q) = v;
   }
 }
 

@@ -7,12 +7,9 @@
 // to fp32; scores use the deterministic fp64 softplus (detmath.cuh); the top-k takes the
 // largest (score + bias), ties to the lower expert id.
 //
-// Routed experts run on a one-time fragment relayout of the MXFP4 weights (logged by the
-// runner): a 16-row x 128-K tile is 1 KB, lane L holding bytes 16 L .. and 512 + 16 L ..,
-// i.e. the A fragments of 8 mma.m16n8k16 (4 E8M0 blocks x 2 halves) for rows g, g + 8; the
-// tile's 64 E8M0 codes are stored 8 a row pair. Activations (MXFP8 e4m3) convert exactly to
-// f16, weights by cvt.e2m1x2; each 32-K block's fp32 partial is scaled by
-// 2^(cw + cx - 254) into the accumulator.
+// Routed experts (moe_tc.cuh) run on a one-time relayout of the MXFP4 weights into 128-row x
+// 128-K tensor-core tiles (logged by the runner): tcgen05 block-scaled MMAs of e2m1 weights and
+// e4m3 activations with their E8M0 codes.
 #pragma once
 
 #include "common.cuh"
@@ -219,14 +216,16 @@ __global__ void __launch_bounds__(512) moe_plan_kernel(const PlanArgs a) {
   pdl_launch();
 }
 
-// ------------------------------------------------------------------ routed expert GEMV
+// ------------------------------------------------------------------ routed expert plan
+// The host's plan of one routed-expert GEMM (gate/up or down); expert_tc_kernel (moe_tc.cuh)
+// runs it.
 struct ExpertArgs {
   int M, topk, N, K;   // N rows of the expert matrix (2 I for gate/up, H for down), K
   int kslices, ks_len;  // K slices (ks_len a multiple of 128)
-  int row_groups;       // 128-row groups of N
-  int max_units;        // union slots launched for (min(E, M topk))
-  const uint8_t* w;     // relayout [E][N/16][K/128][1024]
-  const uint8_t* ws;    // relayout codes [E][N/16][K/128][64]
+  int row_groups;       // 128-row tiles of N
+  int max_units;        // union slots (min(E, M topk))
+  const uint8_t* w;     // tensor-core tiles [E][N/128][K/128][128][64]
+  const uint8_t* ws;    // codes [E][N/128][K/128][512]
   const uint8_t* x;     // e4m3 [rows, K] activations: token rows (gate/up) or pick rows (down)
   const uint8_t* xs;    // codes [rows, K / 32]
   int x_by_pick;        // 1: x rows are natural pick indices; 0: token rows (pick / topk)
@@ -236,203 +235,6 @@ struct ExpertArgs {
   const int32_t* picks;
   float* out;           // [kslices][M * topk][N] fp32 partials, by natural pick index
 };
-
-constexpr int kExpMaxPicks = 16;  // picks staged at once (n-tiles <= 2); more loop over the weights
-
-constexpr int kExpRing = 6;        // weight-stream positions in flight a warp
-// bytes a ring slot: 32 lanes x (2 x 16 B weights + 8 B codes)
-constexpr int kExpSlot = 32 * 40;
-
-__host__ __device__ inline int expert_ring_offset(int ks_len) {
-  return (kExpMaxPicks * (ks_len + 8) * 2 + kExpMaxPicks * (ks_len / 32) * 4 + 127) / 128 * 128;
-}
-__host__ __device__ inline int expert_smem_bytes(int ks_len) {
-  return expert_ring_offset(ks_len) + 8 * kExpRing * kExpSlot;
-}
-
-// One 128-K step of a 16-row tile against NT pick tiles: 4 E8M0 blocks x 2 k16 halves.
-template <int NT>
-__device__ __forceinline__ void expert_step(const uint4& A0, const uint4& A1, const uint2& cw, int s,
-                                            uint32_t xs_base, uint32_t lm, int xs_ld, const float* sx,
-                                            int sx_ld, float (&acc)[2][4], int lane) {
-  const int t = lane & 3;
-  const uint32_t words[8] = {A0.x, A0.y, A0.z, A0.w, A1.x, A1.y, A1.z, A1.w};
-#pragma unroll
-  for (int b = 0; b < 4; ++b) {
-    const uint32_t cws = b < 2 ? cw.x : cw.y;
-    const float sw0 = pow2c((cws >> (16 * (b & 1))) & 0xff);
-    const float sw1 = pow2c((cws >> (16 * (b & 1) + 8)) & 0xff);
-    float blk[NT][4];
-#pragma unroll
-    for (int n = 0; n < NT; ++n)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) blk[n][i] = 0.f;
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const uint32_t wd = words[2 * b + j];
-      const uint32_t a0 = e2m1x2_f16(wd & 0xff), a1 = e2m1x2_f16((wd >> 8) & 0xff);
-      const uint32_t a2 = e2m1x2_f16((wd >> 16) & 0xff), a3 = e2m1x2_f16(wd >> 24);
-#pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        uint32_t bb[2];
-        ldmatrix_x2(bb, xs_base + lm + (uint32_t)((n * 8 * xs_ld + s * 128 + 32 * b + 16 * j) * 2));
-        mma_f16(blk[n], a0, a1, a2, a3, bb[0], bb[1]);
-      }
-    }
-#pragma unroll
-    for (int n = 0; n < NT; ++n) {
-      const float sx0 = sx[(n * 8 + 2 * t) * sx_ld + 4 * s + b];
-      const float sx1 = sx[(n * 8 + 2 * t + 1) * sx_ld + 4 * s + b];
-      acc[n][0] = fmaf(blk[n][0], sw0 * sx0, acc[n][0]);
-      acc[n][1] = fmaf(blk[n][1], sw0 * sx1, acc[n][1]);
-      acc[n][2] = fmaf(blk[n][2], sw1 * sx0, acc[n][2]);
-      acc[n][3] = fmaf(blk[n][3], sw1 * sx1, acc[n][3]);
-    }
-  }
-}
-
-// A warp streams its tiles of a work item as one sequence of (tile, 128-K step) positions,
-// kExpRing positions in flight across tile boundaries, landed in a per-warp shared-memory
-// ring by cp.async (each lane copies, then reads back, only its own 40 bytes a position).
-
-template <int NT>
-__device__ __forceinline__ void expert_stream(const ExpertArgs& a, const uint8_t* wbase, const uint8_t* sbase,
-                                              int tiles_mine, int ksteps, size_t tile_stride_w,
-                                              size_t tile_stride_s, uint32_t xs_base, int xs_ld,
-                                              const float* sx, int sx_ld, const int* picks, int np,
-                                              int row_of_tile0, int lane, uint32_t ring) {
-  const int g = lane >> 2, t = lane & 3;
-  const uint32_t lm = ((lane & 7) * xs_ld + 8 * (lane >> 3)) * 2;
-  const int total = tiles_mine * ksteps;
-  // a slot: the lanes' first 16 B, their second 16 B, then their 8 code bytes (bank-conflict
-  // free: a lane's reads are consecutive across the warp)
-  const uint32_t w0 = ring + 16 * lane, w1 = ring + 512 + 16 * lane, cb = ring + 1024 + 8 * lane;
-  int f_ti = 0, f_st = 0, f_slot = 0;  // the next position to fetch
-  auto fetch = [&](bool live) {
-    if (live) {
-      const uint8_t* wt = wbase + f_ti * tile_stride_w + (size_t)f_st * 1024;
-      const uint32_t so = (uint32_t)(f_slot * kExpSlot);
-      cp_async16_stream(w0 + so, wt + 16 * lane);
-      cp_async16_stream(w1 + so, wt + 512 + 16 * lane);
-      cp_async8(cb + so, sbase + f_ti * tile_stride_s + (size_t)f_st * 64 + 8 * g);
-      if (++f_st == ksteps) {
-        f_st = 0;
-        ++f_ti;
-      }
-      if (++f_slot == kExpRing) f_slot = 0;
-    }
-    cp_async_commit();  // an empty group past the end keeps the wait count uniform
-  };
-#pragma unroll
-  for (int i = 0; i < kExpRing - 1; ++i) fetch(i < total);
-  float acc[2][4];
-#pragma unroll
-  for (int n = 0; n < 2; ++n)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) acc[n][i] = 0.f;
-  int ti = 0, st = 0, slot = 0;
-  for (int p = 0; p < total; ++p) {
-    {
-      fetch(p + kExpRing - 1 < total);
-      cp_async_wait<kExpRing - 1>();  // position p's group has landed
-      const uint32_t so = (uint32_t)(slot * kExpSlot);
-      const uint4 A0 = lds16(w0 + so), A1 = lds16(w1 + so);
-      const uint2 cw = lds8(cb + so);
-      if (++slot == kExpRing) slot = 0;
-      expert_step<NT>(A0, A1, cw, st, xs_base, lm, xs_ld, sx, sx_ld, acc, lane);
-      if (st == ksteps - 1) {
-        const int row0 = row_of_tile0 + ti * 8 * 16;
-#pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int r = n * 8 + 2 * t + (q & 1);
-            if (r < np) a.out[(size_t)picks[r] * a.N + row0 + g + 8 * (q >> 1)] = acc[n][q];
-            acc[n][q] = 0.f;
-          }
-      }
-      if (++st == ksteps) {
-        st = 0;
-        ++ti;
-      }
-    }
-  }
-  cp_async_wait<0>();
-}
-
-// Persistent: a fixed grid loops over work items (union slot u, K slice, row group); the row
-// groups per (u, K slice) are chosen on the device from the step's union so every CTA has
-// about two items. Each item stages its picks' activations once (e4m3 -> f16, exact), then
-// its 8 warps stream the group's row tiles. out: [kslices][M topk][N] by natural pick index.
-__global__ void __launch_bounds__(256, 2) expert_gemv_kernel(const ExpertArgs a) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ int s_picks[kExpMaxPicks];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  pdl_wait();
-  const int nu = *a.n_u;
-  const int tiles = a.N / 16;
-  const int pairs = nu * a.kslices;
-  if (pairs == 0) return;
-  const int RG = max(1, min(cdiv(2 * (int)gridDim.x, pairs), cdiv(tiles, 8)));
-  const int tiles_per = cdiv(tiles, RG);
-  const int items = pairs * RG;
-  const int xs_ld = a.ks_len + 8;
-  __half* xs = reinterpret_cast<__half*>(smem);
-  float* sx = reinterpret_cast<float*>(smem + kExpMaxPicks * xs_ld * 2);
-  const int sx_ld = a.ks_len / 32;
-  const size_t kt_count = a.K / 128;
-  const uint32_t ring = smem_u32(smem) + expert_ring_offset(a.ks_len) + warp * kExpRing * kExpSlot;
-  for (int item = blockIdx.x; item < items; item += gridDim.x) {
-    const int rg = item % RG, pair = item / RG;
-    const int ks = pair % a.kslices, u = pair / a.kslices;
-    const int e = a.u_expert[u];
-    const int p0 = a.u_off[u], np_all = a.u_off[u + 1] - p0;
-    const int k0 = ks * a.ks_len, klen = min(a.ks_len, a.K - k0);
-    const int tile_lo = rg * tiles_per, tile_hi = min(tiles, tile_lo + tiles_per);
-    const int tiles_mine = tile_lo + warp < tile_hi ? cdiv(tile_hi - tile_lo - warp, 8) : 0;
-    const uint8_t* wbase = a.w + (((size_t)e * tiles + tile_lo + warp) * kt_count + k0 / 128) * 1024;
-    const uint8_t* sbase = a.ws + (((size_t)e * tiles + tile_lo + warp) * kt_count + k0 / 128) * 64;
-    float* out = a.out + (size_t)ks * a.M * a.topk * a.N;
-    for (int pb = 0; pb < np_all; pb += kExpMaxPicks) {
-      const int np = min(kExpMaxPicks, np_all - pb);
-      const int npad = (np + 7) / 8 * 8;
-      __syncthreads();  // the previous item's readers are done with the staging buffers
-      if (threadIdx.x < kExpMaxPicks) s_picks[threadIdx.x] = threadIdx.x < np ? a.picks[p0 + pb + threadIdx.x] : 0;
-      for (int i = threadIdx.x; i < npad * (klen / 4); i += blockDim.x) {
-        const int r = i / (klen / 4), q = i % (klen / 4);
-        uint32_t v = 0;
-        if (r < np) {
-          const int pick = a.picks[p0 + pb + r];
-          const int row = a.x_by_pick ? pick : pick / a.topk;
-          v = *reinterpret_cast<const uint32_t*>(a.x + (size_t)row * a.K + k0 + 4 * q);
-        }
-        *reinterpret_cast<uint2*>(xs + r * xs_ld + 4 * q) = make_uint2(e4m3x2_f16(v & 0xffff), e4m3x2_f16(v >> 16));
-      }
-      for (int i = threadIdx.x; i < npad * sx_ld; i += blockDim.x) {
-        const int r = i / sx_ld, b = i % sx_ld;
-        float v = 0.f;
-        if (r < np && b < klen / 32) {
-          const int pick = a.picks[p0 + pb + r];
-          const int row = a.x_by_pick ? pick : pick / a.topk;
-          v = pow2c(a.xs[(size_t)row * (a.K / 32) + k0 / 32 + b]);
-        }
-        sx[r * sx_ld + b] = v;
-      }
-      __syncthreads();
-      ExpertArgs ao = a;
-      ao.out = out;
-      const uint32_t xb = smem_u32(xs);
-      const size_t tsw = (size_t)8 * kt_count * 1024, tss = (size_t)8 * kt_count * 64;
-      if (npad <= 8)
-        expert_stream<1>(ao, wbase, sbase, tiles_mine, klen / 128, tsw, tss, xb, xs_ld, sx, sx_ld, s_picks, np,
-                         (tile_lo + warp) * 16, lane, ring);
-      else
-        expert_stream<2>(ao, wbase, sbase, tiles_mine, klen / 128, tsw, tss, xb, xs_ld, sx, sx_ld, s_picks, np,
-                         (tile_lo + warp) * 16, lane, ring);
-    }
-  }
-  pdl_launch();
-}
 
 // ------------------------------------------------------------------ routed activation
 struct ExpertActArgs {

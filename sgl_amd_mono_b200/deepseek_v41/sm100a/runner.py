@@ -2,7 +2,7 @@
 launches through the C-ABI (the role of the reference's ``gfx950/runner.py:250-728``).
 
 Weights are read in place (row-major FP8 dense projections, bf16 router, fp32 mHC weights);
-the routed experts get one logged copy in the kernels' MXFP4 fragment order. Activations and
+the routed experts get one logged copy in the kernels' MXFP4 tensor-core tile order. Activations and
 scratch belong to the runner and are allocated per width outside graph capture
 (``buffers``); every launch goes on the current stream, so a step can be captured in a CUDA
 graph and replayed. Host-side argument errors raise ``RuntimeError``; a launch's negative
@@ -104,13 +104,14 @@ class MonoRunner:
             _check(w[k], k, shape, dt, d)
         r = {}
         for name, (src, codes, N, K) in {"w13": ("w13", "s13", 2 * Il, H), "w2": ("w2", "s2", H, Il)}.items():
-            dst = torch.empty(E * N * K // 2, dtype=torch.uint8, device=d)
-            dcodes = torch.empty(E * N * K // 32, dtype=torch.uint8, device=d)
+            rows = (N + 127) // 128 * 128  # whole 128-row tensor-core tiles
+            dst = torch.empty(E * rows * K // 2, dtype=torch.uint8, device=d)
+            dcodes = torch.empty(E * rows * K // 32, dtype=torch.uint8, device=d)
             a = abi.RelayoutArgs(src=_p(w[src]), src_codes=_p(w[codes]), dst=_p(dst), dst_codes=_p(dcodes),
                                  E=E, N=N, K=K)
             ext.call("dsv41_relayout_mxfp4", a, _stream())
             r[name], r[name + "_codes"] = dst, dcodes
-            self.copies[("mxfp4 fragment relayout", tag, name)] = (dst, dcodes)
+            self.copies[("mxfp4 tensor-core tile relayout", tag, name)] = (dst, dcodes)
         return Layer(w, r)
 
     # ------------------------------------------------------------ buffers

@@ -18,7 +18,7 @@ launches of ``sm100a``), the head's combine and norm, and SGLang's logits proces
 The kernels read SGLang's weights in place, except the copies logged in ``ctx.copies``: each
 covered layer's FP8 shared expert (this rank's shard, kept at load), the E8M0 codes of the
 power-of-two fp32 block scales, the f32 router bias and attention sinks, the RoPE table, and
-the routed experts in the kernels' MXFP4 fragment order.
+the routed experts in the kernels' MXFP4 tensor-core tile order.
 """
 
 from __future__ import annotations

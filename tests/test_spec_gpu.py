@@ -156,7 +156,7 @@ def test_target_forward_two_layers(fake_sglang):
         _load_shared(spec.SPEC.load_tensor, copies, wd["lm"], _to(w, DEV), f"layers.{i}", wd["s"])
     assert spec.SPEC.model_disable_reasons(wd["lm"], wd["hf"], copies) == []
     built = spec.SPEC.build(wd["lm"], wd["hf"], SimpleNamespace(copies=copies, deadline_s=5.0, widths=range(1, 49)))
-    assert any(k[0] == "mxfp4 fragment relayout" for k in copies) and ("e8m0 scale codes", 0, "wq_b") in copies
+    assert any(k[0] == "mxfp4 tensor-core tile relayout" for k in copies) and ("e8m0 scale codes", 0, "wq_b") in copies
     plan = SimpleNamespace(state={}, key=SimpleNamespace(tokens_per_request=1))
     ids = wd["ids"].to(DEV)
     hidden, _ = built.backbone(plan, ids, wd["positions"], None, None)
