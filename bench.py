@@ -40,6 +40,10 @@ import torch  # noqa: E402
 
 METRIC = "decode tokens/s (one config-2 MoE decode layer, K1 + K2)"
 UNIT = "tokens/s"
+# DRAM bytes (read + write) of the routed-expert stage's two expert_tc_kernel launches per expert
+# of the routing union, from one ncu capture (M = 48, ctx 2048, one layer, union 199: gate/up
+# 1.774859 GB + 27.11 MB, down 0.887746 GB + 14.77 MB).
+EXPERT_DRAM_BYTES_PER_UNIT = (1.774859e9 + 27.109376e6 + 0.887746e9 + 14.774784e6) / 199
 
 
 def parse():
@@ -406,7 +410,10 @@ def run_ours(args, world, rank, local):
                        "stages_us": {k: round(v * 1e3, 2) for k, v in stage_ms.items()}},
             "roofline": {"bound": "hbm", "kernel": "routed experts (gate/up + act + down)",
                          "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-                         "frac": round(achieved / hbm_peak, 4), "traffic": None,
+                         "frac": round(achieved / hbm_peak, 4),
+                         "traffic": int(union * EXPERT_DRAM_BYTES_PER_UNIT),
+                         "traffic_source": "ncu dram bytes of the stage's two expert_tc_kernel launches "
+                                           "(M 48, ctx 2048, union 199) per expert, scaled to this run's union",
                          "algorithmic_bytes": int(exp_bytes), "peak_source": peak_src},
             "cpu_baseline": cpu,
             "e2e": {"value": round(M / (e2e_ms * 1e-3), 1), "unit": UNIT,

@@ -249,7 +249,7 @@ typedef struct {
 int dsv41_argmax_decode(const Dsv41ArgmaxArgs* a, void* stream);
 
 /* DSV41_EDEVICE once a kernel's bounded internal wait gave up in this process (the tcgen05
- * attention's pipeline barriers; sticky), else 0. Synchronizes with the device. */
+ * attention's and the routed experts' pipeline barriers; sticky), else 0. Synchronizes with the device. */
 int dsv41_device_error(void);
 
 /* Kernels this library has launched in this process (all entry points): for profiling. */
