@@ -115,13 +115,14 @@ EncodeTiledFn encode_tiled() {
 }
 
 // The tensor map of a relayout expert weight: `tiles` 128-row x 128-K tiles of packed e2m1 (8 KB
-// each), read as unpacked FP4 (16U4_ALIGN16B) with the 128-byte swizzle, one tile a copy.
+// each), read as unpacked FP4 (16U4_ALIGN16B) with the 128-byte swizzle, kMxDepth consecutive tiles
+// a copy.
 bool expert_weight_map(CUtensorMap* m, const void* w, int64_t tiles) {
   EncodeTiledFn enc = encode_tiled();
   if (!enc || !w || reinterpret_cast<uintptr_t>(w) % 32) return false;
   const cuuint64_t dims[3] = {128, 128, (cuuint64_t)tiles};
   const cuuint64_t strides[2] = {64, 8192};
-  const cuuint32_t box[3] = {128, 128, 1};
+  const cuuint32_t box[3] = {128, 128, kMxDepth};
   const cuuint32_t es[3] = {1, 1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<void*>(w), dims, strides, box, es,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

@@ -17,8 +17,9 @@
 // the MMAs (one thread), warps 2-5 stage each pick batch's activations (e4m3, K-major core
 // matrices) and scale codes, and drain the accumulators. Work item = (expert of the union,
 // K slice, group of row tiles); a batch = up to 32 of the expert's picks; N of the MMA = the
-// batch's picks rounded up to 8, 16 or 32. Pipelines: an 8-stage weight ring (full: TMA
-// transaction bytes; empty: MMA commit), two activation buffers (ready: the stagers; free:
+// batch's picks rounded up to 8, 16 or 32. Pipelines: a 4-stage weight ring of two K steps a
+// stage (one 16 KB TMA request: 8 KB requests stream at ~4.1 TB/s over 148 SMs, 16 KB ones at
+// ~6.1; full: TMA transaction bytes; empty: MMA commit), two activation buffers (ready: the stagers; free:
 // MMA commit), two accumulators (full: MMA commit; empty: the drainers). Every wait is
 // bounded; a timeout sets the device error word and unwinds every role.
 #pragma once
@@ -30,7 +31,8 @@
 
 namespace dsv41 {
 
-constexpr int kMxStages = 8;
+constexpr int kMxStages = 4;
+constexpr int kMxDepth = 2;    // K steps (128-K tiles) a stage: one 16 KB TMA request
 constexpr int kMxThreads = 192;
 constexpr int kMxMaxPicks = 32;
 constexpr int kMxKsMax = 1024;  // K slice bound (activation staging bytes a pick)
@@ -51,9 +53,10 @@ struct ExpertTcArgs {
 };
 
 struct MxSmem {
-  static constexpr int kA = 0;                                 // stages x 16 KB (1024-aligned)
-  static constexpr int kSfa = kMxStages * 16384;               // stages x 512
-  static constexpr int kB = kSfa + kMxStages * 512;            // 2 x [32 picks][kMxKsMax]
+  static constexpr int kStage = kMxDepth * 16384;
+  static constexpr int kA = 0;                                 // stages x depth x 16 KB (1024-aligned)
+  static constexpr int kSfa = kMxStages * kStage;              // stages x depth x 512
+  static constexpr int kB = kSfa + kMxStages * kMxDepth * 512; // 2 x [32 picks][kMxKsMax]
   static constexpr int kBBytes = kMxMaxPicks * kMxKsMax;
   static constexpr int kSfb = kB + 2 * kBBytes;                // 2 x [K step][32 lanes][16 B]
   static constexpr int kSfbBytes = (kMxKsMax / 128) * 512;
@@ -91,6 +94,7 @@ __device__ __forceinline__ void mx_cp_sf(uint32_t tmem_col, uint32_t saddr) {
 __device__ __forceinline__ void mx_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
+// kMxDepth consecutive tiles (K steps) from `tile` on; tiles past the map read as zeros
 __device__ __forceinline__ void mx_tma_tile(uint32_t dst, const CUtensorMap* map, int tile, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
@@ -187,7 +191,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_base;
-  // TMEM columns: accumulators 0, 32 (up to 32 picks); weight scales 64 + 4 stage; activation
+  // TMEM columns: accumulators 0, 32 (up to 32 picks); weight scales 64 + 4 (stage, K step); activation
   // scales 128 + 32 buffer + 4 K step (a scale operand starts on a 4-column boundary: the
   // 32-lane x 4-column atom of tcgen05.cp.32x128b)
   const uint32_t t_d = tmem, t_sfa = tmem + 64, t_sfb = tmem + 128;
@@ -204,16 +208,17 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       for (bool live = w.start(a, nu, gridDim.x, blockIdx.x); live; live = w.next(a)) {
         bool ok = true;
         for (int t = w.tile_lo; ok && t < w.tile_hi; ++t)
-          for (int s = 0; s < ksteps; ++s, ++c) {
+          for (int s = 0; s < ksteps; s += kMxDepth, ++c) {
             const int st = c % kMxStages;
             if (c >= kMxStages && !mbar_wait(empty(st), ((c / kMxStages) - 1) & 1, abort)) {
               ok = false;
               break;
             }
+            const int nk = min(kMxDepth, ksteps - s);  // K steps of this slice in the stage
             const int tile = ((w.e * a.rtiles + t) * (a.K / 128)) + w.ks * ksteps + s;
-            mx_expect_tx(full(st), 8192 + 512);
-            mx_tma_tile(smem_u32(smem + L::kA + st * 16384), &wmap, tile, full(st));
-            mx_bulk(smem_u32(smem + L::kSfa + st * 512), a.ws + (size_t)tile * 512, 512, full(st));
+            mx_expect_tx(full(st), kMxDepth * 8192 + nk * 512);
+            mx_tma_tile(smem_u32(smem + L::kA + st * L::kStage), &wmap, tile, full(st));
+            mx_bulk(smem_u32(smem + L::kSfa + st * kMxDepth * 512), a.ws + (size_t)tile * 512, nk * 512, full(st));
           }
         if (!ok) break;
       }
@@ -239,17 +244,21 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           const int dd = ti & 1;
           if (ti >= 2 && !(ok = mbar_wait(d_empty(dd), ((ti >> 1) - 1) & 1, abort))) break;
           tc_fence_after();
-          for (int s = 0; s < ksteps; ++s, ++c) {
+          for (int s0 = 0; s0 < ksteps; s0 += kMxDepth, ++c) {
             const int st = c % kMxStages;
             if (!(ok = mbar_wait(full(st), (c / kMxStages) & 1, abort))) break;
             tc_fence_after();
-            mx_cp_sf(t_sfa + 4 * st, smem_u32(smem + L::kSfa + st * 512));
-            const uint32_t sa = smem_u32(smem + L::kA + st * 16384);
+            const int nk = min(kMxDepth, ksteps - s0);
+            for (int j = 0; j < nk; ++j) {
+              const int s = s0 + j, slot = st * kMxDepth + j;
+              mx_cp_sf(t_sfa + 4 * slot, smem_u32(smem + L::kSfa + slot * 512));
+              const uint32_t sa = smem_u32(smem + L::kA + st * L::kStage + j * 16384);
 #pragma unroll
-            for (int b = 0; b < 4; ++b) {
-              const uint64_t db = umma_sdesc(sb + (8 * s + 2 * b) * 128, 128, (a.ks_len / 16) * 128);
-              mx_mma(t_d + 32 * dd, mx_sdesc_sw128(sa + 32 * b), db, mx_idesc(N, b), s > 0 || b > 0,
-                     (t_sfa + 4 * st) | ((uint32_t)b << 30), (t_sfb + 32 * bb + 4 * s) | ((uint32_t)b << 30));
+              for (int b = 0; b < 4; ++b) {
+                const uint64_t db = umma_sdesc(sb + (8 * s + 2 * b) * 128, 128, (a.ks_len / 16) * 128);
+                mx_mma(t_d + 32 * dd, mx_sdesc_sw128(sa + 32 * b), db, mx_idesc(N, b), s > 0 || b > 0,
+                       (t_sfa + 4 * slot) | ((uint32_t)b << 30), (t_sfb + 32 * bb + 4 * s) | ((uint32_t)b << 30));
+              }
             }
             umma_commit(empty(st));
           }
