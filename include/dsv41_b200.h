@@ -57,11 +57,12 @@ int dsv41_gemv_fp8_noalloc(const Dsv41GemvArgs* a, void* stream);
 /* ---------------------------------------------------------------- MXFP4 expert relayout
  * One-time copy of routed-expert weights from the checkpoint layout -- w [E, N, K/2] E2M1
  * (even K in the low nibble) with E8M0 codes [E, N, K/32] -- into the tensor-core tiles the
- * expert kernel streams: dst [E][ceil(N/128)][K/128][128 rows][64 B] (rows past N zero),
- * dst_codes [E][ceil(N/128)][K/128][512 B] with row r's code of K block b at
- * (r % 32) * 16 + (r / 32) * 4 + b. dst holds E * ceil(N/128) * 128 * K/2 bytes, dst_codes
- * E * ceil(N/128) * 128 * K/32. N % 16 == 0, K % 128 == 0; src, dst 16-byte aligned (dst
- * 32-byte aligned for the kernels' tensor maps), codes 4-byte aligned.
+ * expert kernel streams: dst [E][ceil(N/256)][K/128][256 rows][64 B] (rows past N zero),
+ * dst_codes [E][ceil(N/256)][K/128][1024 B]: two 512-byte atoms (rows 0..127, 128..255), row r's
+ * code of K block b at (r / 128) * 512 + (r % 32) * 16 + ((r % 128) / 32) * 4 + b. dst holds
+ * E * ceil(N/256) * 256 * K/2 bytes, dst_codes E * ceil(N/256) * 256 * K/32. N % 16 == 0,
+ * K % 128 == 0; src, dst 16-byte aligned (dst 32-byte aligned for the kernels' tensor maps),
+ * codes 4-byte aligned.
  * Replaces the reader of aiter's shuffle_weight / shuffle_scale layout (common/mx.py:35-50,
  * stages/moe.py:567-607); the runner logs the copy as the reference logs its copies
  * (deepseek_v41/spec.py:34-41). */

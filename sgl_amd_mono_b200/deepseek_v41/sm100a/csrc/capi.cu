@@ -114,15 +114,14 @@ EncodeTiledFn encode_tiled() {
   return fn;
 }
 
-// The tensor map of a relayout expert weight: `tiles` 128-row x 128-K tiles of packed e2m1 (8 KB
-// each), read as unpacked FP4 (16U4_ALIGN16B) with the 128-byte swizzle, kMxDepth consecutive tiles
-// a copy.
+// The tensor map of a relayout expert weight: `tiles` 256-row x 128-K tiles of packed e2m1 (16 KB
+// each), read as unpacked FP4 (16U4_ALIGN16B) with the 128-byte swizzle, one tile a copy.
 bool expert_weight_map(CUtensorMap* m, const void* w, int64_t tiles) {
   EncodeTiledFn enc = encode_tiled();
   if (!enc || !w || reinterpret_cast<uintptr_t>(w) % 32) return false;
-  const cuuint64_t dims[3] = {128, 128, (cuuint64_t)tiles};
-  const cuuint64_t strides[2] = {64, 8192};
-  const cuuint32_t box[3] = {128, 128, kMxDepth};
+  const cuuint64_t dims[3] = {128, kMxRows, (cuuint64_t)tiles};
+  const cuuint64_t strides[2] = {64, 64 * kMxRows};
+  const cuuint32_t box[3] = {128, kMxRows, 1};
   const cuuint32_t es[3] = {1, 1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<void*>(w), dims, strides, box, es,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -435,7 +434,7 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   const int max_units = std::min(E, P);
   ExpertArgs eu = {};
   eu.M = M; eu.topk = TK; eu.N = 2 * I; eu.K = H; eu.ks_len = std::min(H, 1024);
-  eu.kslices = cdiv(H, eu.ks_len); eu.row_groups = 2 * I / 128; eu.max_units = max_units;
+  eu.kslices = cdiv(H, eu.ks_len); eu.row_groups = cdiv(2 * I, kMxRows); eu.max_units = max_units;
   eu.w = ptr<const uint8_t>(a->w13); eu.ws = ptr<const uint8_t>(a->w13_codes);
   eu.x = x8r; eu.xs = x8rs; eu.x_by_pick = 0;
   eu.n_u = n_u; eu.u_expert = u_expert; eu.u_off = u_off; eu.picks = picks;
@@ -444,7 +443,7 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   auto* mids = c.take<uint8_t>((int64_t)P * I / 32);
   ExpertArgs ed = eu;
   ed.N = H; ed.K = I; ed.ks_len = std::min(I, 1024); ed.kslices = cdiv(I, ed.ks_len);
-  ed.row_groups = H / 128; ed.w = ptr<const uint8_t>(a->w2); ed.ws = ptr<const uint8_t>(a->w2_codes);
+  ed.row_groups = cdiv(H, kMxRows); ed.w = ptr<const uint8_t>(a->w2); ed.ws = ptr<const uint8_t>(a->w2_codes);
   ed.x = mid; ed.xs = mids; ed.x_by_pick = 1;
   ed.out = c.take<float>((int64_t)ed.kslices * P * H);
   auto* moe_part = a->moe_part ? ptr<__nv_bfloat16>(a->moe_part) : c.take<__nv_bfloat16>((int64_t)M * H);
@@ -538,14 +537,14 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   // ---- routed experts: persistent tcgen05 grouped GEMMs, one CTA an SM
   {
     CUtensorMap m13, m2;
-    if (!expert_weight_map(&m13, ptr<const void>(a->w13), (int64_t)E * (2 * I / 128) * (H / 128)) ||
-        !expert_weight_map(&m2, ptr<const void>(a->w2), (int64_t)E * (H / 128) * (I / 128))) {
+    if (!expert_weight_map(&m13, ptr<const void>(a->w13), (int64_t)E * eu.row_groups * (H / 128)) ||
+        !expert_weight_map(&m2, ptr<const void>(a->w2), (int64_t)E * ed.row_groups * (I / 128))) {
       fprintf(stderr, "dsv41: expert weight tensor map failed (driver entry point or alignment)\n");
       return DSV41_ELAUNCH;
     }
-    const ExpertTcArgs tu = {M, TK, 2 * I, H, eu.kslices, eu.ks_len, 2 * I / 128, eu.ws, eu.x, eu.xs, 0,
+    const ExpertTcArgs tu = {M, TK, 2 * I, H, eu.kslices, eu.ks_len, eu.row_groups, eu.ws, eu.x, eu.xs, 0,
                              n_u, u_expert, u_off, picks, eu.out};
-    const ExpertTcArgs td = {M, TK, H, I, ed.kslices, ed.ks_len, H / 128, ed.ws, ed.x, ed.xs, 1,
+    const ExpertTcArgs td = {M, TK, H, I, ed.kslices, ed.ks_len, ed.row_groups, ed.ws, ed.x, ed.xs, 1,
                              n_u, u_expert, u_off, picks, ed.out};
     DSV41_TRY(launch2(expert_tc_kernel, dim3(std::min(sms, max_units * eu.kslices * eu.row_groups)),
                       dim3(kMxThreads), MxSmem::kBytes, st, m13, tu));

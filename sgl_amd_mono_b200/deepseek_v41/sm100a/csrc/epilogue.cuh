@@ -59,39 +59,40 @@ __global__ void finalize_kernel(const FinalizeArgs a) {
 }
 
 // MXFP4 weight [E][N][K/2] (even K in the low nibble) + E8M0 [E][N][K/32] -> the tensor-core
-// tiles of expert_tc_kernel: tile (e, rt, kt) = 128 rows x 128 K at ((e RT + rt) KT + kt) 8192,
-// RT = ceil(N / 128), KT = K / 128; its row r holds source row 128 rt + r, bytes 64 kt ..
-// 64 kt + 63 (zero past N). Codes: 512 bytes a tile, row r's code of K block 4 kt + b at
-// (r % 32) * 16 + (r / 32) * 4 + b (the TMEM scale-atom order). 16 bytes (4 code bytes) a step.
+// tiles of expert_tc_kernel: tile (e, rt, kt) = 256 rows x 128 K at ((e RT + rt) KT + kt) 16384,
+// RT = ceil(N / 256), KT = K / 128; its row r holds source row 256 rt + r, bytes 64 kt ..
+// 64 kt + 63 (zero past N). Codes: 1024 bytes a tile, two TMEM scale atoms (rows 0..127, then
+// 128..255); row r's code of K block 4 kt + b at (r / 128) * 512 + (r % 32) * 16 +
+// ((r % 128) / 32) * 4 + b. 16 bytes (4 code bytes) a step.
 __global__ void relayout_mxfp4_kernel(const uint8_t* __restrict__ src, const uint8_t* __restrict__ src_codes,
                                       uint8_t* __restrict__ dst, uint8_t* __restrict__ dst_codes,
                                       int64_t E, int N, int K) {
-  const int RT = (N + 127) / 128, KT = K / 128;
+  const int RT = (N + 255) / 256, KT = K / 128;
   const int64_t tiles = E * RT * KT;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < tiles * 512; i += stride) {
-    const int64_t tile = i / 512;
-    const int within = (int)(i % 512) * 16;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < tiles * 1024; i += stride) {
+    const int64_t tile = i / 1024;
+    const int within = (int)(i % 1024) * 16;
     const int r = within / 64, cb = within % 64;
     const int kt = (int)(tile % KT);
     const int rt = (int)((tile / KT) % RT);
     const int64_t ex = tile / ((int64_t)KT * RT);
-    const int row = 128 * rt + r;
+    const int row = 256 * rt + r;
     uint4 v = make_uint4(0, 0, 0, 0);
     if (row < N) v = *reinterpret_cast<const uint4*>(src + (ex * N + row) * (int64_t)(K / 2) + 64 * kt + cb);
     *reinterpret_cast<uint4*>(dst + i * 16) = v;
   }
-  for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < tiles * 128; j += stride) {
-    const int64_t tile = j / 128;
-    const int q = (int)(j % 128);  // (r % 32) * 4 + r / 32
-    const int r = q / 4 + 32 * (q % 4);
+  for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < tiles * 256; j += stride) {
+    const int64_t tile = j / 256;
+    const int q = (int)(j % 256);  // (r / 128) * 128 + (r % 32) * 4 + (r % 128) / 32
+    const int r = 128 * (q / 128) + (q % 128) / 4 + 32 * (q % 4);
     const int kt = (int)(tile % KT);
     const int rt = (int)((tile / KT) % RT);
     const int64_t ex = tile / ((int64_t)KT * RT);
-    const int row = 128 * rt + r;
+    const int row = 256 * rt + r;
     uint32_t v = 0;
     if (row < N) v = *reinterpret_cast<const uint32_t*>(src_codes + (ex * N + row) * (int64_t)(K / 32) + 4 * kt);
-    *reinterpret_cast<uint32_t*>(dst_codes + tile * 512 + 4 * q) = v;
+    *reinterpret_cast<uint32_t*>(dst_codes + tile * 1024 + 4 * q) = v;
   }
 }
 

@@ -7,7 +7,7 @@
 // to fp32; scores use the deterministic fp64 softplus (detmath.cuh); the top-k takes the
 // largest (score + bias), ties to the lower expert id.
 //
-// Routed experts (moe_tc.cuh) run on a one-time relayout of the MXFP4 weights into 128-row x
+// Routed experts (moe_tc.cuh) run on a one-time relayout of the MXFP4 weights into 256-row x
 // 128-K tensor-core tiles (logged by the runner): tcgen05 block-scaled MMAs of e2m1 weights and
 // e4m3 activations with their E8M0 codes.
 #pragma once
@@ -222,10 +222,10 @@ __global__ void __launch_bounds__(512) moe_plan_kernel(const PlanArgs a) {
 struct ExpertArgs {
   int M, topk, N, K;   // N rows of the expert matrix (2 I for gate/up, H for down), K
   int kslices, ks_len;  // K slices (ks_len a multiple of 128)
-  int row_groups;       // 128-row tiles of N
+  int row_groups;       // 256-row tiles of N
   int max_units;        // union slots (min(E, M topk))
-  const uint8_t* w;     // tensor-core tiles [E][N/128][K/128][128][64]
-  const uint8_t* ws;    // codes [E][N/128][K/128][512]
+  const uint8_t* w;     // tensor-core tiles [E][N/256][K/128][256][64]
+  const uint8_t* ws;    // codes [E][N/256][K/128][1024]
   const uint8_t* x;     // e4m3 [rows, K] activations: token rows (gate/up) or pick rows (down)
   const uint8_t* xs;    // codes [rows, K / 32]
   int x_by_pick;        // 1: x rows are natural pick indices; 0: token rows (pick / topk)

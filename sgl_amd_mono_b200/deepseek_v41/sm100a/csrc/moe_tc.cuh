@@ -1,26 +1,32 @@
 // Routed experts on the 5th-generation tensor cores: the grouped MXFP4 x MXFP8 GEMM of
 // stages/moe.py (gate/up over the expert union's token rows, down over the picks' MXFP8
-// activations) as tcgen05.mma.kind::mxf8f6f4.block_scale -- e2m1 weights times e4m3
-// activations with their E8M0 block scales (one per 32 K) applied inside the MMA, fp32
-// accumulation in TMEM.
+// activations) as tcgen05.mma.kind::mxf8f6f4.block_scale -- e4m3 activations times e2m1 weights
+// with their E8M0 block scales (one per 32 K) applied inside the MMA, fp32 accumulation in TMEM.
 //
-// Weights (one-time relayout, relayout_mxfp4_kernel): 128-row x 128-K tiles of packed e2m1,
-// [E][ceil(N / 128)][K / 128][128 rows][64 B] (even K in the low nibble; rows past N zero),
-// each tile 8 KB contiguous; their codes in the TMEM scale-atom order, [E][rtiles][K / 128]
-// [512 B] with row m's code of K block b at (m % 32) * 16 + (m / 32) * 4 + b. A TMA tensor
-// copy (CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 128-byte swizzle) lands a tile in shared memory
-// as the MMA's unpacked FP4 operand (each 8 bytes of 16 values followed by an 8-byte gap),
-// K-major with the 128-byte swizzle; a bulk copy brings the 512 code bytes, and
-// tcgen05.cp.32x128b.warpx4 replicates them into the four TMEM sub-partitions.
+// Operands: A = the batch's picks' activations (M = 128 rows, of which the first np are real),
+// B = 256 rows of the expert's weights (N = 256): one MMA covers 256 weight rows x 32 K in ~135
+// cycles, against ~119 cycles for 128 rows with the weights as A (the instruction's floor), so
+// the MMA keeps ahead of HBM. A is staged in shared memory as K-major core matrices of only the
+// real 8-row groups; the MMA reads all 16 groups, and the rows past np read whatever shared
+// memory follows (the activation buffers sit in front of the weight ring, so every such read
+// stays inside the CTA's allocation); those accumulator rows are never stored.
 //
-// CTA (persistent): warp 0 issues the copies (one thread), warp 1 allocates TMEM and issues
-// the MMAs (one thread), warps 2-5 stage each pick batch's activations (e4m3, K-major core
-// matrices) and scale codes, and drain the accumulators. Work item = (expert of the union,
-// K slice, group of row tiles); a batch = up to 32 of the expert's picks; N of the MMA = the
-// batch's picks rounded up to 8, 16 or 32. Pipelines: a 4-stage weight ring of two K steps a
-// stage (one 16 KB TMA request: 8 KB requests stream at ~4.1 TB/s over 148 SMs, 16 KB ones at
-// ~6.1; full: TMA transaction bytes; empty: MMA commit), two activation buffers (ready: the stagers; free:
-// MMA commit), two accumulators (full: MMA commit; empty: the drainers). Every wait is
+// Weights (one-time relayout, relayout_mxfp4_kernel): 256-row x 128-K tiles of packed e2m1,
+// [E][ceil(N / 256)][K / 128][256 rows][64 B] (even K in the low nibble; rows past N zero), 16 KB
+// contiguous a tile -- one TMA request (CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 128-byte swizzle:
+// the MMA's unpacked FP4 operand, each 8 bytes of 16 values followed by an 8-byte gap, 32 KB in
+// shared memory). Their codes: 1 KB a tile, two 512-byte TMEM scale atoms (rows 0..127, then
+// 128..255), row m's code of K block b at (m % 32) * 16 + (m / 32) * 4 + b within its atom; a bulk
+// copy brings them and tcgen05.cp.32x128b.warpx4 replicates each atom into the four TMEM
+// sub-partitions (weight row n -> lane n % 32, column n / 32, byte = the K block).
+//
+// CTA (persistent, one an SM): warp 0 issues the copies (one thread), warp 1 allocates TMEM and
+// issues the MMAs (one thread), warps 2-5 stage each pick batch's activations and scale atoms and
+// drain the accumulator (warp w holds picks 32 (w % 4) .. of it). Work item = (expert of the
+// union, K slice, group of 256-row tiles); a batch = up to 32 of the expert's picks. Pipelines: a
+// 4-stage weight ring (full: TMA transaction bytes; empty: MMA commit), two activation buffers
+// (ready: the stagers; free: MMA commit), one accumulator (256 columns; full: MMA commit; empty:
+// the drainers -- TMEM has no room for a second one beside the scale columns). Every wait is
 // bounded; a timeout sets the device error word and unwinds every role.
 #pragma once
 
@@ -32,16 +38,16 @@
 namespace dsv41 {
 
 constexpr int kMxStages = 4;
-constexpr int kMxDepth = 2;    // K steps (128-K tiles) a stage: one 16 KB TMA request
+constexpr int kMxRows = 256;     // weight rows a tile (N of the MMA)
 constexpr int kMxThreads = 192;
 constexpr int kMxMaxPicks = 32;
-constexpr int kMxKsMax = 1024;  // K slice bound (activation staging bytes a pick)
+constexpr int kMxKsMax = 1024;   // K slice bound (activation staging bytes a pick)
 
 struct ExpertTcArgs {
   int M, topk, N, K;       // expert matrix rows N (2 I gate/up, H down), K
   int kslices, ks_len;     // K slices (ks_len a multiple of 128, <= kMxKsMax)
-  int rtiles;              // ceil(N / 128)
-  const uint8_t* ws;       // codes [E][rtiles][K / 128][512] (scale-atom order)
+  int rtiles;              // ceil(N / 256)
+  const uint8_t* ws;       // codes [E][rtiles][K / 128][1024] (two scale atoms)
   const uint8_t* x;        // e4m3 [rows, K]: token rows (gate/up) or pick rows (down)
   const uint8_t* xs;       // codes [rows, K / 32]
   int x_by_pick;           // 1: x rows are pick indices; 0: token rows (pick / topk)
@@ -53,17 +59,18 @@ struct ExpertTcArgs {
 };
 
 struct MxSmem {
-  static constexpr int kStage = kMxDepth * 16384;
-  static constexpr int kA = 0;                                 // stages x depth x 16 KB (1024-aligned)
-  static constexpr int kSfa = kMxStages * kStage;              // stages x depth x 512
-  static constexpr int kB = kSfa + kMxStages * kMxDepth * 512; // 2 x [32 picks][kMxKsMax]
-  static constexpr int kBBytes = kMxMaxPicks * kMxKsMax;
-  static constexpr int kSfb = kB + 2 * kBBytes;                // 2 x [K step][32 lanes][16 B]
-  static constexpr int kSfbBytes = (kMxKsMax / 128) * 512;
-  static constexpr int kPicks = kSfb + 2 * kSfbBytes;          // 2 x int [32]
+  // activation buffers first: the MMA's reads past a batch's real rows land in what follows
+  static constexpr int kABytes = kMxMaxPicks * kMxKsMax;       // [K step][group][8 chunks][8 x 16 B]
+  static constexpr int kA = 0;                                 // 2 buffers
+  static constexpr int kStage = kMxRows * 128;                 // 32 KB: 256 rows x 128 B, swizzled
+  static constexpr int kW = kA + 2 * kABytes;                  // stages (1024-aligned)
+  static constexpr int kSfw = kW + kMxStages * kStage;         // stages x 1 KB weight scale atoms
+  static constexpr int kSfxBytes = (kMxKsMax / 128) * 512;
+  static constexpr int kSfx = kSfw + kMxStages * 1024;         // 2 x [K step][32 lanes][16 B]
+  static constexpr int kPicks = kSfx + 2 * kSfxBytes;          // 2 x int [32]
   static constexpr int kBar = kPicks + 2 * kMxMaxPicks * 4;
-  // bars: full[S], empty[S], b_ready[2], b_free[2], d_full[2], d_empty[2], drain
-  static constexpr int kNumBars = 2 * kMxStages + 9;
+  // bars: full[S], empty[S], b_ready[2], b_free[2], d_full, d_empty, drain
+  static constexpr int kNumBars = 2 * kMxStages + 7;
   static constexpr int kMisc = kBar + kNumBars * 8;            // tmem base, abort flag
   static constexpr int kBytes = kMisc + 16 + 1024;             // + slack to align the base to 1 KB
 };
@@ -73,10 +80,10 @@ __device__ __forceinline__ uint64_t mx_sdesc_sw128(uint32_t addr) {
   return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
-// kind::mxf8f6f4 instruction descriptor: A e2m1, B e4m3, K-major both, E8M0 scales, M = 128,
-// scale-factor ids (the byte of each TMEM scale word) = K block b.
-__device__ __forceinline__ uint32_t mx_idesc(int N, int b) {
-  return ((uint32_t)b << 4) | (5u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) | (1u << 23) |
+// kind::mxf8f6f4 instruction descriptor: A e4m3, B e2m1, K-major both, E8M0 scales, M = 128,
+// N = 256; scale-factor ids (the byte of each TMEM scale word) = K block b.
+__device__ __forceinline__ uint32_t mx_idesc(int b) {
+  return ((uint32_t)b << 4) | (0u << 7) | (5u << 10) | ((uint32_t)(kMxRows >> 3) << 17) | (1u << 23) |
          ((uint32_t)(128 >> 4) << 24) | ((uint32_t)b << 29);
 }
 __device__ __forceinline__ void mx_mma(uint32_t d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc,
@@ -94,7 +101,7 @@ __device__ __forceinline__ void mx_cp_sf(uint32_t tmem_col, uint32_t saddr) {
 __device__ __forceinline__ void mx_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
-// kMxDepth consecutive tiles (K steps) from `tile` on; tiles past the map read as zeros
+// one 256-row x 128-K weight tile (16 KB of global memory)
 __device__ __forceinline__ void mx_tma_tile(uint32_t dst, const CUtensorMap* map, int tile, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
@@ -106,6 +113,10 @@ __device__ __forceinline__ void mx_bulk(uint32_t dst, const void* src, uint32_t 
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                "l"(src), "r"(bytes), "r"(bar)
                : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  tmem_ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(v));
+  tmem_ld16(taddr + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
 }
 
 // The CTA's work in order: items (expert unit, K slice, row-tile group), each in pick batches;
@@ -147,7 +158,7 @@ struct MxWalk {
   __device__ int np() const { return min(kMxMaxPicks, np_all - pb); }
 };
 
-__device__ __forceinline__ int mx_ncols(int np) { return np <= 8 ? 8 : np <= 16 ? 16 : 32; }
+__device__ __forceinline__ int mx_groups(int np) { return (np + 7) / 8; }  // real 8-row groups of A
 
 __global__ void __launch_bounds__(kMxThreads, 1)
     expert_tc_kernel(const __grid_constant__ CUtensorMap wmap, const ExpertTcArgs a) {
@@ -160,9 +171,9 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   auto empty = [&](int s) { return smem_u32(bars + kMxStages + s); };
   auto b_ready = [&](int i) { return smem_u32(bars + 2 * kMxStages + i); };
   auto b_free = [&](int i) { return smem_u32(bars + 2 * kMxStages + 2 + i); };
-  auto d_full = [&](int i) { return smem_u32(bars + 2 * kMxStages + 4 + i); };
-  auto d_empty = [&](int i) { return smem_u32(bars + 2 * kMxStages + 6 + i); };
-  const uint32_t drain = smem_u32(bars + 2 * kMxStages + 8);
+  const uint32_t d_full = smem_u32(bars + 2 * kMxStages + 4);
+  const uint32_t d_empty = smem_u32(bars + 2 * kMxStages + 5);
+  const uint32_t drain = smem_u32(bars + 2 * kMxStages + 6);
   uint32_t* tmem_base = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
   int* s_picks = reinterpret_cast<int*>(smem + L::kPicks);
@@ -175,26 +186,26 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(b_ready(i), 1);
       mbar_init(b_free(i), 1);
-      mbar_init(d_full(i), 1);
-      mbar_init(d_empty(i), 4);
     }
+    mbar_init(d_full, 1);
+    mbar_init(d_empty, 4);
     mbar_init(drain, 1);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_base)),
-                 "r"(256));
+                 "r"(512));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_base;
-  // TMEM columns: accumulators 0, 32 (up to 32 picks); weight scales 64 + 4 (stage, K step); activation
-  // scales 128 + 32 buffer + 4 K step (a scale operand starts on a 4-column boundary: the
-  // 32-lane x 4-column atom of tcgen05.cp.32x128b)
-  const uint32_t t_d = tmem, t_sfa = tmem + 64, t_sfb = tmem + 128;
+  // TMEM columns: the accumulator 0 .. 255 (lane = pick, column = weight row); activation scales
+  // 256 + 32 buffer + 4 K step; weight scales 320 + 8 stage (rows 0..127, then 128..255). Every
+  // scale operand starts on a 4-column boundary.
+  const uint32_t t_d = tmem, t_sfx = tmem + 256, t_sfw = tmem + 320;
   const int ksteps = a.ks_len / 128;
 
   pdl_wait();
@@ -208,17 +219,16 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       for (bool live = w.start(a, nu, gridDim.x, blockIdx.x); live; live = w.next(a)) {
         bool ok = true;
         for (int t = w.tile_lo; ok && t < w.tile_hi; ++t)
-          for (int s = 0; s < ksteps; s += kMxDepth, ++c) {
+          for (int s = 0; s < ksteps; ++s, ++c) {
             const int st = c % kMxStages;
             if (c >= kMxStages && !mbar_wait(empty(st), ((c / kMxStages) - 1) & 1, abort)) {
               ok = false;
               break;
             }
-            const int nk = min(kMxDepth, ksteps - s);  // K steps of this slice in the stage
             const int tile = ((w.e * a.rtiles + t) * (a.K / 128)) + w.ks * ksteps + s;
-            mx_expect_tx(full(st), kMxDepth * 8192 + nk * 512);
-            mx_tma_tile(smem_u32(smem + L::kA + st * L::kStage), &wmap, tile, full(st));
-            mx_bulk(smem_u32(smem + L::kSfa + st * kMxDepth * 512), a.ws + (size_t)tile * 512, nk * 512, full(st));
+            mx_expect_tx(full(st), 16384 + 1024);
+            mx_tma_tile(smem_u32(smem + L::kW + st * L::kStage), &wmap, tile, full(st));
+            mx_bulk(smem_u32(smem + L::kSfw + st * 1024), a.ws + (size_t)tile * 1024, 1024, full(st));
           }
         if (!ok) break;
       }
@@ -234,36 +244,34 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       bool ok = true;
       for (bool live = w.start(a, nu, gridDim.x, blockIdx.x); ok && live; live = w.next(a), ++bi) {
         const int bb = bi & 1;
-        const int N = mx_ncols(w.np());
+        const int G = mx_groups(w.np());
         if (!(ok = mbar_wait(b_ready(bb), (bi >> 1) & 1, abort))) break;
         tc_fence_after();
-        const uint32_t sb = smem_u32(smem + L::kB + bb * L::kBBytes);
+        const uint32_t sa = smem_u32(smem + L::kA + bb * L::kABytes);
         for (int s = 0; s < ksteps; ++s)
-          mx_cp_sf(t_sfb + 32 * bb + 4 * s, smem_u32(smem + L::kSfb + bb * L::kSfbBytes + s * 512));
+          mx_cp_sf(t_sfx + 32 * bb + 4 * s, smem_u32(smem + L::kSfx + bb * L::kSfxBytes + s * 512));
         for (int t = w.tile_lo; ok && t < w.tile_hi; ++t, ++ti) {
-          const int dd = ti & 1;
-          if (ti >= 2 && !(ok = mbar_wait(d_empty(dd), ((ti >> 1) - 1) & 1, abort))) break;
+          // the accumulator's previous tile has been drained
+          if (ti >= 1 && !(ok = mbar_wait(d_empty, (ti - 1) & 1, abort))) break;
           tc_fence_after();
-          for (int s0 = 0; s0 < ksteps; s0 += kMxDepth, ++c) {
+          for (int s = 0; s < ksteps; ++s, ++c) {
             const int st = c % kMxStages;
             if (!(ok = mbar_wait(full(st), (c / kMxStages) & 1, abort))) break;
             tc_fence_after();
-            const int nk = min(kMxDepth, ksteps - s0);
-            for (int j = 0; j < nk; ++j) {
-              const int s = s0 + j, slot = st * kMxDepth + j;
-              mx_cp_sf(t_sfa + 4 * slot, smem_u32(smem + L::kSfa + slot * 512));
-              const uint32_t sa = smem_u32(smem + L::kA + st * L::kStage + j * 16384);
+            mx_cp_sf(t_sfw + 8 * st, smem_u32(smem + L::kSfw + st * 1024));
+            mx_cp_sf(t_sfw + 8 * st + 4, smem_u32(smem + L::kSfw + st * 1024 + 512));
+            const uint32_t sw = smem_u32(smem + L::kW + st * L::kStage);
 #pragma unroll
-              for (int b = 0; b < 4; ++b) {
-                const uint64_t db = umma_sdesc(sb + (8 * s + 2 * b) * 128, 128, (a.ks_len / 16) * 128);
-                mx_mma(t_d + 32 * dd, mx_sdesc_sw128(sa + 32 * b), db, mx_idesc(N, b), s > 0 || b > 0,
-                       (t_sfa + 4 * slot) | ((uint32_t)b << 30), (t_sfb + 32 * bb + 4 * s) | ((uint32_t)b << 30));
-              }
+            for (int b = 0; b < 4; ++b) {
+              // A: K step s of the batch's activations, G real 8-row groups 1 KB apart
+              const uint64_t da = umma_sdesc(sa + (s * G * 8 + 2 * b) * 128, 128, 1024);
+              mx_mma(t_d, da, mx_sdesc_sw128(sw + 32 * b), mx_idesc(b), s > 0 || b > 0,
+                     (t_sfx + 32 * bb + 4 * s) | ((uint32_t)b << 30), (t_sfw + 8 * st) | ((uint32_t)b << 30));
             }
             umma_commit(empty(st));
           }
           if (!ok) break;
-          umma_commit(d_full(dd));
+          umma_commit(d_full);
         }
         umma_commit(b_free(bb));
       }
@@ -273,30 +281,32 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     }
   } else {
     // ================= activation staging + accumulator drain (warps 2-5, 128 threads)
-    const int et = tid - 64;
-    const uint32_t lane_addr = (uint32_t)(32 * (warp & 3)) << 16;
-    const int P = a.M * a.topk;
     // (the 128 threads decide together -- softmax_all is the AND over named barrier 1 -- so none
     // leaves while the others wait at a barrier)
+    const int et = tid - 64;
+    const int q = warp & 3;  // this warp's TMEM lanes: picks 32 q .. 32 q + 31
+    const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
+    const int P = a.M * a.topk;
     auto stage = [&](const MxWalk& sw, int bi) -> bool {
       const int bb = bi & 1;
       if (bi >= 2 && !softmax_all(mbar_wait(b_free(bb), ((bi >> 1) - 1) & 1, abort))) return false;
-      const int np = sw.np(), N = mx_ncols(np);
+      const int np = sw.np(), G = mx_groups(np);
       const int k0 = sw.ks * a.ks_len;
       int* pk = s_picks + bb * kMxMaxPicks;
-      uint8_t* sb = smem + L::kB + bb * L::kBBytes;
-      uint8_t* sf = smem + L::kSfb + bb * L::kSfbBytes;
+      uint8_t* sa = smem + L::kA + bb * L::kABytes;
+      uint8_t* sf = smem + L::kSfx + bb * L::kSfxBytes;
       if (et < kMxMaxPicks) pk[et] = et < np ? a.picks[sw.p0 + sw.pb + et] : 0;
       asm volatile("bar.sync 1, 128;" ::: "memory");
+      // A: [K step][group][8 chunks of 16 K][8 rows x 16 B]
       const int kc_n = a.ks_len / 16;
-      for (int i = et; i < N * kc_n; i += 128) {
+      for (int i = et; i < 8 * G * kc_n; i += 128) {
         const int n = i / kc_n, kc = i % kc_n;
         uint4 v = make_uint4(0, 0, 0, 0);
         if (n < np) {
           const int row = a.x_by_pick ? pk[n] : pk[n] / a.topk;
           v = ldg16(a.x + (size_t)row * a.K + k0 + 16 * kc);
         }
-        *reinterpret_cast<uint4*>(sb + ((n >> 3) * kc_n + kc) * 128 + (n & 7) * 16) = v;
+        *reinterpret_cast<uint4*>(sa + ((kc >> 3) * G + (n >> 3)) * 1024 + (kc & 7) * 128 + (n & 7) * 16) = v;
       }
       // scale atoms, one a K step: [lane n][16 B], bytes 0..3 = the codes of blocks 0..3
       for (int i = et; i < ksteps * 32; i += 128) {
@@ -320,30 +330,43 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     int ti = 0;
     bool live = ok && w.start(a, nu, gridDim.x, blockIdx.x);
     for (int bi = 0; ok && live; live = w.next(a), ++bi) {
-      const int np = w.np(), N = mx_ncols(np);
+      const int np = w.np();
       const int* pk = s_picks + (bi & 1) * kMxMaxPicks;
-      float* out = a.out + (size_t)w.ks * P * a.N;
+      const int n = 32 * q + lane;  // this thread's pick slot
+      const bool mine = n < np;
+      float* orow = a.out + ((size_t)w.ks * P + (mine ? pk[n] : 0)) * a.N;
       for (int t = w.tile_lo; t < w.tile_hi; ++t, ++ti) {
-        const int dd = ti & 1;
-        if (!(ok = softmax_all(mbar_wait(d_full(dd), (ti >> 1) & 1, abort)))) break;
+        if (!(ok = softmax_all(mbar_wait(d_full, ti & 1, abort)))) break;
         tc_fence_after();
-        uint32_t v[32];
-        const uint32_t src = t_d + 32 * dd + lane_addr;
-        tmem_ld16(src, *reinterpret_cast<uint32_t(*)[16]>(v));
-        if (N > 16) tmem_ld16(src + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(d_empty(dd));
-        const int row = 128 * t + 32 * (warp & 3) + lane;
-        if (row < a.N) {
+        // two halves of 128 weight rows: the accumulator is free once the second is in registers
+        for (int h = 0; h < 2; ++h) {
+          uint32_t v[128];
+          if (32 * q < np) {
 #pragma unroll
-          for (int n = 0; n < 32; ++n)
-            if (n < np) out[(size_t)pk[n] * a.N + row] = __uint_as_float(v[n]);
+            for (int c = 0; c < 4; ++c)
+              tmem_ld32(t_d + lane_addr + 128 * h + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * c));
+            tmem_wait_ld();
+          }
+          if (h == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(d_empty);
+          }
+          const int row0 = kMxRows * t + 128 * h;
+          if (mine) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int r = row0 + 4 * j;
+              if (r + 3 < a.N)
+                *reinterpret_cast<float4*>(orow + r) =
+                    make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+            }
+          }
         }
       }
-      // the batch two ahead reuses this batch's buffers (its MMAs are done: its last
-      // accumulator was drained)
+      // the batch two ahead reuses this batch's buffers (its MMAs are done: its last tile was
+      // drained)
       asm volatile("bar.sync 1, 128;" ::: "memory");
       if (ok && s_live) {
         ok = stage(sw, si);
@@ -357,7 +380,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
   }
   pdl_launch();
 }

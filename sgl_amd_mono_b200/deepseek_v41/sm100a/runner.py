@@ -104,7 +104,7 @@ class MonoRunner:
             _check(w[k], k, shape, dt, d)
         r = {}
         for name, (src, codes, N, K) in {"w13": ("w13", "s13", 2 * Il, H), "w2": ("w2", "s2", H, Il)}.items():
-            rows = (N + 127) // 128 * 128  # whole 128-row tensor-core tiles
+            rows = (N + 255) // 256 * 256  # whole 256-row tensor-core tiles
             dst = torch.empty(E * rows * K // 2, dtype=torch.uint8, device=d)
             dcodes = torch.empty(E * rows * K // 32, dtype=torch.uint8, device=d)
             a = abi.RelayoutArgs(src=_p(w[src]), src_codes=_p(w[codes]), dst=_p(dst), dst_codes=_p(dcodes),
