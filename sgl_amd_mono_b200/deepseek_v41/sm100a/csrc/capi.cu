@@ -23,6 +23,7 @@
 #include "lmhead.cuh"
 #include "moe.cuh"
 #include "moe_tc.cuh"
+#include "dense_tc.cuh"
 #include "peer.cuh"
 #include "seam.cuh"
 
@@ -128,6 +129,50 @@ bool expert_weight_map(CUtensorMap* m, const void* w, int64_t tiles) {
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The tensor map of a dense FP8 weight [N, K] read in place: 256-row x 128-K boxes, 128-byte
+// swizzle, rows past N read as zeros.
+bool dense_weight_map(CUtensorMap* m, const void* w, int N, int K) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc || !w || reinterpret_cast<uintptr_t>(w) % 16 || K % 16) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)N};
+  const cuuint64_t strides[1] = {(cuuint64_t)K};
+  const cuuint32_t box[2] = {128, 256};
+  const cuuint32_t es[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(w), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Whether a planned GEMV with an MXFP8 input runs on the tcgen05 dense kernel: 16 <= M <= 48
+// (below, the persistent kernel's per-item latency loses to gemv_fp8_kernel), ungrouped, N >= 256,
+// K a multiple of 128, the weight 16-byte aligned. (Independent of the activation pointers, which
+// are null while the scratch is only being measured.)
+bool dense_eligible(const GemvArgs& g) {
+  return g.M >= 16 && g.M <= kDnMaxRows && g.N >= 256 && g.K % 128 == 0 && g.x_group_rows == g.N &&
+         reinterpret_cast<uintptr_t>(g.w) % 16 == 0;
+}
+// Its K slicing: the longest slice (<= kDnKsMax, dividing K) that still gives a (256-row tile,
+// slice) pair to every SM, at most 16 slices (the consumer sums the slices' partials); and the
+// row-tile groups an item covers.
+DenseTcArgs dense_args(const GemvArgs& g, const uint8_t* x8, const uint8_t* xs, int sms) {
+  DenseTcArgs d = {};
+  d.M = g.M; d.N = g.N; d.K = g.K;
+  int ks = std::min(g.K, kDnKsMax) / 128 * 128;
+  while (g.K % ks) ks -= 128;
+  d.rtiles = cdiv(g.N, 256);
+  while (ks > 128 && d.rtiles * (g.K / ks) < sms && g.K / ks < 16 && (ks / 2) % 128 == 0 && g.K % (ks / 2) == 0)
+    ks /= 2;
+  d.ks_len = ks;
+  d.kslices = g.K / ks;
+  d.row_groups = std::max(1, std::min(d.rtiles, cdiv(sms, d.kslices)));
+  d.codes = g.codes; d.x = x8; d.xs = xs; d.x_ld = g.K; d.out = g.out;
+  return d;
+}
+// Plan time: a dense-eligible GEMV takes the dense kernel's K slice count (its partials' count).
+void dense_replan(GemvArgs& g, int sms) {
+  if (dense_eligible(g)) g.kslices = dense_args(g, nullptr, nullptr, sms).kslices;
+}
+
 template <typename Kern, typename Args>
 cudaError_t launch(Kern kernel, dim3 grid, dim3 block, int smem, cudaStream_t st, const Args& args) {
   g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -167,6 +212,20 @@ cudaError_t launch2(Kern kernel, dim3 grid, dim3 block, int smem, cudaStream_t s
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, a0, a1);
+}
+
+// A planned GEMV: the tcgen05 dense kernel when its input is MXFP8, else gemv_fp8_kernel.
+cudaError_t dense_go(const GemvArgs& g, const uint8_t* x8, const uint8_t* xs, cudaStream_t st) {
+  if (!dense_eligible(g)) return gemv_go(g, st);
+  if (!x8 || !xs) return cudaErrorInvalidValue;
+  const DenseTcArgs d = dense_args(g, x8, xs, sm_count());
+  CUtensorMap m;
+  if (!dense_weight_map(&m, g.w, g.N, g.K)) {
+    fprintf(stderr, "dsv41: dense weight tensor map failed (driver entry point or alignment)\n");
+    return cudaErrorInvalidValue;
+  }
+  return launch2(dense_tc_kernel, dim3(std::min(sm_count(), d.kslices * d.row_groups)), dim3(kDnThreads),
+                 DnSmem::kBytes, st, m, d);
 }
 
 // y[m][n] = sum over K slices of partials p[ks][m][n], in slice order.
@@ -260,12 +319,14 @@ int k1_run(const Dsv41K1Args* a, cudaStream_t st, bool go, int64_t* need) {
   auto* pre_out = a->pre_out ? ptr<float>(a->pre_out) : c.take<float>(M * 4);
   GemvArgs g1 = gemv_plan(ptr<const uint8_t>(a->wqkv), ptr<const uint8_t>(a->wqkv_codes), xq, nullptr,
                           M, QKV, H, H, 0, sms);
+  dense_replan(g1, sms);
   g1.out = c.take<float>((int64_t)g1.kslices * M * QKV);
   auto* qxq = c.take<__nv_bfloat16>((int64_t)M * QL);
   auto* qx8 = a->qx8 ? ptr<uint8_t>(a->qx8) : c.take<uint8_t>((int64_t)M * QL);
   auto* qx8s = a->qx8s ? ptr<uint8_t>(a->qx8s) : c.take<uint8_t>((int64_t)M * QL / 32);
   GemvArgs g2 = gemv_plan(ptr<const uint8_t>(a->wqb), ptr<const uint8_t>(a->wqb_codes), qxq, nullptr,
                           M, heads * D, QL, QL, 0, sms);
+  dense_replan(g2, sms);
   g2.out = c.take<float>((int64_t)g2.kslices * M * heads * D);
   *need = c.off;
   if (!go) return DSV41_OK;
@@ -284,7 +345,7 @@ int k1_run(const Dsv41K1Args* a, cudaStream_t st, bool go, int64_t* need) {
   DSV41_TRY(launch(seam_slice_kernel, dim3(H / kSliceCols), dim3(256), 0, st, s));
   DSV41_TRY(launch(seam_gate_norm_kernel, dim3(M), dim3(256), 0, st, s));
   mark(a->events, 1, st);
-  DSV41_TRY(gemv_go(g1, st));
+  DSV41_TRY(dense_go(g1, x8, x8s, st));
   mark(a->events, 2, st);
   FrontArgs f = {};
   f.M = M; f.QL = QL; f.KVD = D; f.nope = nope; f.rope = rope; f.kslices = g1.kslices;
@@ -308,7 +369,7 @@ int k1_run(const Dsv41K1Args* a, cudaStream_t st, bool go, int64_t* need) {
                      st, k));
   }
   mark(a->events, 3, st);
-  DSV41_TRY(gemv_go(g2, st));
+  DSV41_TRY(dense_go(g2, qx8, qx8s, st));
   QRopeArgs qr = {};
   qr.M = M; qr.heads = heads; qr.D = D; qr.nope = nope; qr.rope = rope; qr.kslices = g2.kslices;
   qr.part = g2.out; qr.cos_sin = ptr<const float>(a->cos_sin); qr.pos = ptr<const int64_t>(a->pos);
@@ -400,6 +461,7 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   auto* x8bs = a->x8bs ? ptr<uint8_t>(a->x8bs) : c.take<uint8_t>((int64_t)M * G * O / 32);
   GemvArgs gb = gemv_plan(ptr<const uint8_t>(a->wob), ptr<const uint8_t>(a->wob_codes), x8bq, nullptr,
                           M, H, G * O, G * O, 0, sms);
+  dense_replan(gb, sms);
   gb.out = c.take<float>((int64_t)gb.kslices * M * H);
   auto* attn_part = a->attn_part ? ptr<__nv_bfloat16>(a->attn_part) : c.take<__nv_bfloat16>((int64_t)M * H);
   auto* attn = a->attn ? ptr<__nv_bfloat16>(a->attn) : c.take<__nv_bfloat16>((int64_t)M * H);
@@ -424,12 +486,14 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   auto* picks = c.take<int32_t>(P);
   GemvArgs gs = gemv_plan(ptr<const uint8_t>(a->sgu), ptr<const uint8_t>(a->sgu_codes), xq, nullptr,
                           M, 2 * SI, H, H, 0, sms);
+  dense_replan(gs, sms);
   gs.out = c.take<float>((int64_t)gs.kslices * M * 2 * SI);
   auto* smq = c.take<uint8_t>((int64_t)M * SI);
   auto* smqs = c.take<uint8_t>((int64_t)M * SI / 32);
   auto* smx = c.take<__nv_bfloat16>((int64_t)M * SI);
   GemvArgs gd = gemv_plan(ptr<const uint8_t>(a->sw2), ptr<const uint8_t>(a->sw2_codes), smx, nullptr,
                           M, H, SI, SI, 0, sms);
+  dense_replan(gd, sms);
   gd.out = c.take<float>((int64_t)gd.kslices * M * H);
   const int max_units = std::min(E, P);
   ExpertArgs eu = {};
@@ -489,7 +553,7 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   DSV41_TRY(gemv_go(ga, st));
   FinalizeArgs fa = {M, G * O, ga.kslices, ga.out, x8bq, x8b, x8bs};
   DSV41_TRY(launch(finalize_kernel, dim3(grid_for((int64_t)M * G * O / 8, 256)), dim3(256), 0, st, fa));
-  DSV41_TRY(gemv_go(gb, st));
+  DSV41_TRY(dense_go(gb, x8b, x8bs, st));
   FinalizeArgs fb = {M, H, gb.kslices, gb.out, attn_part, nullptr, nullptr};
   DSV41_TRY(launch(finalize_kernel, dim3(grid_for((int64_t)M * H / 8, 256)), dim3(256), 0, st, fb));
   mark(a->events, 2, st);
@@ -529,10 +593,10 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   DSV41_TRY(launch(moe_plan_kernel, dim3(1), dim3(512), 0, st, pl));
   // ---- shared expert
   mark(a->events, 4, st);
-  DSV41_TRY(gemv_go(gs, st));
+  DSV41_TRY(dense_go(gs, x8, x8s, st));
   SharedActArgs sa = {M, SI, gs.kslices, gs.out, smq, smqs, smx};
   DSV41_TRY(launch(shared_act_kernel, dim3(grid_for((int64_t)M * SI / 8, 256)), dim3(256), 0, st, sa));
-  DSV41_TRY(gemv_go(gd, st));
+  DSV41_TRY(dense_go(gd, smq, smqs, st));
   mark(a->events, 5, st);
   // ---- routed experts: persistent tcgen05 grouped GEMMs, one CTA an SM
   {
