@@ -583,9 +583,10 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   DSV41_TRY(launch(seam_slice_kernel, dim3(H / kSliceCols), dim3(256), 0, st, s));
   DSV41_TRY(launch(seam_gate_norm_kernel, dim3(M), dim3(256), 0, st, s));
   // ---- router, routing, union
-  RouterArgs ra = {M, E, H, normed, ptr<const __nv_bfloat16>(a->gate_w), logits};
+  const int router_smem = 16 * H <= 200 * 1024 ? 16 * H : 0;
+  RouterArgs ra = {M, E, H, normed, ptr<const __nv_bfloat16>(a->gate_w), logits, router_smem > 0};
   mark(a->events, 3, st);
-  DSV41_TRY(launch(router_kernel, dim3(cdiv(E, 8), cdiv(M, 8)), dim3(256), 0, st, ra));
+  DSV41_TRY(launch(router_kernel, dim3(cdiv(E, 8), cdiv(M, 8)), dim3(256), router_smem, st, ra));
   RouteArgs rt = {M, E, TK, (int)a->route_softmax, logits, ptr<const float>(a->bias),
                   ptr<int32_t>(a->ids), ptr<float>(a->wts)};
   DSV41_TRY(launch(route_kernel, dim3(M), dim3(256), 0, st, rt));

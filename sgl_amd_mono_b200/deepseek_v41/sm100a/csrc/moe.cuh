@@ -26,36 +26,61 @@ struct RouterArgs {
   const __nv_bfloat16* x;     // [M, K] normed
   const __nv_bfloat16* gate;  // [E, K]
   float* logits;              // [M, E]
+  int staged;                 // 1: the CTA's 8 rows of x go to shared memory (16 K bytes of it)
 };
 
 // grid (E / 8, ceil(M / 8)); warp w of CTA (ex, tg) = expert 8 ex + w, rows 8 tg .. 8 tg + 7.
+// A lane's weight loads go out 16 at a time (4096 K) before their sums; the CTA's 8 rows of x
+// are staged once in shared memory when they fit. The arithmetic is the contract's, unchanged:
+// per lane and row one fp64 chain over i, then j.
+constexpr int kRouterChunk = 16;  // 256-K iterations a batch of weight loads
 __global__ void __launch_bounds__(256) router_kernel(const RouterArgs a) {
+  extern __shared__ __align__(16) uint8_t router_smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x * 8 + warp;
-  if (e >= a.E) return;
-  pdl_wait();
+  const bool live = e < a.E;
   const int iters = a.K / 256;
-  const __nv_bfloat16* w = a.gate + (size_t)e * a.K + 8 * lane;
+  const __nv_bfloat16* w = a.gate + (size_t)(live ? e : 0) * a.K + 8 * lane;
+  uint4 wv[kRouterChunk];
+  auto load_chunk = [&](int i0) {
+#pragma unroll
+    for (int i = 0; i < kRouterChunk; ++i)
+      wv[i] = (live && i0 + i < iters) ? ldg16(w + 256 * (i0 + i)) : make_uint4(0, 0, 0, 0);
+  };
+  load_chunk(0);  // the gate weights wait on nothing: stream them before the dependency wait
+  pdl_wait();
   const int t0 = blockIdx.y * 8, nt = min(8, a.M - t0);
+  const __nv_bfloat16* xr = a.x + (size_t)t0 * a.K;
+  if (a.staged) {
+    __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(router_smem);
+    for (int v = threadIdx.x; v < nt * (a.K / 8); v += blockDim.x)
+      *reinterpret_cast<uint4*>(xs + 8 * (size_t)v) = *reinterpret_cast<const uint4*>(xr + 8 * (size_t)v);
+    __syncthreads();
+    xr = xs;
+  }
+  if (!live) return;
   // the (up to) 8 rows' chains run side by side; each row's sum keeps the contract's order
   double acc[8] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0};
-#pragma unroll 4
-  for (int i = 0; i < iters; ++i) {
-    const uint4 wv = ldg16(w + 256 * i);
-    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-    double wd[8];
+  for (int i0 = 0; i0 < iters; i0 += kRouterChunk) {
+    if (i0 > 0) load_chunk(i0);
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      wd[j] = (double)__uint_as_float((j & 1) ? (ww[j >> 1] & 0xffff0000u) : (ww[j >> 1] << 16));
+    for (int i = 0; i < kRouterChunk; ++i) {
+      if (i0 + i >= iters) break;
+      const uint32_t ww[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+      double wd[8];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      if (r < nt) {
-        const uint4 xv = *reinterpret_cast<const uint4*>(a.x + (size_t)(t0 + r) * a.K + 8 * lane + 256 * i);
-        const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
+      for (int j = 0; j < 8; ++j)
+        wd[j] = (double)__uint_as_float((j & 1) ? (ww[j >> 1] & 0xffff0000u) : (ww[j >> 1] << 16));
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t xb = (j & 1) ? (xx[j >> 1] & 0xffff0000u) : (xx[j >> 1] << 16);
-          acc[r] = __fma_rn((double)__uint_as_float(xb), wd[j], acc[r]);
+      for (int r = 0; r < 8; ++r) {
+        if (r < nt) {
+          const uint4 xv = *reinterpret_cast<const uint4*>(xr + (size_t)r * a.K + 8 * lane + 256 * (i0 + i));
+          const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t xb = (j & 1) ? (xx[j >> 1] & 0xffff0000u) : (xx[j >> 1] << 16);
+            acc[r] = __fma_rn((double)__uint_as_float(xb), wd[j], acc[r]);
+          }
         }
       }
     }
@@ -182,36 +207,50 @@ struct PlanArgs {
   int32_t* picks;      // [M * topk]: natural pick indices t * topk + k, grouped by expert, ascending
 };
 
+// One CTA of 512 threads (E <= 512, M topk <= kPlanMaxPicks): counts by shared-memory atomics,
+// a block-wide inclusive scan of (picks, union flag) an expert, then each pick's rank among the
+// earlier picks of its expert from the ids staged in shared memory.
+constexpr int kPlanMaxPicks = 48 * 32;
 __global__ void __launch_bounds__(512) moe_plan_kernel(const PlanArgs a) {
-  __shared__ int cnt[512];
-  __shared__ int off[513];
+  __shared__ int cnt[512], s_off[512], s_uf[512];
+  __shared__ int s_ids[kPlanMaxPicks];
   pdl_wait();
   const int P = a.M * a.topk, tid = threadIdx.x;
-  for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;
+  cnt[tid] = 0;
+  for (int p = tid; p < P; p += blockDim.x) s_ids[p] = a.ids[p];
   __syncthreads();
-  for (int p = tid; p < P; p += blockDim.x) atomicAdd(&cnt[a.ids[p]], 1);
+  for (int p = tid; p < P; p += blockDim.x) atomicAdd(&cnt[s_ids[p]], 1);
   __syncthreads();
-  if (tid == 0) {
-    int o = 0, u = 0;
-    for (int e = 0; e < a.E; ++e) {
-      off[e] = o;
-      if (cnt[e] > 0) {
-        a.u_expert[u] = e;
-        a.u_off[u] = o;
-        ++u;
-      }
-      o += cnt[e];
-    }
-    a.u_off[u] = o;
-    *a.n_u = u;
-    off[a.E] = o;
+  // inclusive scans (Hillis-Steele) of the counts and of the union flags over experts
+  const int c = tid < a.E ? cnt[tid] : 0;
+  s_off[tid] = c;
+  s_uf[tid] = c > 0;
+  __syncthreads();
+  for (int d = 1; d < 512; d <<= 1) {
+    const int vo = tid >= d ? s_off[tid - d] : 0, vu = tid >= d ? s_uf[tid - d] : 0;
+    __syncthreads();
+    s_off[tid] += vo;
+    s_uf[tid] += vu;
+    __syncthreads();
   }
+  const int first = s_off[tid] - c;  // this expert's first slot in picks
+  if (tid < a.E && c > 0) {
+    const int u = s_uf[tid] - 1;
+    a.u_expert[u] = tid;
+    a.u_off[u] = first;
+  }
+  if (tid == 0) {
+    const int nu = s_uf[511];
+    a.u_off[nu] = s_off[511];
+    *a.n_u = nu;
+  }
+  cnt[tid] = first;  // reused: the experts' first slots
   __syncthreads();
   for (int p = tid; p < P; p += blockDim.x) {
-    const int e = a.ids[p];
+    const int e = s_ids[p];
     int before = 0;
-    for (int q = 0; q < p; ++q) before += (a.ids[q] == e);
-    a.picks[off[e] + before] = p;
+    for (int q = 0; q < p; ++q) before += (s_ids[q] == e);
+    a.picks[cnt[e] + before] = p;
   }
   pdl_launch();
 }
