@@ -395,6 +395,8 @@ bool k2_ok(const Dsv41K2Args* a) {
   if (a->phase == 2 && (!a->attn || !a->moe_part)) return false;
   if (a->phase == 1 && !a->attn_part) return false;
   if (!a->q || !a->kt || !a->klen || !a->swa || !a->sink || !a->woa || !a->wob) return false;
+  // KV records are fetched by bulk copies: page bases and strides 16-byte aligned
+  if (a->swa % 16 || a->swa_stride % 16 || (a->comp && (a->comp % 16 || a->comp_stride % 16))) return false;
   if (!a->res_in || !a->post_in || !a->comb_in || !a->pre_in || !a->hc_fn || !a->norm_w) return false;
   if (!a->gate_w || !a->w13 || !a->w2 || !a->sgu || !a->sw2 || !a->out || !a->ids || !a->wts) return false;
   if (!a->route_softmax && !a->bias) return false;
