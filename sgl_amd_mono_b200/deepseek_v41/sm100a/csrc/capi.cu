@@ -680,7 +680,7 @@ int dsv41_walk_plan(const Dsv41WalkPlanArgs* a, void* stream) {
     return DSV41_EINVAL;
   WalkPlanArgs w = {(int)a->rows, (int)a->ctas, (int)a->topk, ptr<const int32_t>(a->bounds),
                     ptr<const int32_t>(a->owners), ptr<int32_t>(a->plan)};
-  DSV41_TRY(launch(walk_plan_kernel, dim3(1), dim3(32), 0, reinterpret_cast<cudaStream_t>(stream), w));
+  DSV41_TRY(launch(walk_plan_kernel, dim3(1), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), w));
   return launch_status();
 }
 
@@ -708,10 +708,13 @@ int dsv41_topk(const Dsv41TopkArgs* a, void* stream) {
   if (!a || a->rows < 1 || a->k < 1 || a->k > 65536 || !a->vals || !a->n || !a->out || a->group < 1 ||
       (a->page_out && (!a->table || !a->owners || a->page < 1)))
     return DSV41_EINVAL;
+  // a row has at most vstride values, hence at most ceil(vstride / group) candidates
+  const int cap = std::min<int>(40960, ((int)a->vstride + (int)a->group - 1) / (int)a->group);
   TopkArgs t = {(int)a->rows, (int)a->k, ptr<const float>(a->vals), (int)a->vstride, ptr<const int32_t>(a->n),
                 (int)a->group, ptr<int32_t>(a->out), ptr<int32_t>(a->page_out), ptr<const int32_t>(a->table),
-                (int)a->table_stride, (int)a->page, ptr<const int32_t>(a->owners)};
-  DSV41_TRY(launch(topk_kernel, dim3((int)a->rows), dim3(1024), 0, reinterpret_cast<cudaStream_t>(stream), t));
+                (int)a->table_stride, (int)a->page, ptr<const int32_t>(a->owners), cap};
+  DSV41_TRY(launch(topk_kernel, dim3((int)a->rows), dim3(1024), cap * 4 + 32 * 256 * 4,
+                   reinterpret_cast<cudaStream_t>(stream), t));
   return launch_status();
 }
 

@@ -7,9 +7,10 @@
 //   I_{h,c} = the integer dot of the 2 x E2M1 values of q_h and k_col over chunk c,
 //   logit = fp32( tree-sum over heads of w_h relu(x_h) ) with the tree: s_g = terms of heads
 //   g, g+8, g+16, ... in order, then ((s0 + s4) + (s2 + s6)) + ((s1 + s5) + (s3 + s7)).
-// I_{h,c} comes from mma.sync m16n8k16 f16 on cvt.e2m1x2 operands: every product is a
-// multiple of 1/4 and a 32-dim sum stays below 2^11, so the fp32 accumulation is exact. The
-// f16 operands carry the real E2M1 values (I / 4), so the scale exponent is qe + ke - 254.
+// I_{h,c} comes from mma.sync m16n8k16 f16 on cvt.e2m1x2 operands (converted once a piece for the
+// queries and once a chunk for the keys, read by ldmatrix): every product is a multiple of 1/4
+// and a 32-dim sum stays below 2^11, so the fp32 accumulation is exact. The f16 operands carry
+// the real E2M1 values (I / 4), so the scale exponent is qe + ke - 254.
 #pragma once
 
 #include "common.cuh"
@@ -34,49 +35,74 @@ struct WalkPlanArgs {
 // ceil(need / width) tasks sharing its chunks evenly at the smallest width whose task count
 // fits the CTAs. One thread (rows <= 48).
 __global__ void walk_plan_kernel(const WalkPlanArgs a) {
+  __shared__ int s_owner[64], s_bound[64];
+  __shared__ int s_lead[64], s_span[64], s_need[64], s_k[64], s_first[65], s_pieces;
   pdl_wait();
-  if (threadIdx.x != 0) return;
-  int lead[64], span[64], need[64];
-  int np = 0, run_first = 0;
-  for (int t = 0; t < a.rows; ++t) {
-    const bool start = t == 0 || a.owners[t] != a.owners[t - 1];
-    if (start) run_first = t;
-    if (start || (t - run_first) % kWalkRows == 0) lead[np++] = t;
+  // the rows' owners and bounds in shared memory and the plan cleared, by the whole block
+  for (int t = threadIdx.x; t < a.rows; t += blockDim.x) {
+    s_owner[t] = a.owners[t];
+    s_bound[t] = a.bounds[t];
   }
-  int pieces = 0;
-  for (int i = 0; i < np; ++i) {
-    const int l = lead[i], e = i + 1 < np ? lead[i + 1] : a.rows;
-    int nd = 0;
-    for (int t = l; t < e; ++t) {
-      const int b = a.bounds[t];
-      if (b > a.topk) nd = max(nd, (b + kIdxChunk - 1) / kIdxChunk);
+  for (int i = threadIdx.x; i < a.ctas * 4; i += blockDim.x) a.plan[i] = 0;
+  __syncthreads();
+  if (threadIdx.x == 0) {  // one thread plans (rows <= 48); the block writes the tasks
+    int lead[64], span[64], need[64];
+    int np = 0, run_first = 0;
+    for (int t = 0; t < a.rows; ++t) {
+      const bool start = t == 0 || s_owner[t] != s_owner[t - 1];
+      if (start) run_first = t;
+      if (start || (t - run_first) % kWalkRows == 0) lead[np++] = t;
     }
-    if (nd > 0) {
-      lead[pieces] = l;
-      span[pieces] = e - l;
-      need[pieces] = nd;
-      ++pieces;
+    int pieces = 0;
+    for (int i = 0; i < np; ++i) {
+      const int l = lead[i], e = i + 1 < np ? lead[i + 1] : a.rows;
+      int nd = 0;
+      for (int t = l; t < e; ++t) {
+        const int b = s_bound[t];
+        if (b > a.topk) nd = max(nd, (b + kIdxChunk - 1) / kIdxChunk);
+      }
+      if (nd > 0) {
+        lead[pieces] = l;
+        span[pieces] = e - l;
+        need[pieces] = nd;
+        ++pieces;
+      }
+    }
+    if (pieces == 0 || pieces >= a.ctas) {
+      s_pieces = 0;
+    } else {
+      long total = 0;
+      for (int i = 0; i < pieces; ++i) total += need[i];
+      int width = (int)max((total + a.ctas - 1) / a.ctas, 1L);
+      for (;; ++width) {
+        long tasks = 0;
+        for (int i = 0; i < pieces; ++i) tasks += (need[i] + width - 1) / width;
+        if (tasks <= a.ctas) break;
+      }
+      int r = 0;
+      for (int i = 0; i < pieces; ++i) {
+        s_lead[i] = lead[i];
+        s_span[i] = span[i];
+        s_need[i] = need[i];
+        s_first[i] = r;
+        s_k[i] = (need[i] + width - 1) / width;
+        r += s_k[i];
+      }
+      s_first[pieces] = r;
+      s_pieces = pieces;
     }
   }
-  for (int i = 0; i < a.ctas * 4; ++i) a.plan[i] = 0;
-  if (pieces == 0 || pieces >= a.ctas) return;
-  long total = 0;
-  for (int i = 0; i < pieces; ++i) total += need[i];
-  int width = (int)max((total + a.ctas - 1) / a.ctas, 1L);
-  for (;; ++width) {
-    long tasks = 0;
-    for (int i = 0; i < pieces; ++i) tasks += (need[i] + width - 1) / width;
-    if (tasks <= a.ctas) break;
-  }
-  int r = 0;
-  for (int i = 0; i < pieces; ++i) {
-    const int k = (need[i] + width - 1) / width;
-    for (int j = 0; j < k; ++j, ++r) {
-      a.plan[4 * r + 0] = lead[i];
-      a.plan[4 * r + 1] = span[i];
-      a.plan[4 * r + 2] = j * need[i] / k;
-      a.plan[4 * r + 3] = (j + 1) * need[i] / k;
-    }
+  __syncthreads();
+  // every thread writes its tasks: task r of piece i (r - first[i] = j of k)
+  const int pieces = s_pieces;
+  for (int r = threadIdx.x; pieces > 0 && r < s_first[pieces]; r += blockDim.x) {
+    int i = 0;
+    while (s_first[i + 1] <= r) ++i;
+    const int j = r - s_first[i], k = s_k[i], nd = s_need[i];
+    a.plan[4 * r + 0] = s_lead[i];
+    a.plan[4 * r + 1] = s_span[i];
+    a.plan[4 * r + 2] = j * nd / k;
+    a.plan[4 * r + 3] = (j + 1) * nd / k;
   }
   pdl_launch();
 }
@@ -100,17 +126,21 @@ struct K2iArgs {
   int reindex_chunks;      // a REINDEX row's chunks
 };
 
+// f16 operand rows: 128 dims (256 B) padded to 272 B so ldmatrix's 8 rows hit distinct banks
+constexpr int kIdxRowBytes = 272;
 __host__ __device__ inline int k2i_smem_bytes(int heads) {
-  return kIdxMaxSpan * heads * 68 + kIdxMaxSpan * 4 * heads + 4 * kIdxChunk * 16 + 4 * kIdxChunk;
+  return kIdxMaxSpan * heads * 64 + heads * kIdxRowBytes + kIdxChunk * kIdxRowBytes + kIdxMaxSpan * 4 * heads +
+         4 * kIdxChunk;
 }
 
 __global__ void __launch_bounds__(256) k2i_score_kernel(const K2iArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int H = a.heads, mtiles = H / 16;
-  uint8_t* qraw = smem;                                  // [span][H][68]
-  uint8_t* qe = qraw + kIdxMaxSpan * H * 68;             // [span][4][H]
-  uint8_t* keys = qe + kIdxMaxSpan * 4 * H;              // [4][128][16]
-  uint8_t* ke = keys + 4 * kIdxChunk * 16;               // [4][128]
+  uint8_t* qraw = smem;                                  // [span][H][64] E2M1 bytes
+  uint8_t* qf = qraw + kIdxMaxSpan * H * 64;             // [H] rows of 128 f16 dims: the current row
+  uint8_t* kf = qf + H * kIdxRowBytes;                   // [128 columns] rows of 128 f16 dims
+  uint8_t* qe = kf + kIdxChunk * kIdxRowBytes;           // [span][4][H]
+  uint8_t* ke = qe + kIdxMaxSpan * 4 * H;                // [4][128]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   pdl_wait();
   int lead, span, ch0, ch1;
@@ -132,77 +162,115 @@ __global__ void __launch_bounds__(256) k2i_score_kernel(const K2iArgs a) {
   const int owner = a.owners[lead];
   int piece_bound = 0;
   for (int r = 0; r < span; ++r) piece_bound = max(piece_bound, a.bounds[lead + r]);
-  // the piece's queries: raw E2M1 bytes (rows padded to 68 B: conflict-free lane reads)
-  for (int i = tid; i < span * H * 16; i += blockDim.x) {
-    const int r = i / (H * 16), rem = i % (H * 16), h = rem / 16, wd = rem % 16;
-    *reinterpret_cast<uint32_t*>(qraw + (r * H + h) * 68 + 4 * wd) =
-        *reinterpret_cast<const uint32_t*>(a.q + ((size_t)(lead + r) * H + h) * 64 + 4 * wd);
-  }
+  // the piece's queries: raw E2M1 bytes (each row goes to f16 once a chunk, below)
+  for (int i = tid; i < span * H * 16; i += blockDim.x)
+    reinterpret_cast<uint32_t*>(qraw)[i] = *reinterpret_cast<const uint32_t*>(a.q + (size_t)lead * H * 64 + 4 * i);
   for (int i = tid; i < span * 4 * H; i += blockDim.x) {
     const int r = i / (4 * H), c = (i / H) % 4, h = i % H;
     qe[i] = a.qscale[(size_t)(lead + r) * 256 + c * 64 + (h % 16) * 4 + h / 16];
   }
-  for (int ch = ch0; ch < ch1 && ch * kIdxChunk < piece_bound; ++ch) {
-    __syncthreads();  // the previous chunk's readers are done
-    // the chunk's keys: 128 columns x 4 chunks x 16 B, zero past the piece's bound
-    for (int i = tid; i < 4 * kIdxChunk; i += blockDim.x) {
+  // a chunk's keys: 128 columns x 4 chunks x 16 B, zero past the piece's bound; this thread's
+  // kKeyItems of them are loaded into registers one chunk ahead of their use
+  constexpr int kKeyItems = 4 * kIdxChunk / 256;
+  uint4 kv[kKeyItems];
+  uint8_t ks[kKeyItems];
+  auto load_keys = [&](int ch) {
+#pragma unroll
+    for (int u = 0; u < kKeyItems; ++u) {
+      const int i = tid + 256 * u;
       const int c = i / kIdxChunk, cl = i % kIdxChunk, col = ch * kIdxChunk + cl;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      uint8_t s = 127;
+      kv[u] = make_uint4(0, 0, 0, 0);
+      ks[u] = 127;
       if (col < piece_bound && col / a.entry_rows < a.itab_len) {
         const int entry = a.itab[(size_t)owner * a.itab_stride + col / a.entry_rows];
         const long vrow = (long)entry * a.entry_rows + col % a.entry_rows;
         const long page = vrow / kPlaneRows;
         const int slot = (int)(vrow % kPlaneRows);
-        v = ldg16(a.payload + ((page * 4 + c) * kPlaneRows + slot) * 16);
-        s = a.kscale[(page * 4 + c) * kPlaneRows + (slot % 16) * 4 + slot / 16];
+        kv[u] = ldg16(a.payload + ((page * 4 + c) * kPlaneRows + slot) * 16);
+        ks[u] = a.kscale[(page * 4 + c) * kPlaneRows + (slot % 16) * 4 + slot / 16];
       }
-      *reinterpret_cast<uint4*>(keys + (c * kIdxChunk + cl) * 16) = v;
-      ke[c * kIdxChunk + cl] = s;
+    }
+  };
+  if (ch0 < ch1 && ch0 * kIdxChunk < piece_bound) load_keys(ch0);
+  for (int ch = ch0; ch < ch1 && ch * kIdxChunk < piece_bound; ++ch) {
+    __syncthreads();  // the previous chunk's readers are done
+#pragma unroll
+    for (int u = 0; u < kKeyItems; ++u) {
+      // the 16 E2M1 bytes (32 dims) of chunk c of column cl, as f16 at dims 32 c ..
+      const int i = tid + 256 * u;
+      const int c = i / kIdxChunk, cl = i % kIdxChunk;
+      const uint32_t w[4] = {kv[u].x, kv[u].y, kv[u].z, kv[u].w};
+      uint8_t* dst = kf + cl * kIdxRowBytes + 64 * c;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<uint4*>(dst + 16 * q) =
+            make_uint4(e2m1x2_f16(w[q] & 0xff), e2m1x2_f16((w[q] >> 8) & 0xff), e2m1x2_f16((w[q] >> 16) & 0xff),
+                       e2m1x2_f16(w[q] >> 24));
+      ke[c * kIdxChunk + cl] = ks[u];
     }
     __syncthreads();
+    if (ch + 1 < ch1 && (ch + 1) * kIdxChunk < piece_bound) load_keys(ch + 1);
+    // ldmatrix lane addresses: A rows 16 mt + lane % 16, dims + 8 (lane / 16); B columns
+    // 16 warp + 8 (lane / 16) + lane % 8, dims + 8 ((lane / 8) % 2) -- both n-tiles at once
+    const uint32_t qf_s = smem_u32(qf), kf_s = smem_u32(kf);
+    const uint32_t a_lane = (uint32_t)((lane % 16) * kIdxRowBytes + 16 * (lane / 16));
+    const uint32_t b_lane = (uint32_t)((16 * warp + 8 * (lane / 16) + lane % 8) * kIdxRowBytes + 16 * ((lane / 8) % 2));
     for (int r = 0; r < span; ++r) {
       const int row = lead + r, bound = a.bounds[row];
+      // row r's queries as f16 (exact: E2M1 values); the previous row's readers are done
+      if (r > 0) __syncthreads();
+      for (int i = tid; i < H * 16; i += blockDim.x) {
+        const int h = i / 16, wd = i % 16;
+        const uint32_t v = reinterpret_cast<const uint32_t*>(qraw)[(r * H + h) * 16 + wd];
+        *reinterpret_cast<uint4*>(qf + h * kIdxRowBytes + 16 * wd) =
+            make_uint4(e2m1x2_f16(v & 0xff), e2m1x2_f16((v >> 8) & 0xff), e2m1x2_f16((v >> 16) & 0xff),
+                       e2m1x2_f16(v >> 24));
+      }
+      __syncthreads();
+      double s2[2][2] = {{0.0, 0.0}, {0.0, 0.0}};  // [n-tile][column parity]
+      for (int mt = 0; mt < mtiles; ++mt) {
+        double x[2][4] = {{0.0, 0.0, 0.0, 0.0}, {0.0, 0.0, 0.0, 0.0}};
+        const uint32_t qa = qf_s + (uint32_t)(16 * mt * kIdxRowBytes) + a_lane;
 #pragma unroll
-      for (int nn = 0; nn < 2; ++nn) {
-        const int nt = 2 * warp + nn;  // this warp's n-tile: columns 8 nt .. 8 nt + 7
-        const int col_g = 8 * nt + g;  // the B-fragment column of this lane
-        double s[2] = {0.0, 0.0};
-        for (int mt = 0; mt < mtiles; ++mt) {
-          double x[4] = {0.0, 0.0, 0.0, 0.0};
-          const uint8_t* qa = qraw + (r * H + 16 * mt + g) * 68;
+        for (int c = 0; c < 4; ++c) {
+          float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+          for (int ksp = 0; ksp < 2; ++ksp) {
+            uint32_t af[4], bf[4];
+            ldmatrix_x4(af, qa + (uint32_t)((32 * c + 16 * ksp) * 2));
+            ldmatrix_x4(bf, kf_s + b_lane + (uint32_t)((32 * c + 16 * ksp) * 2));
+            mma_f16(acc[0], af[0], af[1], af[2], af[3], bf[0], bf[1]);
+            mma_f16(acc[1], af[0], af[1], af[2], af[3], bf[2], bf[3]);
+          }
 #pragma unroll
-            for (int ks = 0; ks < 2; ++ks) {
-              const int qb = 16 * c + 8 * ks + t;
-              const uint32_t a0 = e2m1x2_f16(qa[qb]), a1 = e2m1x2_f16(qa[8 * 68 + qb]);
-              const uint32_t a2 = e2m1x2_f16(qa[qb + 4]), a3 = e2m1x2_f16(qa[8 * 68 + qb + 4]);
-              const uint8_t* kb = keys + (c * kIdxChunk + col_g) * 16 + 8 * ks + t;
-              const uint32_t b0 = e2m1x2_f16(kb[0]), b1 = e2m1x2_f16(kb[4]);
-              mma_f16(acc, a0, a1, a2, a3, b0, b1);
-            }
+          for (int nn = 0; nn < 2; ++nn) {
+            const int nt = 2 * warp + nn;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const int h = 16 * mt + g + 8 * (q >> 1);
               const int cl = 8 * nt + 2 * t + (q & 1);
               const int e = (int)qe[(r * 4 + c) * H + h] + (int)ke[c * kIdxChunk + cl] - 254;
               const double f = __longlong_as_double((long long)(e + 1023) << 52);
-              x[q] = __dadd_rn(x[q], __dmul_rn((double)acc[q], f));
+              x[nn][q] = __dadd_rn(x[nn][q], __dmul_rn((double)acc[nn][q], f));
             }
           }
+        }
+#pragma unroll
+        for (int nn = 0; nn < 2; ++nn)
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const int h = 16 * mt + g + 8 * (q >> 1);
             const double wv = (double)bf2f(a.w[(size_t)row * H + h]);
             // heads g + 16 mt (q = 0, 1), then g + 8 + 16 mt (q = 2, 3): the tree's order
-            s[q & 1] = __dadd_rn(s[q & 1], __dmul_rn(wv, fmax(x[q], 0.0)));
+            s2[nn][q & 1] = __dadd_rn(s2[nn][q & 1], __dmul_rn(wv, fmax(x[nn][q], 0.0)));
           }
-        }
+      }
+#pragma unroll
+      for (int nn = 0; nn < 2; ++nn) {
+        const int nt = 2 * warp + nn;
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-          double v = s[j];
+          double v = s2[nn][j];
           v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 16));
           v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 8));
           v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
@@ -237,9 +305,13 @@ struct TopkArgs {
   const int32_t* table;
   int table_stride, page;
   const int32_t* owners;
+  int cap;                 // keys the dynamic shared memory holds (the row is staged when n <= cap);
+                           // 32 warp histograms of 256 ints follow them
 };
 
 __global__ void __launch_bounds__(1024) topk_kernel(const TopkArgs a) {
+  extern __shared__ __align__(16) uint32_t s_keys[];
+  int* whist = reinterpret_cast<int*>(s_keys + a.cap);  // [32 warps][256 bins]
   __shared__ int hist[256];
   __shared__ uint32_t s_prefix;
   __shared__ int s_need, s_gt;
@@ -249,7 +321,7 @@ __global__ void __launch_bounds__(1024) topk_kernel(const TopkArgs a) {
   const int nval = a.n[row];
   const int n = a.group > 1 ? (nval + a.group - 1) / a.group : nval;
   int32_t* out = a.out + (size_t)row * a.k;
-  auto key_at = [&](int i) -> uint32_t {
+  auto key_of = [&](int i) -> uint32_t {
     if (a.group <= 1) return order_key(a.vals[(size_t)row * a.vstride + i]);
     uint32_t m = 0;
     for (int j = 0; j < a.group; ++j) {
@@ -258,6 +330,16 @@ __global__ void __launch_bounds__(1024) topk_kernel(const TopkArgs a) {
     }
     return m;
   };
+  // the row's keys go to shared memory once when they fit: the five passes below read them there
+  const bool staged = n <= a.cap;
+  if (tid == 0) {
+    s_prefix = 0;
+    s_need = a.k;
+  }
+  if (staged && n > a.k)
+    for (int i = tid; i < n; i += blockDim.x) s_keys[i] = key_of(i);
+  __syncthreads();  // the staged keys and the radix state are visible to every thread
+  auto key_at = [&](int i) -> uint32_t { return staged ? s_keys[i] : key_of(i); };
   auto emit = [&](int j, int pos) {
     out[j] = pos;
     if (a.page_out) {
@@ -272,19 +354,23 @@ __global__ void __launch_bounds__(1024) topk_kernel(const TopkArgs a) {
     return;
   }
   // ---- radix select: the threshold key T, count(key > T) < k <= count(key >= T)
-  if (tid == 0) {
-    s_prefix = 0;
-    s_need = a.k;
-  }
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 24 - 8 * pass;
-    for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
-    __syncthreads();
     const uint32_t prefix = s_prefix;
     const uint32_t pmask = pass == 0 ? 0u : (0xFFFFFFFFu << (shift + 8));
+    // one histogram a warp (a pass's keys crowd into a few bins: with one shared histogram every
+    // warp's atomics would queue on the same address), summed into hist afterwards
+    for (int i = tid; i < 32 * 256; i += blockDim.x) whist[i] = 0;
+    __syncthreads();
     for (int i = tid; i < n; i += blockDim.x) {
       const uint32_t kk = key_at(i);
-      if ((kk & pmask) == prefix) atomicAdd(&hist[(kk >> shift) & 0xFF], 1);
+      if ((kk & pmask) == prefix) atomicAdd(&whist[warp * 256 + ((kk >> shift) & 0xFF)], 1);
+    }
+    __syncthreads();
+    for (int b = tid; b < 256; b += blockDim.x) {
+      int sum = 0;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) sum += whist[w * 256 + b];
+      hist[b] = sum;
     }
     __syncthreads();
     if (tid == 0) {
