@@ -94,8 +94,9 @@ struct TcSmem {
   static constexpr int kRed = kP + 4 * kPBytes;      // float [4 warps][64 heads]
   static constexpr int kM = kRed + 4 * 64 * 4;       // float [64]: the used max of each head
   static constexpr int kAlpha = kM + 64 * 4;         // float [64]: the rescale of the reference max
-  static constexpr int kMeta = kAlpha + 64 * 4;      // [2 stages][64 keys]: record pointer, then 8 codes
-  static constexpr int kBar = kMeta + 2 * 64 * 16;   // uint64 mbarriers
+  static constexpr int kMetaStages = 3;
+  static constexpr int kMeta = kAlpha + 64 * 4;      // [3 stages][64 keys]: record pointer, then 8 codes
+  static constexpr int kBar = kMeta + kMetaStages * 64 * 16;  // uint64 mbarriers
   static constexpr int kNumBars = 13;
   static constexpr int kMisc = kBar + kNumBars * 8;  // tmem base, abort flag
   static constexpr int kBytes = kMisc + 16;
@@ -145,6 +146,55 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   *abort = 1;
   atomicExch(&g_tc_error, 1);
   return false;
+}
+// The same with cluster-scope acquire: the arrivals come from the other CTA of a pair too (its
+// producers' remote stores, its MMA completions).
+__device__ __forceinline__ bool mbar_try_cl(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P1;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P1, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, P1;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cl(uint32_t bar, uint32_t parity, volatile int* abort) {
+  for (uint32_t it = 0; it < kTcWaitPolls; ++it) {
+    if (mbar_try_cl(bar, parity)) return true;
+    if ((it & 255) == 255 && *abort) return false;
+  }
+  *abort = 1;
+  atomicExch(&g_tc_error, 1);
+  return false;
+}
+// Cluster plumbing for a CTA pair: the peer's address of a shared-memory location, a store
+// there, an arrival on the peer's mbarrier (release at cluster scope), both CTAs' barrier.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster16(uint32_t addr, const uint4& v) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void fence_async_cluster() {
+  asm volatile("fence.proxy.async.shared::cluster;" ::: "memory");
+}
+// the MMAs' completion arrives on the mbarrier at this offset in both CTAs of the pair
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"((uint16_t)3)
+      : "memory");
 }
 // AND of a predicate over the 224 producer threads (named barrier 2), for the same reason.
 __device__ __forceinline__ bool producers_all(bool v) {
@@ -215,7 +265,11 @@ __device__ __forceinline__ int core_off(int r, int c) {
   return (r >> 3) * (C / 8) * 128 + (c >> 3) * 128 + (r & 7) * 16 + (c & 7) * 2;
 }
 
-template <int NOPE>
+// PAIR: the row's two 32-head tiles run as a cluster of two CTAs that share every key tile:
+// each CTA's producers gather and convert half of the tile's keys (key groups 4 r .. 4 r + 3 of
+// CTA rank r) and store them into both CTAs' tiles; a tile is full after both CTAs' producer
+// warps arrived (14) and free after both CTAs' PV finished with it (2 commit arrivals).
+template <int NOPE, bool PAIR>
 __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs A) {
   constexpr int D = NOPE + 64;
   constexpr int DG = D / 8;                 // 16-byte core columns a row
@@ -259,10 +313,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
     *reinterpret_cast<uint4*>(smem + L::kQ + core_off<D>(h, 8 * c)) = v;
   }
   if (tid == 0) {
-    mbar_init(bar(0), 7);
-    mbar_init(bar(1), 7);
-    mbar_init(bar(2), 1);
-    mbar_init(bar(3), 1);
+    mbar_init(bar(0), PAIR ? 14 : 7);
+    mbar_init(bar(1), PAIR ? 14 : 7);
+    mbar_init(bar(2), PAIR ? 2 : 1);
+    mbar_init(bar(3), PAIR ? 2 : 1);
     mbar_init(bar(4), 1);
     mbar_init(bar(5), 1);
     mbar_init(bar(6), 4);
@@ -286,8 +340,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
+  // the peer's barriers are initialized before anything of this CTA reaches its shared memory
+  if (PAIR) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = *tmem_base;
+  const int rank = PAIR ? ht : 0;  // head tile = rank in the pair (consecutive blocks form a cluster)
+  const uint32_t peer_smem = PAIR ? cluster_map(smem_u32(smem), (uint32_t)(rank ^ 1)) : 0u;
   // TMEM columns: S^T[s] at 32 s (NH), s = the sub-block's parity; O^T block b at 64 + 64 b
   // (2 NH: the head pass's columns, then the tail pass's)
   const uint32_t tm_s = tmem, tm_o = tmem + 64;
@@ -303,19 +361,28 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
     static_assert(CHUNKS % 4 == 0, "records are whole 64-byte runs");
     const int ptid = tid - 5 * 32, wp = warp - 5;
     const int data_bytes = NOPE + 128;
-    const uint8_t** meta_p = reinterpret_cast<const uint8_t**>(smem + L::kMeta);  // [2][64] then codes
-    uint64_t* meta_c = reinterpret_cast<uint64_t*>(smem + L::kMeta + 2 * 64 * 8);
-    constexpr int kUnits = (kTcKeys / 8) * (CHUNKS / 4);
+    // loads run kAhead tiles ahead of the conversion: two for a pair (its producers hold half a
+    // tile's chunks, so three tiles' fit in registers), else one
+    constexpr int kAhead = PAIR ? 2 : 1;
+    constexpr int kStages = kAhead + 1;  // metadata stages: tiles j .. j + kAhead
+    static_assert(kStages <= L::kMetaStages, "metadata stages");
+    const uint8_t** meta_p = reinterpret_cast<const uint8_t**>(smem + L::kMeta);  // [stage][64] then codes
+    uint64_t* meta_c = reinterpret_cast<uint64_t*>(smem + L::kMeta + L::kMetaStages * 64 * 8);
+    constexpr int kGroups = PAIR ? kTcKeys / 16 : kTcKeys / 8;  // 8-key groups this CTA converts
+    constexpr int kUnits = kGroups * (CHUNKS / 4);
     constexpr int kItems = (kUnits + kTcProducers / 32 - 1) / (kTcProducers / 32);
+    constexpr int kMetaKeys = 8 * kGroups;  // keys this CTA locates: threads ptid < kMetaKeys
+    const int g0 = PAIR ? rank * kGroups : 0;
+    const int mkey = 8 * g0 + ptid;  // thread ptid's key of a tile (ptid < kMetaKeys)
     auto item = [&](int i, int& key, int& c) {  // this lane's (key, chunk) of its i-th unit
       const int u = wp + (kTcProducers / 32) * i;
-      key = 8 * (u % 8) + (lane & 7);
-      c = 4 * (u / 8) + (lane >> 3);
+      key = 8 * (g0 + u % kGroups) + (lane & 7);
+      c = 4 * (u / kGroups) + (lane >> 3);
       return u < kUnits;
     };
-    // key lookahead (threads ptid < 64, key ptid of a tile)
+    // key lookahead (threads ptid < kMetaKeys, key mkey of a tile)
     auto kt_load = [&](int j) {  // the key-table entry; -1 past the chunk
-      const int k = k0 + j * kTcKeys + ptid;
+      const int k = k0 + j * kTcKeys + mkey;
       return k < k1 ? a.kt[(size_t)t * a.keys_ld + k] : -1;
     };
     const uint8_t* la_p = nullptr;  // tile j + 2's record and scale-code word (load in flight)
@@ -334,34 +401,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
       }
     };
     auto publish = [&](int j) {
-      meta_p[(j & 1) * 64 + ptid] = la_p;
-      meta_c[(j & 1) * 64 + ptid] = la_c;
+      meta_p[(j % kStages) * 64 + mkey] = la_p;
+      meta_c[(j % kStages) * 64 + mkey] = la_c;
     };
     auto issue = [&](int j, uint4 (&raw)[kItems]) {
-      const int s = j & 1;
+      const int ms = j % kStages;
 #pragma unroll
       for (int i = 0; i < kItems; ++i) {
         int key, c;
         raw[i] = make_uint4(0, 0, 0, 0);
         if (item(i, key, c)) {
-          const uint8_t* dp = meta_p[s * 64 + key];
+          const uint8_t* dp = meta_p[ms * 64 + key];
           if (dp) raw[i] = ldg16(dp + 16 * c);
         }
       }
     };
     auto convert = [&](int j, const uint4 (&raw)[kItems]) {
-      const int s = j & 1;
-      uint8_t* tile = smem + (s ? L::kTile1 : L::kTile0);
+      const int s = j & 1, ms = j % kStages;
+      const int tile_off = s ? L::kTile1 : L::kTile0;
+      // into this CTA's tile and, for a pair, the peer's
+      auto put = [&](int off, const uint4& v) {
+        *reinterpret_cast<uint4*>(smem + tile_off + off) = v;
+        if (PAIR) st_cluster16(peer_smem + (uint32_t)(tile_off + off), v);
+      };
 #pragma unroll
       for (int i = 0; i < kItems; ++i) {
         int key, c;
         if (!item(i, key, c)) continue;
         const int b0 = 16 * c;
-        const bool live = meta_p[s * 64 + key] != nullptr;
+        const bool live = meta_p[ms * 64 + key] != nullptr;
         if (b0 < NOPE) {
           uint4 o0 = make_uint4(0, 0, 0, 0), o1 = o0;
           if (live) {
-            const int cd = (int)((meta_c[s * 64 + key] >> (8 * (b0 / 64))) & 0xff);
+            const int cd = (int)((meta_c[ms * 64 + key] >> (8 * (b0 / 64))) & 0xff);
             const uint32_t w[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
             uint32_t r[8];
             if (cd >= 113 && cd <= 134) {
@@ -384,60 +456,89 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
             o0 = make_uint4(r[0], r[1], r[2], r[3]);
             o1 = make_uint4(r[4], r[5], r[6], r[7]);
           }
-          *reinterpret_cast<uint4*>(tile + core_off<D>(key, b0)) = o0;
-          *reinterpret_cast<uint4*>(tile + core_off<D>(key, b0 + 8)) = o1;
+          put(core_off<D>(key, b0), o0);
+          put(core_off<D>(key, b0 + 8), o1);
         } else {
           uint4 o0 = make_uint4(0, 0, 0, 0);
           if (live)
             o0 = make_uint4(bf16x2_to_f16x2(raw[i].x), bf16x2_to_f16x2(raw[i].y), bf16x2_to_f16x2(raw[i].z),
                             bf16x2_to_f16x2(raw[i].w));
-          *reinterpret_cast<uint4*>(tile + core_off<D>(key, NOPE + (b0 - NOPE) / 2)) = o0;
+          put(core_off<D>(key, NOPE + (b0 - NOPE) / 2), o0);
         }
       }
-      fence_async_smem();
+      if (PAIR)
+        fence_async_cluster();
+      else
+        fence_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(s));
+      if (lane == 0) {
+        mbar_arrive(bar(s));
+        if (PAIR) mbar_arrive_remote(cluster_map(bar(s), (uint32_t)(rank ^ 1)));
+      }
     };
     // one tile: free its stage, publish and issue the next tile, convert this one (cur holds its
     // chunks; nxt receives the next tile's)
-    int la_v = -1;  // tile j + 3's key-table entry (load in flight)
+    int la_v = -1;  // tile j + kAhead + 2's key-table entry (load in flight)
+    // one tile: once its stage is free, convert it (a pair first: its chunks were loaded two
+    // tiles ago), publish and issue tile j + kAhead's loads into nxt, locate tile j + kAhead + 1
     auto step = [&](int j, const uint4 (&cur)[kItems], uint4 (&nxt)[kItems]) {
       const int s = j & 1;
       // the stage is free (PV(j - 2) done), for every producer alike; and every producer is past
       // tile j - 1's conversion (its metadata stage is rewritten next)
-      if (!producers_all(j < 2 || mbar_wait(bar(2 + s), ((j >> 1) - 1) & 1, abort))) return false;
+      if (!producers_all(j < 2 || (PAIR ? mbar_wait_cl(bar(2 + s), ((j >> 1) - 1) & 1, abort)
+                                        : mbar_wait(bar(2 + s), ((j >> 1) - 1) & 1, abort))))
+        return false;
       if (ptid == 0) TC_TRACE(j, 0);
-      if (j + 1 < nsub) {
-        if (ptid < 64) publish(j + 1);
+      if (PAIR) {
+        convert(j, cur);
+        if (ptid == 0) TC_TRACE(j, 1);
+      }
+      if (j + kAhead < nsub) {
+        if (ptid < kMetaKeys) publish(j + kAhead);
         asm volatile("bar.sync 2, %0;" ::"n"(kTcProducers) : "memory");
         if (ptid == 0) TC_TRACE(j, 14);
-        issue(j + 1, nxt);
+        issue(j + kAhead, nxt);
         if (ptid == 0) TC_TRACE(j, 15);
       }
-      if (ptid < 64) {
+      if (ptid < kMetaKeys) {
         locate(la_v);
-        la_v = kt_load(j + 3);
+        la_v = kt_load(j + kAhead + 2);
       }
       if (ptid == 0) TC_TRACE(j, 4);
-      convert(j, cur);
-      if (ptid == 0) TC_TRACE(j, 1);
+      if (!PAIR) {
+        convert(j, cur);
+        if (ptid == 0) TC_TRACE(j, 1);
+      }
       return true;
     };
     uint4 buf0[kItems], buf1[kItems];
     if (nsub > 0) {
-      if (ptid < 64) {
-        locate(kt_load(0));
-        publish(0);
-        const int v1 = kt_load(1);
-        la_v = kt_load(2);
-        locate(v1);
+      if (ptid < kMetaKeys) {
+#pragma unroll
+        for (int i = 0; i < kAhead; ++i) {
+          locate(kt_load(i));
+          publish(i);
+        }
+        const int v = kt_load(kAhead);
+        la_v = kt_load(kAhead + 1);
+        locate(v);
       }
       asm volatile("bar.sync 2, %0;" ::"n"(kTcProducers) : "memory");
       issue(0, buf0);
     }
-    for (int j = 0; j < nsub; j += 2) {
-      if (!step(j, buf0, buf1)) break;
-      if (j + 1 < nsub && !step(j + 1, buf1, buf0)) break;
+    if constexpr (PAIR) {
+      uint4 buf2[kItems];
+      if (nsub > 1) issue(1, buf1);
+      for (int j = 0; j < nsub; j += 3) {
+        if (!step(j, buf0, buf2)) break;
+        if (j + 1 < nsub && !step(j + 1, buf1, buf0)) break;
+        if (j + 2 < nsub && !step(j + 2, buf2, buf1)) break;
+      }
+    } else {
+      for (int j = 0; j < nsub; j += 2) {
+        if (!step(j, buf0, buf1)) break;
+        if (j + 1 < nsub && !step(j + 1, buf1, buf0)) break;
+      }
     }
   } else if (warp == 4) {
     // ================= MMA issue (one elected thread)
@@ -458,10 +559,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
         TC_TRACE(j, 11);
       };
       auto qk_ready = [&](int j) {  // tile j loaded and S[j & 1] consumed by softmax(j - 2)
-        return mbar_try(bar(j & 1), (j >> 1) & 1) && (j < 2 || mbar_try(bar(6 + (j & 1)), ((j - 2) >> 1) & 1));
+        return (PAIR ? mbar_try_cl(bar(j & 1), (j >> 1) & 1) : mbar_try(bar(j & 1), (j >> 1) & 1)) &&
+               (j < 2 || mbar_try(bar(6 + (j & 1)), ((j - 2) >> 1) & 1));
       };
       auto wait_qk = [&](int j) {
-        return mbar_wait(bar(j & 1), (j >> 1) & 1, abort) &&
+        return (PAIR ? mbar_wait_cl(bar(j & 1), (j >> 1) & 1, abort) : mbar_wait(bar(j & 1), (j >> 1) & 1, abort)) &&
                (j < 2 || mbar_wait(bar(6 + (j & 1)), ((j - 2) >> 1) & 1, abort));
       };
       bool ok = true;
@@ -501,7 +603,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
             umma_f16(tm_o + 64 * b, umma_sdesc(tile + (d0 / 8) * 128 + 2 * ks * DG * 128, DG * 128, 128),
                      umma_sdesc(pt + 2 * ks * (2 * NH / 8) * 128, (2 * NH / 8) * 128, 128), id_pv, j > 0 || ks > 0);
         }
-        umma_commit(bar(2 + s));   // the tile is free
+        if (PAIR)
+          umma_commit_pair(bar(2 + s));  // the tile is free, in both CTAs
+        else
+          umma_commit(bar(2 + s));  // the tile is free
         umma_commit(bar(10 + s));  // P[s] free; O holds sub-blocks 0 .. j
         if (!qk_done) {
           ok = wait_qk(j + 1);
@@ -580,31 +685,43 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
 #pragma unroll
         for (int q = 0; q < 32; ++q) sv[q] = (valid && q < NH) ? __uint_as_float(v[q]) * a.scale_log2 : -INFINITY;
       }
-      // per-head max of the sub-block: 16 key lanes, then the 4 warps (through red)
+      // The reference max moves only when a score passes it by more than the slack (in the
+      // first sub-block with a valid key, rarely after): only then the sub-block's per-head max,
+      // over the 16 key lanes and then the 4 warps (through red)
+      bool exceed = false;
 #pragma unroll
-      for (int q = 0; q < 32; ++q) {
-        float x = sv[q];
-        x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 1));
-        x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 2));
-        x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 4));
-        x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 8));
-        if (lane == 0) red[warp * 32 + q] = x;
+      for (int q = 0; q < 32; q += 4) {
+        const float4 m4 = *reinterpret_cast<const float4*>(m_sm + q);
+        exceed |= (sv[q] > m4.x + kTcSlack) | (sv[q + 1] > m4.y + kTcSlack) | (sv[q + 2] > m4.z + kTcSlack) |
+                  (sv[q + 3] > m4.w + kTcSlack);
       }
-      softmax_bar();  // red complete
-      if (tid == 0) TC_TRACE(j, 6);
-      bool moved = false;  // a head's reference moved while O already holds its sums
-      if (tid < NH) {
-        const float bx = fmaxf(fmaxf(red[tid], red[32 + tid]), fmaxf(red[64 + tid], red[96 + tid]));
-        const float mu = m_sm[tid];
-        float al = 1.f;
-        if (bx > mu + kTcSlack) {
-          al = (mu == -INFINITY) ? 0.f : exp2f(mu - bx);
-          moved = mu != -INFINITY;
-          m_sm[tid] = bx;
+      bool rescale = false;
+      if (softmax_any(exceed)) {
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+          float x = sv[q];
+          x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 1));
+          x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 2));
+          x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 4));
+          x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 8));
+          if (lane == 0) red[warp * 32 + q] = x;
         }
-        a_sm[tid] = al;
+        softmax_bar();  // red complete
+        if (tid == 0) TC_TRACE(j, 6);
+        bool moved = false;  // a head's reference moved while O already holds its sums
+        if (tid < NH) {
+          const float bx = fmaxf(fmaxf(red[tid], red[32 + tid]), fmaxf(red[64 + tid], red[96 + tid]));
+          const float mu = m_sm[tid];
+          float al = 1.f;
+          if (bx > mu + kTcSlack) {
+            al = (mu == -INFINITY) ? 0.f : exp2f(mu - bx);
+            moved = mu != -INFINITY;
+            m_sm[tid] = bx;
+          }
+          a_sm[tid] = al;
+        }
+        rescale = softmax_any(moved) && j > 0;  // also publishes m_sm / a_sm
       }
-      const bool rescale = softmax_any(moved) && j > 0;  // also publishes m_sm / a_sm
       if (tid == 0) TC_TRACE(j, 9);
       if (rescale) {
         // O must hold every issued PV before it is scaled
@@ -713,9 +830,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
       a.part_ml[(base + tid) * 2 + 1] = 0.f;
     }
   }
-  // ---- teardown: every role done (a timed-out one unwound); free the TMEM
+  // ---- teardown: every role done (a timed-out one unwound); free the TMEM. A pair leaves
+  // together: the peer's stores and MMA-completion arrivals target this CTA's shared memory
+  // until its own roles are done.
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync_all();
   if (warp == 4) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));

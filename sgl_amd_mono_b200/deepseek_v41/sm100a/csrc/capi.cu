@@ -68,6 +68,17 @@ bool use_tc_attention() {
   return v == 1;
 }
 
+// A row's two 32-head tiles as one CTA pair sharing key tiles (default), or two lone CTAs that
+// each gather every key (DSV41_ATTN_PAIR=0), for comparison.
+bool use_attn_pair() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("DSV41_ATTN_PAIR");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 bool use_pdl() {
   static int v = -1;
   if (v < 0) {
@@ -173,8 +184,10 @@ void dense_replan(GemvArgs& g, int sms) {
   if (dense_eligible(g)) g.kslices = dense_args(g, nullptr, nullptr, sms).kslices;
 }
 
+// cluster_x > 1: consecutive blocks along x form clusters of that size
 template <typename Kern, typename Args>
-cudaError_t launch(Kern kernel, dim3 grid, dim3 block, int smem, cudaStream_t st, const Args& args) {
+cudaError_t launch(Kern kernel, dim3 grid, dim3 block, int smem, cudaStream_t st, const Args& args,
+                   int cluster_x = 1) {
   g_launches.fetch_add(1, std::memory_order_relaxed);
   if (smem > 48 * 1024) {
     cudaError_t e = ensure_smem(reinterpret_cast<const void*>(kernel), smem);
@@ -185,11 +198,18 @@ cudaError_t launch(Kern kernel, dim3 grid, dim3 block, int smem, cudaStream_t st
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = use_pdl() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (cluster_x > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)cluster_x;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  }
   return cudaLaunchKernelEx(&cfg, kernel, args);
 }
 
@@ -535,12 +555,15 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   mark(a->events, 0, st);
   if (tc) {
     AttnTcArgs ta = {at, heads >= 32 ? 32 : std::max(16, cdiv(heads, 16) * 16), head_tiles};
+    // a row's two head tiles share their key tiles as a CTA pair
+    const bool pair = head_tiles == 2 && use_attn_pair();
+    const dim3 grid(M * nchunks * head_tiles), block(kTcThreads);
     if (nope == 512)
-      DSV41_TRY(launch(attn_tc_kernel<512>, dim3(M * nchunks * head_tiles), dim3(kTcThreads), TcSmem<576>::kBytes,
-                       st, ta));
+      DSV41_TRY(pair ? launch(attn_tc_kernel<512, true>, grid, block, TcSmem<576>::kBytes, st, ta, 2)
+                     : launch(attn_tc_kernel<512, false>, grid, block, TcSmem<576>::kBytes, st, ta));
     else
-      DSV41_TRY(launch(attn_tc_kernel<448>, dim3(M * nchunks * head_tiles), dim3(kTcThreads), TcSmem<512>::kBytes,
-                       st, ta));
+      DSV41_TRY(pair ? launch(attn_tc_kernel<448, true>, grid, block, TcSmem<512>::kBytes, st, ta, 2)
+                     : launch(attn_tc_kernel<448, false>, grid, block, TcSmem<512>::kBytes, st, ta));
   } else {
     DSV41_TRY(launch(attn_split_kernel, dim3(M * nchunks * head_tiles), dim3(256), attn_smem_bytes(D), st, at));
   }
@@ -708,12 +731,13 @@ int dsv41_topk(const Dsv41TopkArgs* a, void* stream) {
   if (!a || a->rows < 1 || a->k < 1 || a->k > 65536 || !a->vals || !a->n || !a->out || a->group < 1 ||
       (a->page_out && (!a->table || !a->owners || a->page < 1)))
     return DSV41_EINVAL;
-  // a row has at most vstride values, hence at most ceil(vstride / group) candidates
-  const int cap = std::min<int>(40960, ((int)a->vstride + (int)a->group - 1) / (int)a->group);
+  // a row has at most vstride values, hence at most ceil(vstride / group) candidates (rounded up
+  // to a multiple of 4: the kernel reads the staged keys four at a time)
+  const int cap = (std::min<int>(40960, ((int)a->vstride + (int)a->group - 1) / (int)a->group) + 3) / 4 * 4;
   TopkArgs t = {(int)a->rows, (int)a->k, ptr<const float>(a->vals), (int)a->vstride, ptr<const int32_t>(a->n),
                 (int)a->group, ptr<int32_t>(a->out), ptr<int32_t>(a->page_out), ptr<const int32_t>(a->table),
                 (int)a->table_stride, (int)a->page, ptr<const int32_t>(a->owners), cap};
-  DSV41_TRY(launch(topk_kernel, dim3((int)a->rows), dim3(1024), cap * 4 + 32 * 256 * 4,
+  DSV41_TRY(launch(topk_kernel, dim3((int)a->rows), dim3(1024), cap * 4 + kTopkBins * 4,
                    reinterpret_cast<cudaStream_t>(stream), t));
   return launch_status();
 }

@@ -305,135 +305,220 @@ struct TopkArgs {
   const int32_t* table;
   int table_stride, page;
   const int32_t* owners;
-  int cap;                 // keys the dynamic shared memory holds (the row is staged when n <= cap);
-                           // 32 warp histograms of 256 ints follow them
+  int cap;                 // keys the dynamic shared memory holds (a multiple of 4; the row is staged
+                           // when n <= cap); a 4096-bin histogram follows them
 };
 
+constexpr int kTopkBins = 4096;  // 12-bit digits (bits 31..20, then 19..8), then 8 bits (7..0)
+
 __global__ void __launch_bounds__(1024) topk_kernel(const TopkArgs a) {
-  extern __shared__ __align__(16) uint32_t s_keys[];
-  int* whist = reinterpret_cast<int*>(s_keys + a.cap);  // [32 warps][256 bins]
-  __shared__ int hist[256];
+  extern __shared__ __align__(16) uint32_t s_keys[];  // [cap], then the histogram
+  int* hist = reinterpret_cast<int*>(s_keys + a.cap);
   __shared__ uint32_t s_prefix;
-  __shared__ int s_need, s_gt;
-  __shared__ int warp_cnt[32], warp_tie[32];
+  __shared__ int s_need;
+  __shared__ int s_warp[32], s_warp2[32];
   const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nthr = (int)blockDim.x, nwarps = nthr >> 5;
   pdl_wait();
   const int nval = a.n[row];
   const int n = a.group > 1 ? (nval + a.group - 1) / a.group : nval;
   int32_t* out = a.out + (size_t)row * a.k;
+  const float* vrow = a.vals + (size_t)row * a.vstride;
   auto key_of = [&](int i) -> uint32_t {
-    if (a.group <= 1) return order_key(a.vals[(size_t)row * a.vstride + i]);
+    if (a.group <= 1) return order_key(vrow[i]);
     uint32_t m = 0;
     for (int j = 0; j < a.group; ++j) {
       const int p = i * a.group + j;
-      if (p < nval) m = max(m, order_key(a.vals[(size_t)row * a.vstride + p]));
+      if (p < nval) m = max(m, order_key(vrow[p]));
     }
     return m;
   };
-  // the row's keys go to shared memory once when they fit: the five passes below read them there
+  // the row's keys go to shared memory once when they fit: the passes below read them there,
+  // four a thread at a time
   const bool staged = n <= a.cap;
   if (tid == 0) {
     s_prefix = 0;
     s_need = a.k;
   }
   if (staged && n > a.k)
-    for (int i = tid; i < n; i += blockDim.x) s_keys[i] = key_of(i);
+#pragma unroll 4
+    for (int i = tid; i < n; i += nthr) s_keys[i] = key_of(i);
   __syncthreads();  // the staged keys and the radix state are visible to every thread
-  auto key_at = [&](int i) -> uint32_t { return staged ? s_keys[i] : key_of(i); };
+  const int32_t* tbl = a.page_out ? a.table + (size_t)__ldg(a.owners + row) * a.table_stride : nullptr;
   auto emit = [&](int j, int pos) {
     out[j] = pos;
-    if (a.page_out) {
-      int32_t slot = -1;
-      if (pos >= 0)
-        slot = a.table[(size_t)a.owners[row] * a.table_stride + pos / a.page] * a.page + pos % a.page;
-      a.page_out[(size_t)row * a.k + j] = slot;
-    }
+    if (a.page_out) a.page_out[(size_t)row * a.k + j] = pos >= 0 ? __ldg(tbl + pos / a.page) * a.page + pos % a.page : -1;
   };
   if (n <= a.k) {
-    for (int j = tid; j < a.k; j += blockDim.x) emit(j, j < n ? j : -1);
+    for (int j = tid; j < a.k; j += nthr) emit(j, j < n ? j : -1);
     return;
   }
-  // ---- radix select: the threshold key T, count(key > T) < k <= count(key >= T)
-  for (int pass = 0; pass < 4; ++pass) {
-    const int shift = 24 - 8 * pass;
+  // keys p .. p + 3 (p a multiple of 4; past `end` read as 0 and flagged out)
+  auto load4 = [&](int p, int end, uint32_t (&kq)[4]) {
+    if (staged) {
+      const uint4 v = *reinterpret_cast<const uint4*>(s_keys + p);
+      kq[0] = v.x;
+      kq[1] = v.y;
+      kq[2] = v.z;
+      kq[3] = v.w;
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) kq[q] = p + q < end ? key_of(p + q) : 0u;
+    }
+  };
+  // ---- radix select: the threshold key T, count(key > T) < k <= count(key >= T), in three
+  // passes (12, 12, 8 bits); a 12-bit first digit spreads even logits of a few exponents over
+  // many bins, so plain shared atomics do
+  for (int pass = 0; pass < 3; ++pass) {
+    const int shift = pass == 0 ? 20 : (pass == 1 ? 8 : 0);
+    const int nb = pass == 2 ? 256 : kTopkBins;
+    const uint32_t pmask = pass == 0 ? 0u : (0xFFFFFFFFu << (pass == 1 ? 20 : 8));
     const uint32_t prefix = s_prefix;
-    const uint32_t pmask = pass == 0 ? 0u : (0xFFFFFFFFu << (shift + 8));
-    // one histogram a warp (a pass's keys crowd into a few bins: with one shared histogram every
-    // warp's atomics would queue on the same address), summed into hist afterwards
-    for (int i = tid; i < 32 * 256; i += blockDim.x) whist[i] = 0;
+    const int need = s_need;
+    for (int i = tid; i < nb; i += nthr) hist[i] = 0;
     __syncthreads();
-    for (int i = tid; i < n; i += blockDim.x) {
-      const uint32_t kk = key_at(i);
-      if ((kk & pmask) == prefix) atomicAdd(&whist[warp * 256 + ((kk >> shift) & 0xFF)], 1);
+    for (int p = 4 * tid; p < n; p += 4 * nthr) {
+      uint32_t kq[4];
+      load4(p, n, kq);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (p + q < n && (kq[q] & pmask) == prefix) atomicAdd(&hist[(kq[q] >> shift) & (nb - 1)], 1);
     }
     __syncthreads();
-    for (int b = tid; b < 256; b += blockDim.x) {
-      int sum = 0;
-      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) sum += whist[w * 256 + b];
-      hist[b] = sum;
+    // the digit d with S(d + 1) < need <= S(d), S(d) = count of bins >= d: thread t holds bins
+    // 4 t .. 4 t + 3; a block-wide suffix sum finds the one thread the crossing falls in
+    int c[4], own = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      c[q] = 4 * tid + q < nb ? hist[4 * tid + q] : 0;
+      own += c[q];
     }
+    int incl = own;  // this thread's bins and every higher lane's of the warp
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int o = __shfl_down_sync(0xffffffffu, incl, d);
+      if (lane + d < 32) incl += o;
+    }
+    if (lane == 0) s_warp[warp] = incl;
     __syncthreads();
-    if (tid == 0) {
-      int need = s_need, d = 255;
-      for (; d > 0; --d) {
-        if (hist[d] >= need) break;
-        need -= hist[d];
+    if (warp == 0) {
+      const int wt = lane < nwarps ? s_warp[lane] : 0;
+      int ws = wt;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int o = __shfl_down_sync(0xffffffffu, ws, d);
+        if (lane + d < 32) ws += o;
       }
-      s_need = need;
+      if (lane < nwarps) s_warp2[lane] = ws - wt;  // the warps above
+    }
+    __syncthreads();
+    incl += s_warp2[warp];
+    const int above = incl - own;
+    if (above < need && need <= incl) {
+      int acc = above, d = 4 * tid;
+#pragma unroll
+      for (int q = 3; q >= 0; --q) {
+        if (acc + c[q] >= need) {
+          d = 4 * tid + q;
+          break;
+        }
+        acc += c[q];
+      }
+      s_need = need - acc;
       s_prefix = prefix | ((uint32_t)d << shift);
     }
     __syncthreads();
   }
   const uint32_t T = s_prefix;
   const int ties_taken = s_need;  // how many keys equal to T are selected (lowest positions)
-  // ---- ordered compaction: thread i handles positions [i c, i c + c)
-  const int per = (n + blockDim.x - 1) / blockDim.x;
-  const int p0 = min(n, tid * per), p1 = min(n, p0 + per);
+  // ---- ordered compaction (exactly k selections): warp w walks positions [w seg, (w + 1) seg)
+  // 128 at a time, lane l holding positions + 4 l .. + 3; counts, then emits in order by scans
+  const int seg = ((n + nwarps - 1) / nwarps + 127) / 128 * 128;
+  const int p0 = min(n, warp * seg), p1 = min(n, p0 + seg);
   int cnt_gt = 0, cnt_eq = 0;
-  for (int p = p0; p < p1; ++p) {
-    const uint32_t kk = key_at(p);
-    cnt_gt += kk > T;
-    cnt_eq += kk == T;
-  }
-  // exclusive scans of the ties (for the tie budget) and of the selections
-  auto block_excl_scan = [&](int v, int* buf, int& total) {
-    int incl = v;
-    for (int d = 1; d < 32; d <<= 1) {
-      const int o = __shfl_up_sync(0xffffffffu, incl, d);
-      if (lane >= d) incl += o;
-    }
-    if (lane == 31) buf[warp] = incl;
-    __syncthreads();
-    if (warp == 0) {
-      int w = lane < (int)(blockDim.x >> 5) ? buf[lane] : 0;
-      for (int d = 1; d < 32; d <<= 1) {
-        const int o = __shfl_up_sync(0xffffffffu, w, d);
-        if (lane >= d) w += o;
+  for (int base = p0; base < p1; base += 128) {
+    const int p = base + 4 * lane;
+    if (p >= p1) continue;
+    uint32_t kq[4];
+    load4(p, p1, kq);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (p + q < p1) {
+        cnt_gt += kq[q] > T;
+        cnt_eq += kq[q] == T;
       }
-      buf[lane] = w;  // inclusive warp totals
-    }
-    __syncthreads();
-    total = buf[(blockDim.x >> 5) - 1];
-    const int before = (warp > 0 ? buf[warp - 1] : 0) + incl - v;
-    __syncthreads();
-    return before;
-  };
-  int tot;
-  const int eq_before = block_excl_scan(cnt_eq, warp_tie, tot);
-  const int eq_mine = max(0, min(cnt_eq, ties_taken - eq_before));
-  const int sel = cnt_gt + eq_mine;
-  const int sel_before = block_excl_scan(sel, warp_cnt, tot);
-  int j = sel_before, eq_seen = 0;
-  for (int p = p0; p < p1; ++p) {
-    const uint32_t kk = key_at(p);
-    bool take = kk > T;
-    if (kk == T) {
-      take = eq_seen < eq_mine;
-      ++eq_seen;
-    }
-    if (take) emit(j++, p);
   }
-  for (int q = tot + tid; q < a.k; q += blockDim.x) emit(q, -1);
+  cnt_gt = __reduce_add_sync(0xffffffffu, cnt_gt);
+  cnt_eq = __reduce_add_sync(0xffffffffu, cnt_eq);
+  // exclusive scans over the warps: of the ties (for the tie budget), then of the selections
+  if (lane == 0) {
+    s_warp[warp] = cnt_gt;
+    s_warp2[warp] = cnt_eq;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int te = lane < nwarps ? s_warp2[lane] : 0, ge = lane < nwarps ? s_warp[lane] : 0;
+    int ti = te;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, ti, d);
+      if (lane >= d) ti += o;
+    }
+    const int eq_mine = max(0, min(te, ties_taken - (ti - te)));
+    const int sel = ge + eq_mine;
+    int si = sel;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, si, d);
+      if (lane >= d) si += o;
+    }
+    if (lane < nwarps) {
+      s_warp2[lane] = eq_mine;  // this warp's ties to take
+      s_warp[lane] = si - sel;  // this warp's first output slot
+    }
+  }
+  __syncthreads();
+  const int eq_mine = s_warp2[warp];
+  int j = s_warp[warp], eq_seen = 0;  // warp-uniform
+  for (int base = p0; base < p1; base += 128) {
+    const int p = base + 4 * lane;
+    uint32_t kq[4] = {0u, 0u, 0u, 0u};
+    if (p < p1) load4(p, p1, kq);
+    bool gt[4], eq[4];
+    int ne = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      gt[q] = p + q < p1 && kq[q] > T;
+      eq[q] = p + q < p1 && kq[q] == T;
+      ne += eq[q];
+    }
+    int ei = ne;  // ties at this lane's positions and the lanes' below
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, ei, d);
+      if (lane >= d) ei += o;
+    }
+    int seen = eq_seen + ei - ne, nt = 0;
+    bool take[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      take[q] = gt[q] || (eq[q] && seen < eq_mine);
+      seen += eq[q];
+      nt += take[q];
+    }
+    int tsum = nt;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, tsum, d);
+      if (lane >= d) tsum += o;
+    }
+    int slot = j + tsum - nt;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (take[q]) emit(slot++, p + q);
+    j += __shfl_sync(0xffffffffu, tsum, 31);
+    eq_seen += __shfl_sync(0xffffffffu, ei, 31);
+  }
   pdl_launch();
 }
 
