@@ -346,42 +346,90 @@ struct CombineArgs {
   __nv_bfloat16* xo;       // [M, heads * D]
 };
 
-__global__ void attn_combine_kernel(const CombineArgs a) {
+// One CTA a (row, head): the chunks' weights 2^(m_c - m) (0 for an empty chunk) go to shared
+// memory first and one thread sums the denominator in chunk order; then each thread sums 4 dims
+// over the chunks in order, with 8 chunks' loads in flight (the same sums, in the same order, as
+// one chunk at a time).
+constexpr int kCombineThreads = 160;
+__global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(const CombineArgs a) {
+  extern __shared__ float s_w[];  // [nchunks] weights, then [nchunks] the chunks' sums of p
+  float* s_l = s_w + a.nchunks;
+  __shared__ float s_red[kCombineThreads / 32];
+  __shared__ float s_m, s_inv;
   pdl_wait();
-  const int t = blockIdx.x / a.heads, h = blockIdx.x % a.heads;
+  const int t = blockIdx.x / a.heads, h = blockIdx.x % a.heads, tid = threadIdx.x, lane = tid & 31;
+  const int nw = (int)(blockDim.x >> 5);
   const float sink2 = a.sink[h] * kLog2e;
-  float m = sink2;
-  for (int c = 0; c < a.nchunks; ++c) m = fmaxf(m, a.part_ml[(((size_t)t * a.nchunks + c) * a.heads + h) * 2]);
-  float l = exp2f(sink2 - m);
-  for (int c = 0; c < a.nchunks; ++c) {
-    const float* ml = a.part_ml + (((size_t)t * a.nchunks + c) * a.heads + h) * 2;
-    if (ml[0] != -INFINITY) l += ml[1] * exp2f(ml[0] - m);
+  const float* ml = a.part_ml + ((size_t)t * a.nchunks * a.heads + h) * 2;  // chunk c at + c * heads * 2
+  float mx = sink2;
+  for (int c = tid; c < a.nchunks; c += blockDim.x) mx = fmaxf(mx, ml[(size_t)c * a.heads * 2]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) s_red[tid >> 5] = mx;
+  __syncthreads();
+  if (tid == 0) {
+    float m = s_red[0];
+    for (int w = 1; w < nw; ++w) m = fmaxf(m, s_red[w]);
+    s_m = m;
   }
-  const float inv = 1.0f / l;
+  __syncthreads();
+  const float m = s_m;
+  for (int c = tid; c < a.nchunks; c += blockDim.x) {
+    const float mc = ml[(size_t)c * a.heads * 2], lc = ml[(size_t)c * a.heads * 2 + 1];
+    const float w = mc == -INFINITY ? 0.f : exp2f(mc - m);
+    s_w[c] = w;
+    s_l[c] = lc;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float l = exp2f(sink2 - m);
+    for (int c = 0; c < a.nchunks; ++c)
+      if (s_w[c] != 0.f) l = fmaf(s_l[c], s_w[c], l);
+    s_inv = 1.0f / l;
+  }
+  __syncthreads();
+  const float inv = s_inv;
   const int64_t p = rope_row(a.pos[t], a.rope_rows);
-  for (int d2 = threadIdx.x; d2 < a.D / 2; d2 += blockDim.x) {
-    const int d = 2 * d2;
-    float v0 = 0.f, v1 = 0.f;
-    for (int c = 0; c < a.nchunks; ++c) {
-      const size_t base = ((size_t)t * a.nchunks + c) * a.heads + h;
-      const float mc = a.part_ml[base * 2];
-      if (mc == -INFINITY) continue;
-      const float w = exp2f(mc - m);
-      const float2 ov = *reinterpret_cast<const float2*>(a.part_o + base * a.D + d);
-      v0 += ov.x * w;
-      v1 += ov.y * w;
+  const float* po = a.part_o + ((size_t)t * a.nchunks * a.heads + h) * a.D;  // chunk c at + c * heads * D
+  const size_t cstride = (size_t)a.heads * a.D;
+  for (int d4 = tid; d4 < a.D / 4; d4 += blockDim.x) {
+    const int d = 4 * d4;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int c0 = 0; c0 < a.nchunks; c0 += 8) {
+      float4 ov[8];
+      float wv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + u;
+        wv[u] = c < a.nchunks ? s_w[c] : 0.f;
+        ov[u] = wv[u] != 0.f ? *reinterpret_cast<const float4*>(po + c * cstride + d) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (wv[u] == 0.f) continue;
+        v[0] += ov[u].x * wv[u];
+        v[1] += ov[u].y * wv[u];
+        v[2] += ov[u].z * wv[u];
+        v[3] += ov[u].w * wv[u];
+      }
     }
-    v0 = bf16r(v0 * inv);
-    v1 = bf16r(v1 * inv);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = bf16r(v[i] * inv);
     if (d >= a.nope) {
-      const int j = (d - a.nope) >> 1;
-      const float c = a.cos_sin[p * a.rope + j], s = a.cos_sin[p * a.rope + a.rope / 2 + j];
-      const float e0 = __fadd_rn(__fmul_rn(v0, c), __fmul_rn(v1, s));
-      const float e1 = __fsub_rn(__fmul_rn(v1, c), __fmul_rn(v0, s));
-      v0 = e0;
-      v1 = e1;
+#pragma unroll
+      for (int i = 0; i < 4; i += 2) {
+        const int j = (d + i - a.nope) >> 1;
+        const float c = a.cos_sin[p * a.rope + j], s = a.cos_sin[p * a.rope + a.rope / 2 + j];
+        const float e0 = __fadd_rn(__fmul_rn(v[i], c), __fmul_rn(v[i + 1], s));
+        const float e1 = __fsub_rn(__fmul_rn(v[i + 1], c), __fmul_rn(v[i], s));
+        v[i] = e0;
+        v[i + 1] = e1;
+      }
     }
-    *reinterpret_cast<uint32_t*>(a.xo + ((size_t)t * a.heads + h) * a.D + d) = pack_bf16x2(v0, v1);
+    uint2 pk;
+    pk.x = pack_bf16x2(v[0], v[1]);
+    pk.y = pack_bf16x2(v[2], v[3]);
+    *reinterpret_cast<uint2*>(a.xo + ((size_t)t * a.heads + h) * a.D + d) = pk;
   }
   pdl_launch();
 }

@@ -5,22 +5,23 @@
 //   warps 0-3  softmax + epilogue (each owns the TMEM lane quarter of its warp index),
 //   warp  4    TMEM allocation and the MMA issue (one elected thread),
 //   warps 5-11 producers: 64-key sub-blocks of FP8 records -> an f16 tile in shared memory.
-// Per sub-block j (tile, P and O_sub buffers j & 1; one S buffer, released as soon as the
-// softmax threads hold it in registers):
-//   S^T[64 keys x NH heads]  = K_tile . Q^T      tcgen05.mma M=64 (keys), N=NH, K=D: A = the tile
+// A row's two head tiles run as a cluster of two CTAs (PAIR) that share every key tile: each
+// converts half of the tile's keys into both CTAs' shared memory.
+// Per sub-block j (tile, S and P buffers j & 1):
+//   S^T[64 keys x NH heads] = K_tile . Q^T        tcgen05.mma M=64 (keys), N=NH, K=D: A = the tile
 //                                                (K-major), B = Q (K-major), D in TMEM;
-//   softmax over keys (the threads holding keys 16 w + lane, lane < 16, of warp w) with the
-//   running max per head;
-//   O_sub^T[D dims x NH heads] = V_tile^T . P^T  M=128 (dims, in 128-dim blocks), N=NH, K=64
+//   softmax over keys (the threads holding keys 16 w + lane, lane < 16, of warp w) against a
+//   per-head reference max that moves only when a score passes it by more than 2^8 (then O is
+//   rescaled in TMEM);
+//   O^T[D dims x 2 NH] += V_tile^T . P^T          M=128 (dims, in 128-dim blocks), N=2 NH, K=64
 //                                                keys: A = the same tile read MN-major, B = P^T
-//                                                (MN-major, written by the softmax threads) --
-//                                                twice into the same accumulator: P's f16 head,
-//                                                then its f16 tail (p keeps ~22 bits, as the
-//                                                averages over thousands of keys need);
-//   O_acc = O_acc * alpha + O_sub by the softmax threads two sub-blocks later (one fp32 FMA an
-//   element), so the softmax never waits for the PV just issued: the tensor core's
-//   accumulation into TMEM truncates, so a chunk's thousands of keys are summed 8 MMA steps at
-//   a time in hardware and across sub-blocks in round-to-nearest fp32.
+//                                                (MN-major, written by the softmax threads) whose
+//                                                columns are p's f16 head (0 .. NH - 1), then its
+//                                                f16 tail: p keeps ~22 bits, and head and tail
+//                                                accumulate in separate TMEM columns, summed in
+//                                                fp32 by the epilogue (the tensor core's fp32
+//                                                accumulation truncates: a tail added into the
+//                                                head's columns lost its precision).
 // The tile is stored as 8 x 16-byte core matrices: element (key, d) at
 //   (key / 8) * (D / 8) * 128 + (d / 8) * 128 + (key % 8) * 16 + (d % 8) * 2,
 // which is the K-major layout of the QK operand (leading offset 128 B, stride (D / 8) * 128 B)
@@ -221,6 +222,12 @@ __device__ __forceinline__ bool softmax_any(bool v) {
   return r != 0;
 }
 __device__ __forceinline__ void softmax_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// The maximum of v over the warp's 32 lanes, in every lane (one instruction on sm_100a).
+__device__ __forceinline__ float warp_max_f32(float v) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
+}
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -298,6 +305,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
 
   pdl_wait();
   TC_SPAN(0);
+  if (tid == 0) TC_TRACE(62, 0);  // timeline row 62: start, setup done; row 63: the epilogue
   const int kv = a.klen[t];
   const int k0 = ch * a.chunk_keys, k1 = min(k0 + a.chunk_keys, kv);
   const int nsub = k1 > k0 ? (k1 - k0 + kTcKeys - 1) / kTcKeys : 0;
@@ -343,6 +351,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
   // the peer's barriers are initialized before anything of this CTA reaches its shared memory
   if (PAIR) cluster_sync_all();
   tc_fence_after();
+  if (tid == 0) TC_TRACE(62, 1);
   const uint32_t tmem = *tmem_base;
   const int rank = PAIR ? ht : 0;  // head tile = rank in the pair (consecutive blocks form a cluster)
   const uint32_t peer_smem = PAIR ? cluster_map(smem_u32(smem), (uint32_t)(rank ^ 1)) : 0u;
@@ -697,14 +706,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
       }
       bool rescale = false;
       if (softmax_any(exceed)) {
+        // (lanes 16 .. 31 hold no key: -inf)
 #pragma unroll
         for (int q = 0; q < 32; ++q) {
-          float x = sv[q];
-          x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 1));
-          x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 2));
-          x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 4));
-          x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 8));
-          if (lane == 0) red[warp * 32 + q] = x;
+          const float x = warp_max_f32(sv[q]);
+          if (lane == q) red[warp * 32 + q] = x;
         }
         softmax_bar();  // red complete
         if (tid == 0) TC_TRACE(j, 6);
@@ -785,26 +791,35 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
     }
     // ---- epilogue: every PV done, then O^T (head + tail columns) and (m, l) of the chunk
     if (ok && nsub > 0) ok = softmax_all(mbar_wait(bar(10 + ((nsub - 1) & 1)), ((nsub - 1) >> 1) & 1, abort));
+    if (tid == 0) TC_TRACE(63, 0);
     const size_t base = ((size_t)t * a.nchunks + ch) * a.heads + h0;
     const int nh_live = min(NH, a.heads - h0);
     if (ok && nsub > 0) {
       tc_fence_after();
-      // l: the partial sums of the 64 key threads (16 lanes x 4 warps)
+      // l: the partial sums of the 64 key threads (16 lanes x 4 warps). A transposing reduction
+      // over the warp: each step halves the heads a lane holds and exchanges the other half with
+      // the partner lane, so lane h ends with the warp's sum of head h (31 shuffles in 5
+      // dependent steps, against 4 dependent shuffles for each of the 32 heads)
 #pragma unroll
-      for (int h = 0; h < 32; ++h) {
-        if (h >= NH) break;
-        float x = has_key ? l_part[h] : 0.f;
-        x += __shfl_xor_sync(0xffffffffu, x, 1);
-        x += __shfl_xor_sync(0xffffffffu, x, 2);
-        x += __shfl_xor_sync(0xffffffffu, x, 4);
-        x += __shfl_xor_sync(0xffffffffu, x, 8);
-        if (lane == 0) red[warp * 32 + h] = x;
+      for (int h = 0; h < 32; ++h)
+        if (!has_key || h >= NH) l_part[h] = 0.f;
+#pragma unroll
+      for (int step = 16; step >= 1; step >>= 1) {
+        const bool upper = (lane & step) != 0;
+#pragma unroll
+        for (int i = 0; i < step; ++i) {
+          const float send = upper ? l_part[i] : l_part[i + step];
+          const float keep = upper ? l_part[i + step] : l_part[i];
+          l_part[i] = keep + __shfl_xor_sync(0xffffffffu, send, step);
+        }
       }
+      red[warp * 32 + lane] = l_part[0];
       softmax_bar();
       if (tid < nh_live) {
         a.part_ml[(base + tid) * 2] = m_sm[tid];
         a.part_ml[(base + tid) * 2 + 1] = (red[tid] + red[32 + tid]) + (red[64 + tid] + red[96 + tid]);
       }
+      if (tid == 0) TC_TRACE(63, 1);
       const int dl = 32 * warp + lane;  // this thread's dim within a block
 #pragma unroll 1
       for (int b = 0; b < NBLK; ++b) {
@@ -833,9 +848,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
   // ---- teardown: every role done (a timed-out one unwound); free the TMEM. A pair leaves
   // together: the peer's stores and MMA-completion arrivals target this CTA's shared memory
   // until its own roles are done.
+  if (tid == 0) TC_TRACE(63, 2);
   tc_fence_before();
   __syncthreads();
   if (PAIR) cluster_sync_all();
+  if (tid == 0) TC_TRACE(63, 3);
   if (warp == 4) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));

@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(256) k2i_score_kernel(const K2iArgs a) {
   uint8_t* qraw = smem;                                  // [span][H][64] E2M1 bytes
   uint8_t* qf = qraw + kIdxMaxSpan * H * 64;             // [H] rows of 128 f16 dims: the current row
   uint8_t* kf = qf + H * kIdxRowBytes;                   // [128 columns] rows of 128 f16 dims
-  uint8_t* qe = kf + kIdxChunk * kIdxRowBytes;           // [span][4][H]
+  uint8_t* qe = kf + kIdxChunk * kIdxRowBytes;           // [span][H][4]: a head's 4 chunk codes in a word
   uint8_t* ke = qe + kIdxMaxSpan * 4 * H;                // [4][128]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   pdl_wait();
@@ -166,7 +166,7 @@ __global__ void __launch_bounds__(256) k2i_score_kernel(const K2iArgs a) {
   for (int i = tid; i < span * H * 16; i += blockDim.x)
     reinterpret_cast<uint32_t*>(qraw)[i] = *reinterpret_cast<const uint32_t*>(a.q + (size_t)lead * H * 64 + 4 * i);
   for (int i = tid; i < span * 4 * H; i += blockDim.x) {
-    const int r = i / (4 * H), c = (i / H) % 4, h = i % H;
+    const int r = i / (4 * H), h = (i / 4) % H, c = i % 4;
     qe[i] = a.qscale[(size_t)(lead + r) * 256 + c * 64 + (h % 16) * 4 + h / 16];
   }
   // a chunk's keys: 128 columns x 4 chunks x 16 B, zero past the piece's bound; this thread's
@@ -215,20 +215,38 @@ __global__ void __launch_bounds__(256) k2i_score_kernel(const K2iArgs a) {
     const uint32_t qf_s = smem_u32(qf), kf_s = smem_u32(kf);
     const uint32_t a_lane = (uint32_t)((lane % 16) * kIdxRowBytes + 16 * (lane / 16));
     const uint32_t b_lane = (uint32_t)((16 * warp + 8 * (lane / 16) + lane % 8) * kIdxRowBytes + 16 * ((lane / 8) % 2));
+    // this thread's key codes of the chunk: columns 16 warp + 8 nn + 2 t + j, byte 2 nn + j of
+    // word c
+    uint32_t kev[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint8_t* kc = ke + c * kIdxChunk + 16 * warp + 2 * t;
+      kev[c] = (uint32_t)*reinterpret_cast<const uint16_t*>(kc) |
+               ((uint32_t)*reinterpret_cast<const uint16_t*>(kc + 8) << 16);
+    }
     for (int r = 0; r < span; ++r) {
       const int row = lead + r, bound = a.bounds[row];
-      // row r's queries as f16 (exact: E2M1 values); the previous row's readers are done
-      if (r > 0) __syncthreads();
-      for (int i = tid; i < H * 16; i += blockDim.x) {
-        const int h = i / 16, wd = i % 16;
-        const uint32_t v = reinterpret_cast<const uint32_t*>(qraw)[(r * H + h) * 16 + wd];
-        *reinterpret_cast<uint4*>(qf + h * kIdxRowBytes + 16 * wd) =
-            make_uint4(e2m1x2_f16(v & 0xff), e2m1x2_f16((v >> 8) & 0xff), e2m1x2_f16((v >> 16) & 0xff),
-                       e2m1x2_f16(v >> 24));
+      // row r's queries as f16 (exact: E2M1 values), once a chunk (a one-row piece: once)
+      if (span > 1 || ch == ch0) {
+        if (r > 0) __syncthreads();  // the previous row's readers are done
+        for (int i = tid; i < H * 16; i += blockDim.x) {
+          const int h = i / 16, wd = i % 16;
+          const uint32_t v = reinterpret_cast<const uint32_t*>(qraw)[(r * H + h) * 16 + wd];
+          *reinterpret_cast<uint4*>(qf + h * kIdxRowBytes + 16 * wd) =
+              make_uint4(e2m1x2_f16(v & 0xff), e2m1x2_f16((v >> 8) & 0xff), e2m1x2_f16((v >> 16) & 0xff),
+                         e2m1x2_f16(v >> 24));
+        }
+        __syncthreads();
       }
-      __syncthreads();
       double s2[2][2] = {{0.0, 0.0}, {0.0, 0.0}};  // [n-tile][column parity]
-      for (int mt = 0; mt < mtiles; ++mt) {
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt) {
+        if (mt >= mtiles) break;
+        // heads 16 mt + g (q = 0, 1) and 16 mt + g + 8 (q = 2, 3): their chunk codes and weights
+        const uint32_t qw0 = *reinterpret_cast<const uint32_t*>(qe + (r * H + 16 * mt + g) * 4);
+        const uint32_t qw1 = *reinterpret_cast<const uint32_t*>(qe + (r * H + 16 * mt + g + 8) * 4);
+        const double wv0 = (double)bf2f(a.w[(size_t)row * H + 16 * mt + g]);
+        const double wv1 = (double)bf2f(a.w[(size_t)row * H + 16 * mt + g + 8]);
         double x[2][4] = {{0.0, 0.0, 0.0, 0.0}, {0.0, 0.0, 0.0, 0.0}};
         const uint32_t qa = qf_s + (uint32_t)(16 * mt * kIdxRowBytes) + a_lane;
 #pragma unroll
@@ -242,28 +260,24 @@ __global__ void __launch_bounds__(256) k2i_score_kernel(const K2iArgs a) {
             mma_f16(acc[0], af[0], af[1], af[2], af[3], bf[0], bf[1]);
             mma_f16(acc[1], af[0], af[1], af[2], af[3], bf[2], bf[3]);
           }
+          const uint32_t qb0 = (qw0 >> (8 * c)) & 0xffu, qb1 = (qw1 >> (8 * c)) & 0xffu;
 #pragma unroll
-          for (int nn = 0; nn < 2; ++nn) {
-            const int nt = 2 * warp + nn;
+          for (int nn = 0; nn < 2; ++nn)
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              const int h = 16 * mt + g + 8 * (q >> 1);
-              const int cl = 8 * nt + 2 * t + (q & 1);
-              const int e = (int)qe[(r * 4 + c) * H + h] + (int)ke[c * kIdxChunk + cl] - 254;
-              const double f = __longlong_as_double((long long)(e + 1023) << 52);
-              x[nn][q] = __dadd_rn(x[nn][q], __dmul_rn((double)acc[nn][q], f));
+              // 2^(qe + ke - 254) as a double (biased exponent qe + ke + 769); acc times it is
+              // exact, so the fused add rounds as the separate multiply and add would
+              const uint32_t kb = (kev[c] >> (16 * nn + 8 * (q & 1))) & 0xffu;
+              const double f = __hiloint2double((int)(((q >> 1) ? qb1 : qb0) + kb + 769u) << 20, 0);
+              x[nn][q] = __fma_rn((double)acc[nn][q], f, x[nn][q]);
             }
-          }
         }
 #pragma unroll
         for (int nn = 0; nn < 2; ++nn)
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int h = 16 * mt + g + 8 * (q >> 1);
-            const double wv = (double)bf2f(a.w[(size_t)row * H + h]);
+          for (int q = 0; q < 4; ++q)
             // heads g + 16 mt (q = 0, 1), then g + 8 + 16 mt (q = 2, 3): the tree's order
-            s2[nn][q & 1] = __dadd_rn(s2[nn][q & 1], __dmul_rn(wv, fmax(x[nn][q], 0.0)));
-          }
+            s2[nn][q & 1] = __dadd_rn(s2[nn][q & 1], __dmul_rn((q >> 1) ? wv1 : wv0, fmax(x[nn][q], 0.0)));
       }
 #pragma unroll
       for (int nn = 0; nn < 2; ++nn) {
