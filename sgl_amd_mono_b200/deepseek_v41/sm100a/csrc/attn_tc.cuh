@@ -796,23 +796,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
     const int nh_live = min(NH, a.heads - h0);
     if (ok && nsub > 0) {
       tc_fence_after();
-      // l: the partial sums of the 64 key threads (16 lanes x 4 warps). A transposing reduction
-      // over the warp: each step halves the heads a lane holds and exchanges the other half with
-      // the partner lane, so lane h ends with the warp's sum of head h (31 shuffles in 5
-      // dependent steps, against 4 dependent shuffles for each of the 32 heads)
+      // l: the partial sums of the 64 key threads (16 lanes x 4 warps), lane h taking head h
 #pragma unroll
       for (int h = 0; h < 32; ++h)
         if (!has_key || h >= NH) l_part[h] = 0.f;
-#pragma unroll
-      for (int step = 16; step >= 1; step >>= 1) {
-        const bool upper = (lane & step) != 0;
-#pragma unroll
-        for (int i = 0; i < step; ++i) {
-          const float send = upper ? l_part[i] : l_part[i + step];
-          const float keep = upper ? l_part[i + step] : l_part[i];
-          l_part[i] = keep + __shfl_xor_sync(0xffffffffu, send, step);
-        }
-      }
+      warp_transpose_sum(l_part, lane);
       red[warp * 32 + lane] = l_part[0];
       softmax_bar();
       if (tid < nh_live) {

@@ -317,6 +317,7 @@ bool k1_ok(const Dsv41K1Args* a) {
   if (a->build_kt && a->topk_width > 0 && (!a->topk_idx || !a->topk_lens)) return false;
   if (a->index && !a->qr) return false;
   if (a->hidden % 128 || a->q_lora % 128) return false;
+  if (a->q % 16) return false;  // q_rope stores 8 bf16 (16 bytes) at a time
   return true;
 }
 
@@ -395,7 +396,7 @@ int k1_run(const Dsv41K1Args* a, cudaStream_t st, bool go, int64_t* need) {
   qr.part = g2.out; qr.cos_sin = ptr<const float>(a->cos_sin); qr.pos = ptr<const int64_t>(a->pos);
   qr.rope_rows = a->rope_rows;
   qr.q = ptr<__nv_bfloat16>(a->q);
-  DSV41_TRY(launch(q_rope_kernel, dim3(cdiv(heads * D / 2, 256), M), dim3(256), 0, st, qr));
+  DSV41_TRY(launch(q_rope_kernel, dim3(cdiv(heads * D / 8, 256), M), dim3(256), 0, st, qr));
   mark(a->events, 4, st);
   return launch_status();
 }
@@ -413,6 +414,7 @@ bool k2_ok(const Dsv41K2Args* a) {
   if (a->tp > 1 && a->phase == 0 && (!a->peers || a->peer_cap < a->M * a->hidden || a->peer_cap % 8))
     return false;
   if (a->phase == 2 && (!a->attn || !a->moe_part)) return false;
+  if (a->moe_part % 16) return false;  // the MoE combine stores 8 bf16 (16 bytes) at a time
   if (a->phase == 1 && !a->attn_part) return false;
   if (!a->q || !a->kt || !a->klen || !a->swa || !a->sink || !a->woa || !a->wob) return false;
   // KV records are fetched by bulk copies: page bases and strides 16-byte aligned
@@ -645,7 +647,7 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   }
   CombineMoeArgs cm = {M, H, TK, ed.kslices, gd.kslices, ed.out, ptr<const float>(a->wts), gd.out, moe_part};
   mark(a->events, 6, st);
-  DSV41_TRY(launch(moe_combine_kernel, dim3(grid_for((int64_t)M * H, 256)), dim3(256), 0, st, cm));
+  DSV41_TRY(launch(moe_combine_kernel, dim3(grid_for((int64_t)M * H / 8, 256)), dim3(256), 0, st, cm));
   if (phase == 2) return launch_status();
   if (tp > 1) {
     // the MoE all-reduce (site 2)

@@ -76,6 +76,52 @@ __device__ __forceinline__ float warp_sum(float v) {
   for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
   return v;
 }
+// v[q] = the sum over k < kslices of src[k kstride + q] (q < 8), added in k order from 0.f; the
+// loads of 4 slices (two 16-byte loads each) are in flight together, where a loop of scalar
+// loads a value would wait out one memory latency a slice. src 16-byte aligned, kstride a
+// multiple of 4 floats.
+__device__ __forceinline__ void sum_slices8(const float* src, size_t kstride, int kslices, float (&v)[8]) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) v[q] = 0.f;
+  int k = 0;
+  for (; k + 4 <= kslices; k += 4) {
+    float4 u[4][2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4* p = reinterpret_cast<const float4*>(src + (size_t)(k + i) * kstride);
+      u[i][0] = p[0];
+      u[i][1] = p[1];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[0] += u[i][0].x; v[1] += u[i][0].y; v[2] += u[i][0].z; v[3] += u[i][0].w;
+      v[4] += u[i][1].x; v[5] += u[i][1].y; v[6] += u[i][1].z; v[7] += u[i][1].w;
+    }
+  }
+  for (; k < kslices; ++k) {
+    const float4* p = reinterpret_cast<const float4*>(src + (size_t)k * kstride);
+    const float4 a = p[0], b = p[1];
+    v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+    v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+  }
+}
+// 32 sums over the warp at once: lane l ends with the warp's sum of v[l] (v is consumed). Each
+// step halves the values a lane holds and exchanges the other half with the xor partner, so
+// value j meets the same partners in the same order (16, 8, 4, 2, 1) as warp_sum(v[j]) and
+// gives the same bits, in 31 shuffles over 5 dependent steps instead of 160 over 5 x 32.
+__device__ __forceinline__ float warp_transpose_sum(float (&v)[32], int lane) {
+#pragma unroll
+  for (int step = 16; step >= 1; step >>= 1) {
+    const bool upper = (lane & step) != 0;
+#pragma unroll
+    for (int i = 0; i < step; ++i) {
+      const float send = upper ? v[i] : v[i + step];
+      const float keep = upper ? v[i + step] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, step);
+    }
+  }
+  return v[0];
+}
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, d));

@@ -23,12 +23,9 @@ __global__ void finalize_kernel(const FinalizeArgs a) {
     const bool live = i < total;
     const int t = live ? i / g8 : 0, c = live ? (i % g8) * 8 : 0;
     float v[8];
+    sum_slices8(a.part + (size_t)t * a.N + c, (size_t)a.M * a.N, live ? a.kslices : 0, v);
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      float s = 0.f;
-      for (int k = 0; live && k < a.kslices; ++k) s += a.part[((size_t)k * a.M + t) * a.N + c + q];
-      v[q] = bf16r(s);
-    }
+    for (int q = 0; q < 8; ++q) v[q] = bf16r(v[q]);
     uint32_t o[4];
     if (a.q8) {
       float amax = 0.f;

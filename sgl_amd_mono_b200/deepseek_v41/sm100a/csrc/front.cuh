@@ -39,29 +39,58 @@ __global__ void __launch_bounds__(256) front_qkv_kernel(const FrontArgs a) {
   const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int W = a.QL + a.KVD;
   pdl_wait();
-  auto qkv = [&](int n) {
-    float v = a.qkv_part[(size_t)t * W + n];
-    for (int s = 1; s < a.kslices; ++s) v += a.qkv_part[((size_t)s * a.M + t) * W + n];
-    if (a.qkv_out) a.qkv_out[(size_t)t * W + n] = v;
-    return v;
-  };
-  // ---- q: 4 consecutive values a thread (QL <= 1024), q_norm, bf16, vLLM MXFP8
-  const int qper = a.QL / 256;  // values a thread: 1, 2 or 4 (QL 256, 512, 1024)
+  // the wqkv_a partials of this thread's values summed over the K slices in order, four slices'
+  // loads in flight at a time: q values tid qper + i (qper = QL / 256 <= 4), kv values
+  // QL + tid + 64 r (threads tid < 64, r < R <= 12)
+  const int qper = a.QL / 256;
+  const int R = a.KVD / 64;
+  const bool kvt = tid < 64;
   float xq[4] = {0.f, 0.f, 0.f, 0.f};
+  float xk[12];
+#pragma unroll
+  for (int r = 0; r < 12; ++r) xk[r] = 0.f;
+  {
+    const float* base = a.qkv_part + (size_t)t * W;
+    const size_t sstride = (size_t)a.M * W;
+    for (int s0 = 0; s0 < a.kslices; s0 += 4) {
+      float uq[4][4], uk[4][12];
+#pragma unroll
+      for (int ds = 0; ds < 4; ++ds) {
+        const bool in = s0 + ds < a.kslices;
+        const float* b = base + (size_t)(s0 + ds) * sstride;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) uq[ds][i] = (in && i < qper) ? b[tid * qper + i] : 0.f;
+#pragma unroll
+        for (int r = 0; r < 12; ++r) uk[ds][r] = (in && kvt && r < R) ? b[a.QL + tid + 64 * r] : 0.f;
+      }
+#pragma unroll
+      for (int ds = 0; ds < 4; ++ds) {
+        if (s0 + ds >= a.kslices) break;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) xq[i] += uq[ds][i];
+#pragma unroll
+        for (int r = 0; r < 12; ++r) xk[r] += uk[ds][r];
+      }
+    }
+    if (a.qkv_out) {
+      for (int i = 0; i < qper; ++i) a.qkv_out[(size_t)t * W + tid * qper + i] = xq[i];
+      if (kvt)
+        for (int r = 0; r < R; ++r) a.qkv_out[(size_t)t * W + a.QL + tid + 64 * r] = xk[r];
+    }
+  }
+  // ---- q: 4 consecutive values a thread (QL <= 1024), q_norm, bf16, vLLM MXFP8
   float ss = 0.f;
   for (int i = 0; i < qper; ++i) {
-    xq[i] = bf16r(qkv(tid * qper + i));
+    xq[i] = bf16r(xq[i]);
     ss = fmaf(xq[i], xq[i], ss);
   }
   ss = warp_sum(ss);
   if (lane == 0) red[warp] = ss;
   // ---- kv: 64 threads, thread i holds dims i + 64 r (fixed-order fp64 sum of squares)
-  const int R = a.KVD / 64;
-  float xk[12];
-  if (tid < 64) {
+  if (kvt) {
     double acc = 0.0;
     for (int r = 0; r < R; ++r) {
-      xk[r] = bf16r(qkv(a.QL + tid + 64 * r));
+      xk[r] = bf16r(xk[r]);
       acc = __dadd_rn(acc, __dmul_rn((double)xk[r], (double)xk[r]));
     }
     acc = warp_sum_d(acc);
@@ -159,31 +188,33 @@ struct QRopeArgs {
   __nv_bfloat16* q;        // [M, heads, D]
 };
 
-// q = bf16(wq_b partials summed); GPT-J RoPE of each head's dims past nope; bf16.
+// q = bf16(wq_b partials summed); GPT-J RoPE of each head's dims past nope; bf16. A thread = 8
+// consecutive dims (never across a head or the nope boundary: D and nope are multiples of 8).
 __global__ void q_rope_kernel(const QRopeArgs a) {
   pdl_wait();
   const int t = blockIdx.y;
   const int N = a.heads * a.D;
-  for (int pr = blockIdx.x * blockDim.x + threadIdx.x; pr < N / 2; pr += gridDim.x * blockDim.x) {
-    const int n = 2 * pr;
-    float v0 = a.part[(size_t)t * N + n], v1 = a.part[(size_t)t * N + n + 1];
-    for (int s = 1; s < a.kslices; ++s) {
-      v0 += a.part[((size_t)s * a.M + t) * N + n];
-      v1 += a.part[((size_t)s * a.M + t) * N + n + 1];
-    }
-    v0 = bf16r(v0);
-    v1 = bf16r(v1);
+  for (int g8 = blockIdx.x * blockDim.x + threadIdx.x; g8 < N / 8; g8 += gridDim.x * blockDim.x) {
+    const int n = 8 * g8;
+    float v[8];
+    sum_slices8(a.part + (size_t)t * N + n, (size_t)a.M * N, a.kslices, v);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v[q] = bf16r(v[q]);
     const int d = n % a.D;
     if (d >= a.nope) {
-      const int j = (d - a.nope) >> 1;
       const int64_t p = rope_row(a.pos[t], a.rope_rows);
-      const float c = a.cos_sin[p * a.rope + j], s = a.cos_sin[p * a.rope + a.rope / 2 + j];
-      const float e0 = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, s));
-      const float e1 = __fadd_rn(__fmul_rn(v0, s), __fmul_rn(v1, c));
-      v0 = e0;
-      v1 = e1;
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        const int j = (d + i - a.nope) >> 1;
+        const float c = a.cos_sin[p * a.rope + j], s = a.cos_sin[p * a.rope + a.rope / 2 + j];
+        const float e0 = __fsub_rn(__fmul_rn(v[i], c), __fmul_rn(v[i + 1], s));
+        const float e1 = __fadd_rn(__fmul_rn(v[i], s), __fmul_rn(v[i + 1], c));
+        v[i] = e0;
+        v[i + 1] = e1;
+      }
     }
-    *reinterpret_cast<uint32_t*>(a.q + (size_t)t * N + n) = pack_bf16x2(v0, v1);
+    *reinterpret_cast<uint4*>(a.q + (size_t)t * N + n) =
+        make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
   }
   pdl_launch();
 }

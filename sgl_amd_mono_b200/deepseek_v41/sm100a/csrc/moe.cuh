@@ -292,16 +292,13 @@ __global__ void expert_act_kernel(const ExpertActArgs a) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < padded; i += gridDim.x * blockDim.x) {
     const bool live = i < total;
     const int p = live ? i / groups8 : 0, c = live ? (i % groups8) * 8 : 0;
-    float v[8];
+    float v[8], gs[8], us[8];
+    const float* row = a.part + (size_t)p * 2 * a.I;
+    sum_slices8(row + c, (size_t)a.P * 2 * a.I, live ? a.kslices : 0, gs);
+    sum_slices8(row + a.I + c, (size_t)a.P * 2 * a.I, live ? a.kslices : 0, us);
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      float gg = 0.f, uu = 0.f;
-      for (int s = 0; live && s < a.kslices; ++s) {
-        const float* row = a.part + ((size_t)s * a.P + p) * 2 * a.I;
-        gg += row[c + q];
-        uu += row[a.I + c + q];
-      }
-      const float gc = fminf(gg, kLimit), uc = fminf(fmaxf(uu, -kLimit), kLimit);
+      const float gc = fminf(gs[q], kLimit), uc = fminf(fmaxf(us[q], -kLimit), kLimit);
       v[q] = bf16r(gc * (1.0f / (1.0f + expf(-gc))) * uc);
     }
     float amax = 0.f;
@@ -343,17 +340,14 @@ __global__ void shared_act_kernel(const SharedActArgs a) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < padded; i += gridDim.x * blockDim.x) {
     const bool live = i < total;
     const int t = live ? i / groups8 : 0, c = live ? (i % groups8) * 8 : 0;
-    float v[8];
+    float v[8], gs[8], us[8];
+    const float* row = a.part + (size_t)t * 2 * a.SI;
+    sum_slices8(row + c, (size_t)a.M * 2 * a.SI, live ? a.kslices : 0, gs);
+    sum_slices8(row + a.SI + c, (size_t)a.M * 2 * a.SI, live ? a.kslices : 0, us);
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      float gg = 0.f, uu = 0.f;
-      for (int s = 0; live && s < a.kslices; ++s) {
-        const float* row = a.part + ((size_t)s * a.M + t) * 2 * a.SI;
-        gg += row[c + q];
-        uu += row[a.SI + c + q];
-      }
-      const float gq = bf16r(fminf(bf16r(gg), kLimit));
-      const float uq = fminf(fmaxf(bf16r(uu), -kLimit), kLimit);
+      const float gq = bf16r(fminf(bf16r(gs[q]), kLimit));
+      const float uq = fminf(fmaxf(bf16r(us[q]), -kLimit), kLimit);
       const float act = bf16r(gq / (1.0f + expf(-gq)));
       v[q] = bf16r(act * uq);
     }
@@ -389,21 +383,53 @@ struct CombineMoeArgs {
   __nv_bfloat16* out;    // [M, H]: bf16(routed + shared)
 };
 
-// routed = bf16(routed + bf16(y_k w_k)) in top-k order; out = bf16(routed + bf16(shared)).
+// routed = bf16(routed + bf16(y_k w_k)) in top-k order; out = bf16(routed + bf16(shared)). A
+// thread = 8 consecutive columns of a row; slice by slice, the loads of 8 picks are in flight
+// together (each pick's slices still added in slice order).
 __global__ void moe_combine_kernel(const CombineMoeArgs a) {
   pdl_wait();
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.M * a.H; i += gridDim.x * blockDim.x) {
-    const int t = i / a.H, n = i % a.H;
-    float routed = 0.f;
-    for (int k = 0; k < a.topk; ++k) {
-      const size_t pick = (size_t)t * a.topk + k;
-      float y = 0.f;
-      for (int s = 0; s < a.routed_slices; ++s) y += a.routed[((size_t)s * a.M * a.topk + pick) * a.H + n];
-      routed = bf16r(routed + bf16r(y * a.wts[pick]));
+  const int g8 = a.H / 8;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.M * g8; i += gridDim.x * blockDim.x) {
+    const int t = i / g8, n = (i % g8) * 8;
+    float routed[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int k0 = 0; k0 < a.topk; k0 += 8) {
+      float y[8][8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) y[k][q] = 0.f;
+      for (int s = 0; s < a.routed_slices; ++s) {
+        float4 u[8][2];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (k0 + k < a.topk) {
+            const float4* p = reinterpret_cast<const float4*>(
+                a.routed + ((size_t)s * a.M * a.topk + (size_t)t * a.topk + k0 + k) * a.H + n);
+            u[k][0] = p[0];
+            u[k][1] = p[1];
+          }
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (k0 + k < a.topk) {
+            y[k][0] += u[k][0].x; y[k][1] += u[k][0].y; y[k][2] += u[k][0].z; y[k][3] += u[k][0].w;
+            y[k][4] += u[k][1].x; y[k][5] += u[k][1].y; y[k][6] += u[k][1].z; y[k][7] += u[k][1].w;
+          }
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (k0 + k < a.topk) {
+          const float w = a.wts[(size_t)t * a.topk + k0 + k];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) routed[q] = bf16r(routed[q] + bf16r(y[k][q] * w));
+        }
     }
-    float sh = 0.f;
-    for (int s = 0; s < a.shared_slices; ++s) sh += a.shared[((size_t)s * a.M + t) * a.H + n];
-    a.out[i] = __float2bfloat16_rn(routed + bf16r(sh));
+    float sh[8];
+    sum_slices8(a.shared + (size_t)t * a.H + n, (size_t)a.M * a.H, a.shared_slices, sh);
+    uint32_t o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      o[q] = pack_bf16x2(routed[2 * q] + bf16r(sh[2 * q]), routed[2 * q + 1] + bf16r(sh[2 * q + 1]));
+    *reinterpret_cast<uint4*>(a.out + (size_t)t * a.H + n) = make_uint4(o[0], o[1], o[2], o[3]);
   }
   pdl_launch();
 }

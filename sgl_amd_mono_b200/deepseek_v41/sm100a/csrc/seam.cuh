@@ -60,56 +60,66 @@ __global__ void __launch_bounds__(256) seam_slice_kernel(const SeamArgs a) {
     fn[e] = __ldg(a.hc_fn + (size_t)j * kHC * H + (size_t)o * H + c0 + c);
   }
   pdl_wait();
-  for (int e = tid; e < a.M * kHC * kSliceCols; e += blockDim.x) {
-    const int t = e / (kHC * kSliceCols), r = e % (kHC * kSliceCols), o = r / kSliceCols,
-              c = r % kSliceCols;
-    const size_t at = ((size_t)t * kHC + o) * H + c0 + c;
-    float v;
-    if (a.fold) {
-      const float* cm = a.comb_in + t * 16;
-      float r0 = bf2f(a.res_in[((size_t)t * kHC + 0) * H + c0 + c]);
-      float r1 = bf2f(a.res_in[((size_t)t * kHC + 1) * H + c0 + c]);
-      float r2 = bf2f(a.res_in[((size_t)t * kHC + 2) * H + c0 + c]);
-      float r3 = bf2f(a.res_in[((size_t)t * kHC + 3) * H + c0 + c]);
-      float xv = bf2f(a.x[(size_t)t * H + c0 + c]);
-      v = __fadd_rn(__fmul_rn(a.post_in[t * kHC + o], xv), __fmul_rn(r0, cm[0 * 4 + o]));
-      v = __fadd_rn(v, __fmul_rn(cm[1 * 4 + o], r1));
-      v = __fadd_rn(v, __fmul_rn(cm[2 * 4 + o], r2));
-      v = bf16r(__fmaf_rn(cm[3 * 4 + o], r3, v));
-    } else {
-      v = bf2f(a.res_in[at]);
-    }
-    a.res_out[at] = __float2bfloat16_rn(v);
-    rs[t * kHC * kSliceCols + r] = v;
-  }
-  __syncthreads();
-  // the layer input: R_new collapsed with the previous pre, h in order
+  // R_new of (row t, column c) and the collapsed layer input: one thread an element, its loads
+  // before any store
+#pragma unroll 2
   for (int e = tid; e < a.M * kSliceCols; e += blockDim.x) {
     const int t = e / kSliceCols, c = e % kSliceCols;
-    float acc;
+    const size_t col = (size_t)t * kHC * H + c0 + c;  // copy o at + o * H
+    float rv[kHC];
+    if (a.fold) {
+      float r[kHC];
+#pragma unroll
+      for (int h = 0; h < kHC; ++h) r[h] = bf2f(a.res_in[col + (size_t)h * H]);
+      const float xv = bf2f(a.x[(size_t)t * H + c0 + c]);
+      const float* cm = a.comb_in + t * 16;
+#pragma unroll
+      for (int o = 0; o < kHC; ++o) {
+        float v = __fadd_rn(__fmul_rn(a.post_in[t * kHC + o], xv), __fmul_rn(r[0], cm[0 * 4 + o]));
+        v = __fadd_rn(v, __fmul_rn(cm[1 * 4 + o], r[1]));
+        v = __fadd_rn(v, __fmul_rn(cm[2 * 4 + o], r[2]));
+        rv[o] = bf16r(__fmaf_rn(cm[3 * 4 + o], r[3], v));
+      }
+    } else {
+#pragma unroll
+      for (int o = 0; o < kHC; ++o) rv[o] = bf2f(a.res_in[col + (size_t)o * H]);
+    }
+    float acc;  // the layer input: R_new collapsed with the previous pre, h in order
     if (a.first) {
-      acc = rs[t * kHC * kSliceCols + c];
+      acc = rv[0];
     } else {
       acc = 0.f;
 #pragma unroll
-      for (int h = 0; h < kHC; ++h)
-        acc = __fadd_rn(acc, __fmul_rn(a.pre_in[t * kHC + h], rs[t * kHC * kSliceCols + h * kSliceCols + c]));
+      for (int h = 0; h < kHC; ++h) acc = __fadd_rn(acc, __fmul_rn(a.pre_in[t * kHC + h], rv[h]));
+    }
+#pragma unroll
+    for (int o = 0; o < kHC; ++o) {
+      a.res_out[col + (size_t)o * H] = __float2bfloat16_rn(rv[o]);
+      rs[t * kHC * kSliceCols + o * kSliceCols + c] = rv[o];
     }
     a.lin[(size_t)t * H + c0 + c] = __float2bfloat16_rn(acc);
   }
-  // partial mixes and the sum of squares: a warp a (row, projection), 4 terms a lane
+  __syncthreads();
+  // partial mixes and the sum of squares: a warp a row, its 25 dot products of 4 terms a lane
+  // reduced over the warp together (lane j takes product j)
   const int nslices = H / kSliceCols;
-  for (int p = warp; p < a.M * kPart; p += 8) {
-    const int t = p / kPart, j = p % kPart;
+  for (int t = warp; t < a.M; t += 8) {
     const float* r = rs + t * kHC * kSliceCols;
-    float acc = 0.f;
+    float rr[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int e = lane + 32 * q;
-      acc = fmaf(j < kMix ? fn[j * kHC * kSliceCols + e] : r[e], r[e], acc);
+    for (int q = 0; q < 4; ++q) rr[q] = r[lane + 32 * q];
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      float acc = 0.f;
+      if (j < kPart) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc = fmaf(j < kMix ? fn[j * kHC * kSliceCols + lane + 32 * q] : rr[q], rr[q], acc);
+      }
+      v[j] = acc;
     }
-    acc = warp_sum(acc);
-    if (lane == 0) a.part[((size_t)t * nslices + s) * kPart + j] = acc;
+    const float sum = warp_transpose_sum(v, lane);
+    if (lane < kPart) a.part[((size_t)t * nslices + s) * kPart + lane] = sum;
   }
   pdl_launch();
 }
@@ -155,8 +165,18 @@ __global__ void __launch_bounds__(256) seam_gate_norm_kernel(const SeamArgs a) {
     const int nslices = H / kSliceCols;
     const int s0 = warp * nslices / 8, s1 = (warp + 1) * nslices / 8;
     if (lane < kPart) {
+      // (eight slices' loads in flight, added in slice order)
+      const float* pp = a.part + (size_t)t * nslices * kPart + lane;
       float acc = 0.f;
-      for (int s = s0; s < s1; ++s) acc += a.part[((size_t)t * nslices + s) * kPart + lane];
+      int s = s0;
+      for (; s + 8 <= s1; s += 8) {
+        float u[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) u[i] = pp[(size_t)(s + i) * kPart];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc += u[i];
+      }
+      for (; s < s1; ++s) acc += pp[(size_t)s * kPart];
       gsum[warp][lane] = acc;
     }
   }
