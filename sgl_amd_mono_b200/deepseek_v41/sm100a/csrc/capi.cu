@@ -79,6 +79,17 @@ bool use_attn_pair() {
   return v == 1;
 }
 
+// The smallest M whose MXFP8-input GEMVs run on the tcgen05 dense kernel (DSV41_DENSE_MIN_M,
+// default 16).
+int dense_min_rows() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("DSV41_DENSE_MIN_M");
+    v = e ? std::max(1, atoi(e)) : 16;
+  }
+  return v;
+}
+
 bool use_pdl() {
   static int v = -1;
   if (v < 0) {
@@ -155,11 +166,13 @@ bool dense_weight_map(CUtensorMap* m, const void* w, int N, int K) {
 }
 
 // Whether a planned GEMV with an MXFP8 input runs on the tcgen05 dense kernel: 16 <= M <= 48
-// (below, the persistent kernel's per-item latency loses to gemv_fp8_kernel), ungrouped, N >= 256,
+// (below, the persistent kernel's per-item latency loses to gemv_fp8_kernel: at M = 1 and 4 its
+// wq_b is ~2 us faster, its shared expert ~7 us slower, and front_qkv has 16 partial slices to
+// sum instead of the GEMV's few), ungrouped, N >= 256,
 // K a multiple of 128, the weight 16-byte aligned. (Independent of the activation pointers, which
 // are null while the scratch is only being measured.)
 bool dense_eligible(const GemvArgs& g) {
-  return g.M >= 16 && g.M <= kDnMaxRows && g.N >= 256 && g.K % 128 == 0 && g.x_group_rows == g.N &&
+  return g.M >= dense_min_rows() && g.M <= kDnMaxRows && g.N >= 256 && g.K % 128 == 0 && g.x_group_rows == g.N &&
          reinterpret_cast<uintptr_t>(g.w) % 16 == 0;
 }
 // Its K slicing: the longest slice (<= kDnKsMax, dividing K) that still gives a (256-row tile,
