@@ -4,16 +4,22 @@
 // CTA = (row, chunk of the row's keys, 32-head tile), 12 warps:
 //   warps 0-3  softmax + epilogue (each owns the TMEM lane quarter of its warp index),
 //   warp  4    TMEM allocation and the MMA issue (one elected thread),
-//   warps 5-11 producers: 64-key sub-blocks of FP8 records -> an f16 tile in shared memory.
+//   warps 5-11 producers: 48-key sub-blocks of FP8 records -> an f16 tile in shared memory, in a
+//              ring of 3 tiles (a 64-key tile is 73.7 KB and only two fit beside Q and P; three
+//              48-key tiles let the producer run a tile further ahead of the QK -> softmax -> PV
+//              chain).
 // A row's two head tiles run as a cluster of two CTAs (PAIR) that share every key tile: each
-// converts half of the tile's keys into both CTAs' shared memory.
-// Per sub-block j (tile, S and P buffers j & 1):
+// converts half of the tile's keys into its own shared memory and copies that half into the
+// peer's with one cp.async.bulk, counted on the peer's tile-full mbarrier.
+// Per sub-block j (tile j % 3; S and P buffers j & 1):
 //   S^T[64 keys x NH heads] = K_tile . Q^T        tcgen05.mma M=64 (keys), N=NH, K=D: A = the tile
-//                                                (K-major), B = Q (K-major), D in TMEM;
+//                                                (K-major; its rows 48 .. 63 read whatever follows
+//                                                the tile in shared memory, and those keys are
+//                                                masked), B = Q (K-major), D in TMEM;
 //   softmax over keys (the threads holding keys 16 w + lane, lane < 16, of warp w) against a
 //   per-head reference max that moves only when a score passes it by more than 2^8 (then O is
 //   rescaled in TMEM);
-//   O^T[D dims x 2 NH] += V_tile^T . P^T          M=128 (dims, in 128-dim blocks), N=2 NH, K=64
+//   O^T[D dims x 2 NH] += V_tile^T . P^T          M=128 (dims, in 128-dim blocks), N=2 NH, K=48
 //                                                keys: A = the same tile read MN-major, B = P^T
 //                                                (MN-major, written by the softmax threads) whose
 //                                                columns are p's f16 head (0 .. NH - 1), then its
@@ -37,7 +43,8 @@
 
 namespace dsv41 {
 
-constexpr int kTcKeys = 64;                // keys a sub-block
+constexpr int kTcKeys = 48;                // keys a sub-block (the QK's M = 64 rows: 16 padded)
+constexpr int kTcStages = 3;               // key tiles in flight
 constexpr int kTcThreads = 384;            // 12 warps
 constexpr int kTcProducers = 7 * 32;       // warps 5..11
 constexpr uint32_t kTcWaitPolls = 1u << 24;
@@ -88,9 +95,8 @@ struct TcSmem {
   static constexpr int kTileBytes = kTcKeys * D * 2;
   static constexpr int kQBytes = 32 * D * 2;
   static constexpr int kPBytes = kTcKeys * 32 * 2;
-  static constexpr int kTile0 = 0;
-  static constexpr int kTile1 = kTileBytes;
-  static constexpr int kQ = 2 * kTileBytes;
+  static constexpr int kTile0 = 0;                      // kTcStages tiles
+  static constexpr int kQ = kTcStages * kTileBytes;     // (the QK's padded rows of the last tile read Q)
   static constexpr int kP = kQ + kQBytes;
   static constexpr int kRed = kP + 4 * kPBytes;      // float [4 warps][64 heads]
   static constexpr int kM = kRed + 4 * 64 * 4;       // float [64]: the used max of each head
@@ -98,7 +104,7 @@ struct TcSmem {
   static constexpr int kMetaStages = 3;
   static constexpr int kMeta = kAlpha + 64 * 4;      // [3 stages][64 keys]: record pointer, then 8 codes
   static constexpr int kBar = kMeta + kMetaStages * 64 * 16;  // uint64 mbarriers
-  static constexpr int kNumBars = 13;
+  static constexpr int kNumBars = 2 * kTcStages + 9;
   static constexpr int kMisc = kBar + kNumBars * 8;  // tmem base, abort flag
   static constexpr int kBytes = kMisc + 16;
 };
@@ -169,26 +175,28 @@ __device__ __forceinline__ bool mbar_wait_cl(uint32_t bar, uint32_t parity, vola
   atomicExch(&g_tc_error, 1);
   return false;
 }
-// Cluster plumbing for a CTA pair: the peer's address of a shared-memory location, a store
-// there, an arrival on the peer's mbarrier (release at cluster scope), both CTAs' barrier.
+// Cluster plumbing for a CTA pair: the peer's address of a shared-memory location, both CTAs'
+// barrier.
 __device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
 }
-__device__ __forceinline__ void st_cluster16(uint32_t addr, const uint4& v) {
-  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
-               "r"(v.w)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void fence_async_cluster() {
-  asm volatile("fence.proxy.async.shared::cluster;" ::: "memory");
+// An arrival on the peer's mbarrier that also raises its expected transaction bytes by tx.
+__device__ __forceinline__ void mbar_arrive_tx_remote(uint32_t cluster_addr, uint32_t tx) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(cluster_addr),
+               "r"(tx)
+               : "memory");
+}
+// bytes of this CTA's shared memory into the peer's (cluster addresses dst, bar), counted on the
+// peer's mbarrier bar as they land (a plain copy: no multicast)
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "r"(src), "r"(bytes), "r"(bar)
+               : "memory");
 }
 // the MMAs' completion arrives on the mbarrier at this offset in both CTAs of the pair
 __device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
@@ -273,9 +281,10 @@ __device__ __forceinline__ int core_off(int r, int c) {
 }
 
 // PAIR: the row's two 32-head tiles run as a cluster of two CTAs that share every key tile:
-// each CTA's producers gather and convert half of the tile's keys (key groups 4 r .. 4 r + 3 of
-// CTA rank r) and store them into both CTAs' tiles; a tile is full after both CTAs' producer
-// warps arrived (14) and free after both CTAs' PV finished with it (2 commit arrivals).
+// each CTA's producers gather and convert half of the tile's keys (key groups 3 r .. 3 r + 2 of
+// CTA rank r) into its own tile, then one thread copies that half into the peer's; a tile is full
+// after this CTA's 7 producer warps and the peer's copy (an arrival raising the expected bytes,
+// then the bytes) arrived, and free after both CTAs' PV finished with it (2 commit arrivals).
 template <int NOPE, bool PAIR>
 __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs A) {
   constexpr int D = NOPE + 64;
@@ -295,6 +304,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
   // bars: 0,1 tile full; 2,3 tile free; 4,5 S ready; 6,7 S consumed; 8,9 P ready; 10,11 PV
   // done; 12 MMA drain (pairs by the sub-block's parity)
   auto bar = [&](int i) { return smem_u32(bars + i); };
+  // tile stage ts = j % 3 (parity (j / 3) & 1); S and P buffers s = j & 1 (parity (j >> 1) & 1)
+  auto b_full = [&](int ts) { return bar(ts); };                     // producers -> MMA
+  auto b_free = [&](int ts) { return bar(kTcStages + ts); };         // PV done with the tile
+  auto b_sready = [&](int sb) { return bar(2 * kTcStages + sb); };   // QK -> softmax
+  auto b_scons = [&](int sb) { return bar(2 * kTcStages + 2 + sb); }; // softmax holds S
+  auto b_pready = [&](int sb) { return bar(2 * kTcStages + 4 + sb); }; // softmax -> PV
+  auto b_pvdone = [&](int sb) { return bar(2 * kTcStages + 6 + sb); }; // PV(j) complete
+  const uint32_t b_drain = bar(2 * kTcStages + 8);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
   uint32_t* tmem_base = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   float* red = reinterpret_cast<float*>(smem + L::kRed);
@@ -321,19 +338,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
     *reinterpret_cast<uint4*>(smem + L::kQ + core_off<D>(h, 8 * c)) = v;
   }
   if (tid == 0) {
-    mbar_init(bar(0), PAIR ? 14 : 7);
-    mbar_init(bar(1), PAIR ? 14 : 7);
-    mbar_init(bar(2), PAIR ? 2 : 1);
-    mbar_init(bar(3), PAIR ? 2 : 1);
-    mbar_init(bar(4), 1);
-    mbar_init(bar(5), 1);
-    mbar_init(bar(6), 4);
-    mbar_init(bar(7), 4);
-    mbar_init(bar(8), 4);
-    mbar_init(bar(9), 4);
-    mbar_init(bar(10), 1);
-    mbar_init(bar(11), 1);
-    mbar_init(bar(12), 1);
+    for (int ts = 0; ts < kTcStages; ++ts) {
+      mbar_init(b_full(ts), PAIR ? 8 : 7);  // the producer warps (+ the peer's copy of its half)
+      mbar_init(b_free(ts), PAIR ? 2 : 1);
+    }
+    for (int sb = 0; sb < 2; ++sb) {
+      mbar_init(b_sready(sb), 1);
+      mbar_init(b_scons(sb), 4);
+      mbar_init(b_pready(sb), 4);
+      mbar_init(b_pvdone(sb), 1);
+    }
+    mbar_init(b_drain, 1);
     *abort = 0;
   }
   if (tid < 64) {
@@ -382,6 +397,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
     constexpr int kItems = (kUnits + kTcProducers / 32 - 1) / (kTcProducers / 32);
     constexpr int kMetaKeys = 8 * kGroups;  // keys this CTA locates: threads ptid < kMetaKeys
     const int g0 = PAIR ? rank * kGroups : 0;
+    constexpr uint32_t kHalfBytes = (uint32_t)(kGroups * 8 * DG * 16);  // a pair's half tile
     const int mkey = 8 * g0 + ptid;  // thread ptid's key of a tile (ptid < kMetaKeys)
     auto item = [&](int i, int& key, int& c) {  // this lane's (key, chunk) of its i-th unit
       const int u = wp + (kTcProducers / 32) * i;
@@ -426,13 +442,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
       }
     };
     auto convert = [&](int j, const uint4 (&raw)[kItems]) {
-      const int s = j & 1, ms = j % kStages;
-      const int tile_off = s ? L::kTile1 : L::kTile0;
-      // into this CTA's tile and, for a pair, the peer's
-      auto put = [&](int off, const uint4& v) {
-        *reinterpret_cast<uint4*>(smem + tile_off + off) = v;
-        if (PAIR) st_cluster16(peer_smem + (uint32_t)(tile_off + off), v);
-      };
+      const int ts = j % kTcStages, ms = j % kStages;
+      const int tile_off = L::kTile0 + ts * L::kTileBytes;
+      // into this CTA's tile (a pair's half then goes to the peer by one bulk copy, below)
+      auto put = [&](int off, const uint4& v) { *reinterpret_cast<uint4*>(smem + tile_off + off) = v; };
 #pragma unroll
       for (int i = 0; i < kItems; ++i) {
         int key, c;
@@ -475,14 +488,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
           put(core_off<D>(key, NOPE + (b0 - NOPE) / 2), o0);
         }
       }
-      if (PAIR)
-        fence_async_cluster();
-      else
-        fence_async_smem();
+      fence_async_smem();  // the MMA and the bulk copy (async proxy) read these writes
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(bar(s));
-        if (PAIR) mbar_arrive_remote(cluster_map(bar(s), (uint32_t)(rank ^ 1)));
+      if (lane == 0) mbar_arrive(b_full(ts));
+      if (PAIR) {
+        // this CTA's half (key groups g0 .. g0 + kGroups - 1: contiguous in the core layout) into
+        // the peer's tile once every producer warp has written it
+        asm volatile("bar.sync 2, %0;" ::"n"(kTcProducers) : "memory");
+        if (ptid == 0) {
+          const uint32_t off = (uint32_t)(tile_off + g0 * 8 * DG * 16);
+          const uint32_t peer_bar = cluster_map(b_full(ts), (uint32_t)(rank ^ 1));
+          mbar_arrive_tx_remote(peer_bar, kHalfBytes);
+          bulk_copy_to_peer(peer_smem + off, smem_u32(smem) + off, kHalfBytes, peer_bar);
+        }
       }
     };
     // one tile: free its stage, publish and issue the next tile, convert this one (cur holds its
@@ -491,16 +509,33 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
     // one tile: once its stage is free, convert it (a pair first: its chunks were loaded two
     // tiles ago), publish and issue tile j + kAhead's loads into nxt, locate tile j + kAhead + 1
     auto step = [&](int j, const uint4 (&cur)[kItems], uint4 (&nxt)[kItems]) {
-      const int s = j & 1;
-      // the stage is free (PV(j - 2) done), for every producer alike; and every producer is past
+      const int ts = j % kTcStages, fpar = ((j / kTcStages) - 1) & 1;
+      // the stage is free (PV(j - 3) done), for every producer alike; and every producer is past
       // tile j - 1's conversion (its metadata stage is rewritten next)
-      if (!producers_all(j < 2 || (PAIR ? mbar_wait_cl(bar(2 + s), ((j >> 1) - 1) & 1, abort)
-                                        : mbar_wait(bar(2 + s), ((j >> 1) - 1) & 1, abort))))
+      if (!producers_all(j < kTcStages || (PAIR ? mbar_wait_cl(b_free(ts), fpar, abort)
+                                                : mbar_wait(b_free(ts), fpar, abort))))
         return false;
       if (ptid == 0) TC_TRACE(j, 0);
       if (PAIR) {
         convert(j, cur);
         if (ptid == 0) TC_TRACE(j, 1);
+        // the metadata before the records: publish and locate use loads issued before the last
+        // record loads, so they wait for nothing newer (a use of a load waits for the loads issued
+        // ahead of it); then the next key-table entry, then the records kAhead tiles on
+        const bool more = j + kAhead < nsub;
+        if (more && ptid < kMetaKeys) publish(j + kAhead);
+        if (ptid < kMetaKeys) {
+          locate(la_v);
+          la_v = kt_load(j + kAhead + 2);
+        }
+        if (ptid == 0) TC_TRACE(j, 4);
+        if (more) {
+          asm volatile("bar.sync 2, %0;" ::"n"(kTcProducers) : "memory");
+          if (ptid == 0) TC_TRACE(j, 14);
+          issue(j + kAhead, nxt);
+          if (ptid == 0) TC_TRACE(j, 15);
+        }
+        return true;
       }
       if (j + kAhead < nsub) {
         if (ptid < kMetaKeys) publish(j + kAhead);
@@ -514,10 +549,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
         la_v = kt_load(j + kAhead + 2);
       }
       if (ptid == 0) TC_TRACE(j, 4);
-      if (!PAIR) {
-        convert(j, cur);
-        if (ptid == 0) TC_TRACE(j, 1);
-      }
+      convert(j, cur);
+      if (ptid == 0) TC_TRACE(j, 1);
       return true;
     };
     uint4 buf0[kItems], buf1[kItems];
@@ -558,29 +591,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
       const uint32_t id_qk = umma_idesc(64, NH, 0, 0);
       const uint32_t id_pv = umma_idesc(128, 2 * NH, 1, 1);
       auto issue_qk = [&](int j) {
-        const uint32_t tile = s_tile0 + ((j & 1) ? L::kTileBytes : 0);
+        const uint32_t tile = s_tile0 + (j % kTcStages) * L::kTileBytes;
         const uint32_t dst = tm_s + 32 * (j & 1);
 #pragma unroll 4
         for (int ks = 0; ks < D / 16; ++ks)
           umma_f16(dst, umma_sdesc(tile + 256 * ks, 128, DG * 128), umma_sdesc(s_q + 256 * ks, 128, DG * 128), id_qk,
                    ks > 0);
-        umma_commit(bar(4 + (j & 1)));
+        umma_commit(b_sready(j & 1));
         TC_TRACE(j, 11);
       };
       auto qk_ready = [&](int j) {  // tile j loaded and S[j & 1] consumed by softmax(j - 2)
-        return (PAIR ? mbar_try_cl(bar(j & 1), (j >> 1) & 1) : mbar_try(bar(j & 1), (j >> 1) & 1)) &&
-               (j < 2 || mbar_try(bar(6 + (j & 1)), ((j - 2) >> 1) & 1));
+        const int ts = j % kTcStages, tpar = (j / kTcStages) & 1;
+        return (PAIR ? mbar_try_cl(b_full(ts), tpar) : mbar_try(b_full(ts), tpar)) &&
+               (j < 2 || mbar_try(b_scons(j & 1), ((j - 2) >> 1) & 1));
       };
       auto wait_qk = [&](int j) {
-        return (PAIR ? mbar_wait_cl(bar(j & 1), (j >> 1) & 1, abort) : mbar_wait(bar(j & 1), (j >> 1) & 1, abort)) &&
-               (j < 2 || mbar_wait(bar(6 + (j & 1)), ((j - 2) >> 1) & 1, abort));
+        const int ts = j % kTcStages, tpar = (j / kTcStages) & 1;
+        return (PAIR ? mbar_wait_cl(b_full(ts), tpar, abort) : mbar_wait(b_full(ts), tpar, abort)) &&
+               (j < 2 || mbar_wait(b_scons(j & 1), ((j - 2) >> 1) & 1, abort));
       };
       bool ok = true;
       if (nsub > 0) ok = wait_qk(0);
       if (ok && nsub > 0) issue_qk(0);
       for (int j = 0; ok && j < nsub; ++j) {
         const int s = j & 1;
-        const uint32_t p_ready = bar(8 + s), p_par = (j >> 1) & 1;
+        const uint32_t p_ready = b_pready(s), p_par = (j >> 1) & 1;
         bool qk_done = j + 1 >= nsub;
         if (!qk_done && qk_ready(j + 1)) {
           issue_qk(j + 1);
@@ -602,7 +637,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
         TC_TRACE(j, 3);
         tc_fence_after();
         // PV: O += V^T P^T, P^T's columns the f16 head of p (0 .. NH - 1), then its tail
-        const uint32_t tile = s_tile0 + (s ? L::kTileBytes : 0);
+        const uint32_t tile = s_tile0 + (j % kTcStages) * L::kTileBytes;
         const uint32_t pt = s_p + 2 * s * L::kPBytes;
 #pragma unroll
         for (int b = 0; b < NBLK; ++b) {
@@ -613,10 +648,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
                      umma_sdesc(pt + 2 * ks * (2 * NH / 8) * 128, (2 * NH / 8) * 128, 128), id_pv, j > 0 || ks > 0);
         }
         if (PAIR)
-          umma_commit_pair(bar(2 + s));  // the tile is free, in both CTAs
+          umma_commit_pair(b_free(j % kTcStages));  // the tile is free, in both CTAs
         else
-          umma_commit(bar(2 + s));  // the tile is free
-        umma_commit(bar(10 + s));  // P[s] free; O holds sub-blocks 0 .. j
+          umma_commit(b_free(j % kTcStages));  // the tile is free
+        umma_commit(b_pvdone(s));  // P[s] free; O holds sub-blocks 0 .. j
         if (!qk_done) {
           ok = wait_qk(j + 1);
           if (!ok) break;
@@ -624,8 +659,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
         }
       }
       // drain: every issued MMA complete before the TMEM is freed (also after an abort)
-      umma_commit(bar(12));
-      mbar_wait(bar(12), 0, abort);
+      umma_commit(b_drain);
+      mbar_wait(b_drain, 0, abort);
     }
   } else {
     // ================= softmax + epilogue (warps 0-3: TMEM lanes 32 w .. 32 w + 31)
@@ -635,7 +670,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
     // (p <= 2^kTcSlack stays well inside f16): then O and the partial sums are rescaled once.
     // Each key thread keeps its own partial sums of p.
     const int key = 16 * warp + (lane & 15);
-    const bool has_key = lane < 16;
+    const bool has_key = lane < 16 && key < kTcKeys;  // keys 48 .. 63: the QK's padded rows
     const uint32_t lane_addr = (uint32_t)(32 * warp) << 16;
     const int ngroups = NH / 16;
     float l_part[32];
@@ -676,7 +711,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
       const int kv_ = kt_next;
       kt_next = j + 1 < nsub ? kt_entry(j + 1) : -1;
       const bool valid = kv_ != -1 && (kv_ >= 0 || a.comp != nullptr);
-      ok = softmax_all(mbar_wait(bar(4 + s), (j >> 1) & 1, abort));
+      ok = softmax_all(mbar_wait(b_sready(s), (j >> 1) & 1, abort));
       if (!ok) break;
       if (tid == 0) TC_TRACE(j, 5);
       tc_fence_after();
@@ -689,7 +724,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
         // S[s] is in registers: QK(j + 2) may overwrite it
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar(6 + s));
+        if (lane == 0) mbar_arrive(b_scons(s));
         if (tid == 0) TC_TRACE(j, 8);
 #pragma unroll
         for (int q = 0; q < 32; ++q) sv[q] = (valid && q < NH) ? __uint_as_float(v[q]) * a.scale_log2 : -INFINITY;
@@ -731,7 +766,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
       if (tid == 0) TC_TRACE(j, 9);
       if (rescale) {
         // O must hold every issued PV before it is scaled
-        ok = softmax_all(mbar_wait(bar(10 + ((j - 1) & 1)), ((j - 1) >> 1) & 1, abort));
+        ok = softmax_all(mbar_wait(b_pvdone((j - 1) & 1), ((j - 1) >> 1) & 1, abort));
         if (!ok) break;
         tc_fence_after();
         rescale_o();
@@ -764,7 +799,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
       if (tid == 0) TC_TRACE(j, 12);
       // P^T[s] is free once PV(j - 2) is done
       if (j >= 2) {
-        ok = softmax_all(mbar_wait(bar(10 + s), ((j - 2) >> 1) & 1, abort));
+        ok = softmax_all(mbar_wait(b_pvdone(s), ((j - 2) >> 1) & 1, abort));
         if (!ok) break;
       }
       if (tid == 0) TC_TRACE(j, 13);
@@ -784,13 +819,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
       fence_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(8 + s));
+      if (lane == 0) mbar_arrive(b_pready(s));
       if (tid == 0) TC_TRACE(j, 7);
       // (the next update of red, m_sm and a_sm comes after the next sub-block's first barrier,
       // which every thread reaches only after this sub-block's reads)
     }
     // ---- epilogue: every PV done, then O^T (head + tail columns) and (m, l) of the chunk
-    if (ok && nsub > 0) ok = softmax_all(mbar_wait(bar(10 + ((nsub - 1) & 1)), ((nsub - 1) >> 1) & 1, abort));
+    if (ok && nsub > 0) ok = softmax_all(mbar_wait(b_pvdone((nsub - 1) & 1), ((nsub - 1) >> 1) & 1, abort));
     if (tid == 0) TC_TRACE(63, 0);
     const size_t base = ((size_t)t * a.nchunks + ch) * a.heads + h0;
     const int nh_live = min(NH, a.heads - h0);

@@ -474,17 +474,18 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   const int head_tiles = tc ? cdiv(heads, 32) : cdiv(heads, 16);
   const int units = M * head_tiles;
   int nchunks = cdiv(2 * sms, units);
+  const int sub = tc ? kTcKeys : kSub;  // keys a sub-block
   if (tc) {
     // one CTA an SM: the split with the fewest sub-block periods over all waves, a CTA's start
     // and drain counted as 4 periods (ties: fewer chunks, so fewer partials for the combine)
     int64_t best = INT64_MAX;
-    for (int c = 1; c <= cdiv(keys, kSub); ++c) {
-      const int64_t cost = (int64_t)cdiv(units * c, sms) * (cdiv(cdiv(keys, c), kSub) + 4);
+    for (int c = 1; c <= cdiv(keys, sub); ++c) {
+      const int64_t cost = (int64_t)cdiv(units * c, sms) * (cdiv(cdiv(keys, c), sub) + 4);
       if (cost < best) best = cost, nchunks = c;
     }
   }
-  nchunks = std::max(1, std::min(nchunks, cdiv(keys, kSub)));
-  const int chunk_keys = cdiv(cdiv(keys, nchunks), kSub) * kSub;
+  nchunks = std::max(1, std::min(nchunks, cdiv(keys, sub)));
+  const int chunk_keys = cdiv(cdiv(keys, nchunks), sub) * sub;
   nchunks = cdiv(keys, chunk_keys);
   auto* part_o = c.take<float>((int64_t)M * nchunks * heads * D);
   auto* part_ml = c.take<float>((int64_t)M * nchunks * heads * 2);
