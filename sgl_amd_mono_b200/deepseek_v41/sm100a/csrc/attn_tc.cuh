@@ -593,10 +593,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
       auto issue_qk = [&](int j) {
         const uint32_t tile = s_tile0 + (j % kTcStages) * L::kTileBytes;
         const uint32_t dst = tm_s + 32 * (j & 1);
-#pragma unroll 4
+        // descriptors built once: a K step advances both start addresses by 256 B (16 in the
+        // descriptor's address field, which holds addr >> 4 and cannot carry below 256 KB)
+        const uint64_t da = umma_sdesc(tile, 128, DG * 128), db = umma_sdesc(s_q, 128, DG * 128);
+#pragma unroll 6
         for (int ks = 0; ks < D / 16; ++ks)
-          umma_f16(dst, umma_sdesc(tile + 256 * ks, 128, DG * 128), umma_sdesc(s_q + 256 * ks, 128, DG * 128), id_qk,
-                   ks > 0);
+          umma_f16(dst, da + (uint64_t)(16 * ks), db + (uint64_t)(16 * ks), id_qk, ks > 0);
         umma_commit(b_sready(j & 1));
         TC_TRACE(j, 11);
       };
@@ -639,13 +641,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
         // PV: O += V^T P^T, P^T's columns the f16 head of p (0 .. NH - 1), then its tail
         const uint32_t tile = s_tile0 + (j % kTcStages) * L::kTileBytes;
         const uint32_t pt = s_p + 2 * s * L::kPBytes;
+        // (descriptors advanced per K step as in the QK: 2 key groups of the tile, of P^T)
+        const uint64_t db0 = umma_sdesc(pt, (2 * NH / 8) * 128, 128);
+        const uint32_t db_step = (uint32_t)(2 * (2 * NH / 8) * 128) >> 4;
 #pragma unroll
         for (int b = 0; b < NBLK; ++b) {
           const int d0 = min(128 * b, D - 128);
+          const uint64_t da0 = umma_sdesc(tile + (d0 / 8) * 128, DG * 128, 128);
 #pragma unroll
           for (int ks = 0; ks < kTcKeys / 16; ++ks)
-            umma_f16(tm_o + 64 * b, umma_sdesc(tile + (d0 / 8) * 128 + 2 * ks * DG * 128, DG * 128, 128),
-                     umma_sdesc(pt + 2 * ks * (2 * NH / 8) * 128, (2 * NH / 8) * 128, 128), id_pv, j > 0 || ks > 0);
+            umma_f16(tm_o + 64 * b, da0 + (uint64_t)(ks * ((2 * DG * 128) >> 4)), db0 + (uint64_t)(ks * db_step),
+                     id_pv, j > 0 || ks > 0);
         }
         if (PAIR)
           umma_commit_pair(b_free(j % kTcStages));  // the tile is free, in both CTAs
