@@ -28,11 +28,12 @@
 //                                                fp32 by the epilogue (the tensor core's fp32
 //                                                accumulation truncates: a tail added into the
 //                                                head's columns lost its precision).
-// The tile is stored as 8 x 16-byte core matrices: element (key, d) at
-//   (key / 8) * (D / 8) * 128 + (d / 8) * 128 + (key % 8) * 16 + (d % 8) * 2,
-// which is the K-major layout of the QK operand (leading offset 128 B, stride (D / 8) * 128 B)
-// and the MN-major layout of the PV operand (dims contiguous: stride 128 B, leading (D / 8)
-// * 128 B); Q likewise ([head][d]), P^T as [key group][head group][8 keys][8 heads].
+// The tile and Q are stored in the 128-byte-swizzle layout: [64-dim chunk][8-row group][8 rows x
+// 128 B] atoms of 1 KB, the 16-byte chunk q of row r at q ^ r (sw_off). For the tile this is at
+// once the K-major operand of the QK (8-row groups 1 KB apart, a K step 32 B into the rows) and
+// the MN-major operand V^T of the PV (64-dim atoms (kTcKeys / 8) KB apart, 8-key groups 1 KB
+// apart); with the unswizzled core-matrix layout each MMA fetched its operands 128 B at a time.
+// P^T is [key group][head group][8 keys][8 heads] (unswizzled, MN-major).
 // Synchronization: mbarriers (producer -> MMA: tile full; MMA -> producer: tile free;
 // MMA -> softmax: S ready, PV done; softmax -> MMA: S consumed, P ready), tcgen05.commit for MMA
 // completion; every wait is bounded and a timeout sets an error word and unwinds.
@@ -106,12 +107,27 @@ struct TcSmem {
   static constexpr int kBar = kMeta + kMetaStages * 64 * 16;  // uint64 mbarriers
   static constexpr int kNumBars = 2 * kTcStages + 9;
   static constexpr int kMisc = kBar + kNumBars * 8;  // tmem base, abort flag
-  static constexpr int kBytes = kMisc + 16;
+  static constexpr int kBytes = kMisc + 16 + 1024;  // + slack to align the base to 1 KB
 };
 
 __device__ __forceinline__ uint64_t umma_sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
   return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
          ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46);  // sm100 version, no swizzle
+}
+// The same with the 128-byte swizzle (layout type 2): K-major, sbo = the 8-row group stride (lbo
+// unused); MN-major, lbo = the stride between 64-element (128-byte) atoms along MN, sbo = the
+// 8-row group stride along K.
+__device__ __forceinline__ uint64_t umma_sdesc_sw128(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return umma_sdesc(addr, lbo, sbo) | ((uint64_t)2 << 61);
+}
+// Byte offset of element (row, d) of a [ROWS][D] f16 operand in the swizzled layout the tile and Q
+// use: [64-dim chunk][8-row group][8 rows x 128 B] atoms of 1 KB, the 16-byte chunk q of row r at
+// q ^ r (the 128-byte swizzle). It is at once the K-major operand of the QK and, for the tile, the
+// MN-major operand V^T of the PV.
+template <int ROWS>
+__device__ __forceinline__ int sw_off(int row, int d) {
+  return (d >> 6) * (ROWS / 8) * 1024 + (row >> 3) * 1024 + (row & 7) * 128 + ((((d & 63) >> 3) ^ (row & 7)) << 4) +
+         (d & 7) * 2;
 }
 // kind::f16 instruction descriptor: f16 x f16 -> f32, A / B major (0 K, 1 MN), N, M
 __device__ __forceinline__ uint32_t umma_idesc(int M, int N, int a_mn, int b_mn) {
@@ -153,6 +169,28 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   *abort = 1;
   atomicExch(&g_tc_error, 1);
   return false;
+}
+// Non-blocking tests (test_wait never suspends the thread, where a failed try_wait may for a while):
+// for a thread that polls several barriers and must act on whichever completes first.
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P1;\n\tmbarrier.test_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, P1;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_test_cl(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P1;\n\tmbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 P1, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, P1;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
 }
 // The same with cluster-scope acquire: the arrivals come from the other CTA of a pair too (its
 // producers' remote stores, its MMA completions).
@@ -274,11 +312,6 @@ __device__ __forceinline__ uint32_t cvt_f16x2(float lo, float hi) {
   return r;
 }
 
-// Core-matrix byte offset of element (row r, column c) of a [rows][C] tile.
-template <int C>
-__device__ __forceinline__ int core_off(int r, int c) {
-  return (r >> 3) * (C / 8) * 128 + (c >> 3) * 128 + (r & 7) * 16 + (c & 7) * 2;
-}
 
 // PAIR: the row's two 32-head tiles run as a cluster of two CTAs that share every key tile:
 // each CTA's producers gather and convert half of the tile's keys (key groups 3 r .. 3 r + 2 of
@@ -292,7 +325,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
   constexpr int NBLK = (D + 127) / 128;     // 128-dim PV blocks
   constexpr int CHUNKS = (NOPE + 128) / 16; // 16-byte chunks of a record's data
   using L = TcSmem<D>;
-  extern __shared__ __align__(16) uint8_t smem[];
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);  // swizzle atoms: 1 KB
   const AttnArgs& a = A.a;
   const int NH = A.nh;
   const int ht = blockIdx.x % A.head_tiles;
@@ -335,7 +369,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
       v = *reinterpret_cast<const uint4*>(a.q + ((size_t)t * a.heads + h0 + h) * D + 8 * c);
       v = make_uint4(bf16x2_to_f16x2(v.x), bf16x2_to_f16x2(v.y), bf16x2_to_f16x2(v.z), bf16x2_to_f16x2(v.w));
     }
-    *reinterpret_cast<uint4*>(smem + L::kQ + core_off<D>(h, 8 * c)) = v;
+    *reinterpret_cast<uint4*>(smem + L::kQ + sw_off<32>(h, 8 * c)) = v;
   }
   if (tid == 0) {
     for (int ts = 0; ts < kTcStages; ++ts) {
@@ -398,6 +432,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
     constexpr int kMetaKeys = 8 * kGroups;  // keys this CTA locates: threads ptid < kMetaKeys
     const int g0 = PAIR ? rank * kGroups : 0;
     constexpr uint32_t kHalfBytes = (uint32_t)(kGroups * 8 * DG * 16);  // a pair's half tile
+    constexpr int kChunkT = (kTcKeys / 8) * 1024;                         // a 64-dim chunk of a tile
     const int mkey = 8 * g0 + ptid;  // thread ptid's key of a tile (ptid < kMetaKeys)
     auto item = [&](int i, int& key, int& c) {  // this lane's (key, chunk) of its i-th unit
       const int u = wp + (kTcProducers / 32) * i;
@@ -478,28 +513,30 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
             o0 = make_uint4(r[0], r[1], r[2], r[3]);
             o1 = make_uint4(r[4], r[5], r[6], r[7]);
           }
-          put(core_off<D>(key, b0), o0);
-          put(core_off<D>(key, b0 + 8), o1);
+          put(sw_off<kTcKeys>(key, b0), o0);
+          put(sw_off<kTcKeys>(key, b0 + 8), o1);
         } else {
           uint4 o0 = make_uint4(0, 0, 0, 0);
           if (live)
             o0 = make_uint4(bf16x2_to_f16x2(raw[i].x), bf16x2_to_f16x2(raw[i].y), bf16x2_to_f16x2(raw[i].z),
                             bf16x2_to_f16x2(raw[i].w));
-          put(core_off<D>(key, NOPE + (b0 - NOPE) / 2), o0);
+          put(sw_off<kTcKeys>(key, NOPE + (b0 - NOPE) / 2), o0);
         }
       }
       fence_async_smem();  // the MMA and the bulk copy (async proxy) read these writes
       __syncwarp();
       if (lane == 0) mbar_arrive(b_full(ts));
       if (PAIR) {
-        // this CTA's half (key groups g0 .. g0 + kGroups - 1: contiguous in the core layout) into
-        // the peer's tile once every producer warp has written it
+        // this CTA's half (key groups g0 .. g0 + kGroups - 1: contiguous within each 64-dim
+        // chunk) into the peer's tile once every producer warp has written it, a copy a chunk
         asm volatile("bar.sync 2, %0;" ::"n"(kTcProducers) : "memory");
-        if (ptid == 0) {
-          const uint32_t off = (uint32_t)(tile_off + g0 * 8 * DG * 16);
+        // (lane c of the first producer warp copies chunk c; lane 0 also raises the peer's
+        // expected bytes -- the transaction count is signed, so a copy may land first)
+        if (ptid < D / 64) {
           const uint32_t peer_bar = cluster_map(b_full(ts), (uint32_t)(rank ^ 1));
-          mbar_arrive_tx_remote(peer_bar, kHalfBytes);
-          bulk_copy_to_peer(peer_smem + off, smem_u32(smem) + off, kHalfBytes, peer_bar);
+          if (ptid == 0) mbar_arrive_tx_remote(peer_bar, kHalfBytes);
+          const uint32_t off = (uint32_t)(tile_off + ptid * kChunkT + g0 * 1024);
+          bulk_copy_to_peer(peer_smem + off, smem_u32(smem) + off, (uint32_t)(kGroups * 1024), peer_bar);
         }
       }
     };
@@ -593,19 +630,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
       auto issue_qk = [&](int j) {
         const uint32_t tile = s_tile0 + (j % kTcStages) * L::kTileBytes;
         const uint32_t dst = tm_s + 32 * (j & 1);
-        // descriptors built once: a K step advances both start addresses by 256 B (16 in the
-        // descriptor's address field, which holds addr >> 4 and cannot carry below 256 KB)
-        const uint64_t da = umma_sdesc(tile, 128, DG * 128), db = umma_sdesc(s_q, 128, DG * 128);
-#pragma unroll 6
+        // K-major, 128-byte swizzle: K step ks = 16 dims, byte 32 (ks % 4) of chunk ks / 4's rows
+        // (tile chunks (kTcKeys / 8) KB apart, Q's 4 KB); 8-row groups 1 KB apart
+#pragma unroll 4
         for (int ks = 0; ks < D / 16; ++ks)
-          umma_f16(dst, da + (uint64_t)(16 * ks), db + (uint64_t)(16 * ks), id_qk, ks > 0);
+          umma_f16(dst, umma_sdesc_sw128(tile + (ks >> 2) * ((kTcKeys / 8) * 1024) + (ks & 3) * 32, 16, 1024),
+                   umma_sdesc_sw128(s_q + (ks >> 2) * 4096 + (ks & 3) * 32, 16, 1024), id_qk, ks > 0);
         umma_commit(b_sready(j & 1));
         TC_TRACE(j, 11);
       };
       auto qk_ready = [&](int j) {  // tile j loaded and S[j & 1] consumed by softmax(j - 2)
         const int ts = j % kTcStages, tpar = (j / kTcStages) & 1;
-        return (PAIR ? mbar_try_cl(b_full(ts), tpar) : mbar_try(b_full(ts), tpar)) &&
-               (j < 2 || mbar_try(b_scons(j & 1), ((j - 2) >> 1) & 1));
+        return (PAIR ? mbar_test_cl(b_full(ts), tpar) : mbar_test(b_full(ts), tpar)) &&
+               (j < 2 || mbar_test(b_scons(j & 1), ((j - 2) >> 1) & 1));
       };
       auto wait_qk = [&](int j) {
         const int ts = j % kTcStages, tpar = (j / kTcStages) & 1;
@@ -626,7 +663,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
         if (!qk_done) {
           // wait for whichever comes first: P(j) (then PV), or QK(j + 1)'s inputs
           for (uint32_t it = 0; !qk_done && it < kTcWaitPolls; ++it) {
-            if (mbar_try(p_ready, p_par)) break;
+            if (mbar_test(p_ready, p_par)) break;
             if (qk_ready(j + 1)) {
               issue_qk(j + 1);
               qk_done = true;
@@ -641,17 +678,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
         // PV: O += V^T P^T, P^T's columns the f16 head of p (0 .. NH - 1), then its tail
         const uint32_t tile = s_tile0 + (j % kTcStages) * L::kTileBytes;
         const uint32_t pt = s_p + 2 * s * L::kPBytes;
-        // (descriptors advanced per K step as in the QK: 2 key groups of the tile, of P^T)
+        // A = V^T, MN-major, 128-byte swizzle: a 128-dim block = 2 chunks (kTcKeys / 8) KB apart
+        // (lbo), K step ks = key groups 2 ks, 2 ks + 1 (1 KB apart: sbo); B = P^T, no swizzle
         const uint64_t db0 = umma_sdesc(pt, (2 * NH / 8) * 128, 128);
         const uint32_t db_step = (uint32_t)(2 * (2 * NH / 8) * 128) >> 4;
 #pragma unroll
         for (int b = 0; b < NBLK; ++b) {
           const int d0 = min(128 * b, D - 128);
-          const uint64_t da0 = umma_sdesc(tile + (d0 / 8) * 128, DG * 128, 128);
 #pragma unroll
           for (int ks = 0; ks < kTcKeys / 16; ++ks)
-            umma_f16(tm_o + 64 * b, da0 + (uint64_t)(ks * ((2 * DG * 128) >> 4)), db0 + (uint64_t)(ks * db_step),
-                     id_pv, j > 0 || ks > 0);
+            umma_f16(tm_o + 64 * b,
+                     umma_sdesc_sw128(tile + (d0 / 64) * ((kTcKeys / 8) * 1024) + ks * 2048, (kTcKeys / 8) * 1024, 1024),
+                     db0 + (uint64_t)(ks * db_step), id_pv, j > 0 || ks > 0);
         }
         if (PAIR)
           umma_commit_pair(b_free(j % kTcStages));  // the tile is free, in both CTAs
