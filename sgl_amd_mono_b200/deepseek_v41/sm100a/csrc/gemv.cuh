@@ -150,10 +150,11 @@ __global__ void __launch_bounds__(256, 2) gemv_fp8_kernel(const GemvArgs a) {
     const int xg = (tile0 * 16) / a.x_group_rows;
     const int col0 = xg * a.K + kb0 * 128;
     const int quads = KS / 4;
-    for (int i = threadIdx.x; i < MP * quads; i += blockDim.x) {
+    // only the M real rows: the token tile's rows past M feed only the MMA output columns of
+    // tokens past M (each output column reads its own B column), which are never stored
+    for (int i = threadIdx.x; i < a.M * quads; i += blockDim.x) {
       const int m = i / quads, q = i - m * quads;
-      uint2 v = make_uint2(0u, 0u);
-      if (m < a.M) v = *reinterpret_cast<const uint2*>(a.x + (size_t)m * a.x_ld + col0 + 4 * q);
+      const uint2 v = *reinterpret_cast<const uint2*>(a.x + (size_t)m * a.x_ld + col0 + 4 * q);
       const float s = 18446744073709551616.0f;  // 2^64
       float x0 = __uint_as_float(v.x << 16) * s, x1 = __uint_as_float(v.x & 0xffff0000u) * s;
       float x2 = __uint_as_float(v.y << 16) * s, x3 = __uint_as_float(v.y & 0xffff0000u) * s;
