@@ -150,9 +150,7 @@ __global__ void __launch_bounds__(256, 2) gemv_fp8_kernel(const GemvArgs a) {
     const int xg = (tile0 * 16) / a.x_group_rows;
     const int col0 = xg * a.K + kb0 * 128;
     const int quads = KS / 4;
-    // only the M real rows: the token tile's rows past M feed only the MMA output columns of
-    // tokens past M (each output column reads its own B column), which are never stored
-    for (int i = threadIdx.x; i < a.M * quads; i += blockDim.x) {
+    auto stage = [&](int i) {
       const int m = i / quads, q = i - m * quads;
       const uint2 v = *reinterpret_cast<const uint2*>(a.x + (size_t)m * a.x_ld + col0 + 4 * q);
       const float s = 18446744073709551616.0f;  // 2^64
@@ -163,6 +161,14 @@ __global__ void __launch_bounds__(256, 2) gemv_fp8_kernel(const GemvArgs a) {
       __nv_bfloat16* row = xs + m * xs_ld + c * 64 + 16 * j + 2 * tp;
       *reinterpret_cast<uint32_t*>(row) = pack_bf16x2(x0, x2);
       *reinterpret_cast<uint32_t*>(row + 8) = pack_bf16x2(x1, x3);
+    };
+    // only the M real rows: the token tile's rows past M feed only the MMA output columns of
+    // tokens past M (each output column reads its own B column), which are never stored. (A
+    // full tile keeps the compile-time trip count, which the compiler schedules better.)
+    if (a.M == MP) {
+      for (int i = threadIdx.x; i < MP * quads; i += blockDim.x) stage(i);
+    } else {
+      for (int i = threadIdx.x; i < a.M * quads; i += blockDim.x) stage(i);
     }
   }
   __syncthreads();
