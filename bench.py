@@ -356,22 +356,53 @@ def run_ours(args, world, rank, local):
     d2h = sum(t.numel() * t.element_size() for t in host_out[0])
     graphs = graphs_by_m[M]
 
-    def e2e_step(i):
-        k = i % len(graphs)
-        for n, t in zip(names, host_in[k]):
-            steps_by_m[M][k][n].copy_(t, non_blocking=True)
-        graphs[k].replay()
-        for n, t in zip(("out", "res2"), host_out[k]):
-            t.copy_(bufs_by_m[M][k][n], non_blocking=True)
+    # As a server pipelines them: step i + 1's inputs go host -> device on a copy stream while step i
+    # computes (the layer copies alternate, so its buffers are idle), and step i's results go
+    # device -> host while step i + 1 computes. Events order each copy after the compute that last
+    # used its buffers and each compute after its inputs; every step still copies all its inputs
+    # in and its results out inside the timed region.
+    copy_stream = torch.cuda.Stream(device=dev)
+    nb = len(graphs)
+    ev = lambda: [torch.cuda.Event() for _ in range(nb)]
+    h2d_done, comp_done, d2h_done = ev(), ev(), ev()
+    used = [False] * nb
 
-    for i in range(args.warmup):
-        e2e_step(i)
+    def copy_in(i):
+        k = i % nb
+        with torch.cuda.stream(copy_stream):
+            if used[k]:
+                copy_stream.wait_event(comp_done[k])  # the step that last read these inputs
+            for n, t in zip(names, host_in[k]):
+                steps_by_m[M][k][n].copy_(t, non_blocking=True)
+            h2d_done[k].record(copy_stream)
+
+    def e2e_run(first, count, start=None):
+        if start is not None:
+            copy_stream.wait_event(start)  # the first copy inside the timed region too
+        copy_in(first)
+        for i in range(first, first + count):
+            k = i % nb
+            stream.wait_event(h2d_done[k])
+            if used[k]:
+                stream.wait_event(d2h_done[k])  # results of the step that last wrote these buffers
+            graphs[k].replay()
+            comp_done[k].record(stream)
+            used[k] = True
+            if i + 1 < first + count:
+                copy_in(i + 1)
+            with torch.cuda.stream(copy_stream):
+                copy_stream.wait_event(comp_done[k])
+                for n, t in zip(("out", "res2"), host_out[k]):
+                    t.copy_(bufs_by_m[M][k][n], non_blocking=True)
+                d2h_done[k].record(copy_stream)
+        stream.wait_stream(copy_stream)
+
+    e2e_run(0, args.warmup)
     torch.cuda.synchronize()
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(args.steps):
-        e2e_step(i)
+    e2e_run(args.warmup, args.steps, e0)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
