@@ -410,12 +410,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
 
   if (warp >= 5) {
     // ================= producers
-    // Per tile: producer threads 0..63 publish their key (record pointer, the 8 scale codes;
-    // null = masked) into shared memory; then each producer warp converts units of 8 keys x 4
-    // consecutive 16-byte chunks (lane: key 8 g + lane % 8, chunk 4 q + lane / 8), so a warp's
-    // loads are whole 64-byte runs of 8 records. Loads run ahead of use: while tile j converts,
-    // tile j + 1's record chunks, tile j + 2's scale codes and tile j + 3's key-table entries
-    // are in flight.
+    // Per tile: the metadata threads publish their key (record pointer, the 8 scale codes;
+    // null = masked) into shared memory; then each conversion warp converts units of 8 keys x 4
+    // consecutive 16-byte chunks (lane: key 8 g + lane % 8, chunk 4 q + lane / 8) of its key
+    // group g, so a warp's loads are whole 64-byte runs of 8 records. Loads run ahead of use:
+    // while tile j converts, the record chunks of the next kAhead tiles and the following tiles'
+    // scale codes and key-table entries are in flight.
     static_assert(CHUNKS % 4 == 0, "records are whole 64-byte runs");
     const int ptid = tid - 5 * 32, wp = warp - 5;
     const int data_bytes = NOPE + 128;
@@ -427,20 +427,29 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
     const uint8_t** meta_p = reinterpret_cast<const uint8_t**>(smem + L::kMeta);  // [stage][64] then codes
     uint64_t* meta_c = reinterpret_cast<uint64_t*>(smem + L::kMeta + L::kMetaStages * 64 * 8);
     constexpr int kGroups = PAIR ? kTcKeys / 16 : kTcKeys / 8;  // 8-key groups this CTA converts
-    constexpr int kUnits = kGroups * (CHUNKS / 4);
-    constexpr int kItems = (kUnits + kTcProducers / 32 - 1) / (kTcProducers / 32);
-    constexpr int kMetaKeys = 8 * kGroups;  // keys this CTA locates: threads ptid < kMetaKeys
+    // 6 conversion warps, each on ONE key group (so its keys' metadata and the key part of every
+    // store offset hold for all its items) and a run of chunk groups; the 7th warp does the
+    // metadata (key table, record address, codes) and issues the pair's half-tile copies
+    constexpr int kConvWarps = 6;
+    static_assert(kConvWarps % kGroups == 0, "whole key groups a warp");
+    constexpr int kWpg = kConvWarps / kGroups;                 // warps a key group
+    constexpr int kItems = (CHUNKS / 4 + kWpg - 1) / kWpg;     // chunk groups a warp
+    constexpr int kMetaKeys = 8 * kGroups;  // keys this CTA locates
     const int g0 = PAIR ? rank * kGroups : 0;
+    // metadata threads: the 7th warp's first lanes (a pair: 24 keys), or the first 48 producer
+    // threads (a lone CTA's 48 keys)
+    const int meta_tid = PAIR ? ptid - 32 * kConvWarps : ptid;
+    const bool is_meta = meta_tid >= 0 && meta_tid < kMetaKeys;
     constexpr uint32_t kHalfBytes = (uint32_t)(kGroups * 8 * DG * 16);  // a pair's half tile
     constexpr int kChunkT = (kTcKeys / 8) * 1024;                         // a 64-dim chunk of a tile
-    const int mkey = 8 * g0 + ptid;  // thread ptid's key of a tile (ptid < kMetaKeys)
+    const int mkey = 8 * g0 + meta_tid;  // a metadata thread's key of a tile
     auto item = [&](int i, int& key, int& c) {  // this lane's (key, chunk) of its i-th unit
-      const int u = wp + (kTcProducers / 32) * i;
-      key = 8 * (g0 + u % kGroups) + (lane & 7);
-      c = 4 * (u / kGroups) + (lane >> 3);
-      return u < kUnits;
+      const int cg = (wp % kWpg) * kItems + i;
+      key = 8 * (g0 + wp / kWpg) + (lane & 7);
+      c = 4 * cg + (lane >> 3);
+      return wp < kConvWarps && cg < CHUNKS / 4;
     };
-    // key lookahead (threads ptid < kMetaKeys, key mkey of a tile)
+    // key lookahead (metadata threads, key mkey of a tile)
     auto kt_load = [&](int j) {  // the key-table entry; -1 past the chunk
       const int k = k0 + j * kTcKeys + mkey;
       return k < k1 ? a.kt[(size_t)t * a.keys_ld + k] : -1;
@@ -530,12 +539,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
         // this CTA's half (key groups g0 .. g0 + kGroups - 1: contiguous within each 64-dim
         // chunk) into the peer's tile once every producer warp has written it, a copy a chunk
         asm volatile("bar.sync 2, %0;" ::"n"(kTcProducers) : "memory");
-        // (lane c of the first producer warp copies chunk c; lane 0 also raises the peer's
+        // (lane c of the metadata warp copies chunk c; lane 0 also raises the peer's
         // expected bytes -- the transaction count is signed, so a copy may land first)
-        if (ptid < D / 64) {
+        const int ct = ptid - 32 * kConvWarps;  // the metadata warp's lanes
+        if (ct >= 0 && ct < D / 64) {
           const uint32_t peer_bar = cluster_map(b_full(ts), (uint32_t)(rank ^ 1));
-          if (ptid == 0) mbar_arrive_tx_remote(peer_bar, kHalfBytes);
-          const uint32_t off = (uint32_t)(tile_off + ptid * kChunkT + g0 * 1024);
+          if (ct == 0) mbar_arrive_tx_remote(peer_bar, kHalfBytes);
+          const uint32_t off = (uint32_t)(tile_off + ct * kChunkT + g0 * 1024);
           bulk_copy_to_peer(peer_smem + off, smem_u32(smem) + off, (uint32_t)(kGroups * 1024), peer_bar);
         }
       }
@@ -560,8 +570,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
         // record loads, so they wait for nothing newer (a use of a load waits for the loads issued
         // ahead of it); then the next key-table entry, then the records kAhead tiles on
         const bool more = j + kAhead < nsub;
-        if (more && ptid < kMetaKeys) publish(j + kAhead);
-        if (ptid < kMetaKeys) {
+        if (more && is_meta) publish(j + kAhead);
+        if (is_meta) {
           locate(la_v);
           la_v = kt_load(j + kAhead + 2);
         }
@@ -575,13 +585,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
         return true;
       }
       if (j + kAhead < nsub) {
-        if (ptid < kMetaKeys) publish(j + kAhead);
+        if (is_meta) publish(j + kAhead);
         asm volatile("bar.sync 2, %0;" ::"n"(kTcProducers) : "memory");
         if (ptid == 0) TC_TRACE(j, 14);
         issue(j + kAhead, nxt);
         if (ptid == 0) TC_TRACE(j, 15);
       }
-      if (ptid < kMetaKeys) {
+      if (is_meta) {
         locate(la_v);
         la_v = kt_load(j + kAhead + 2);
       }
@@ -592,7 +602,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
     };
     uint4 buf0[kItems], buf1[kItems];
     if (nsub > 0) {
-      if (ptid < kMetaKeys) {
+      if (is_meta) {
 #pragma unroll
         for (int i = 0; i < kAhead; ++i) {
           locate(kt_load(i));
