@@ -347,9 +347,9 @@ struct CombineArgs {
 };
 
 // One CTA a (row, head): the chunks' weights 2^(m_c - m) (0 for an empty chunk) go to shared
-// memory first and one thread sums the denominator in chunk order; then each thread sums 4 dims
-// over the chunks in order, with 8 chunks' loads in flight (the same sums, in the same order, as
-// one chunk at a time).
+// memory first; then each thread sums 4 dims over the chunks in order, with 16 chunks' loads in
+// flight, while one otherwise idle thread sums the denominator in chunk order (the same sums, in
+// the same order, as one chunk at a time).
 constexpr int kCombineThreads = 160;
 __global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(const CombineArgs a) {
   extern __shared__ float s_w[];  // [nchunks] weights, then [nchunks] the chunks' sums of p
@@ -381,38 +381,47 @@ __global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(const Com
     s_l[c] = lc;
   }
   __syncthreads();
-  if (tid == 0) {
+  // thread tid sums dims 4 tid .. 4 tid + 3 over the chunks (D <= 576: one column group a thread),
+  // 16 chunks' loads in flight; meanwhile the last thread -- past the columns -- sums the
+  // denominator in chunk order
+  const int64_t p = rope_row(a.pos[t], a.rope_rows);
+  const float* po = a.part_o + ((size_t)t * a.nchunks * a.heads + h) * a.D;  // chunk c at + c * heads * D
+  const size_t cstride = (size_t)a.heads * a.D;
+  const int d = 4 * tid;
+  const bool col = d < a.D;
+  float v[4] = {0.f, 0.f, 0.f, 0.f};
+  if (col) {
+    for (int c0 = 0; c0 < a.nchunks; c0 += 16) {
+      float4 ov[16];
+      float wv[16];
+      // (loads unconditional, so all 16 are in flight: a chunk past the end or without keys --
+      // whose partial was never written, but is allocated -- reads its slot and is skipped below)
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int c = min(c0 + u, a.nchunks - 1);
+        wv[u] = c0 + u < a.nchunks ? s_w[c] : 0.f;
+        const uint4 r = ldg_stream(po + c * cstride + d);  // (volatile: issued here, in order)
+        ov[u] = make_float4(__uint_as_float(r.x), __uint_as_float(r.y), __uint_as_float(r.z), __uint_as_float(r.w));
+      }
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {  // (selects, not branches: a skipped chunk leaves v as it is)
+        const bool on = wv[u] != 0.f;
+        v[0] = on ? fmaf(ov[u].x, wv[u], v[0]) : v[0];
+        v[1] = on ? fmaf(ov[u].y, wv[u], v[1]) : v[1];
+        v[2] = on ? fmaf(ov[u].z, wv[u], v[2]) : v[2];
+        v[3] = on ? fmaf(ov[u].w, wv[u], v[3]) : v[3];
+      }
+    }
+  }
+  if (tid == (int)blockDim.x - 1) {
     float l = exp2f(sink2 - m);
     for (int c = 0; c < a.nchunks; ++c)
       if (s_w[c] != 0.f) l = fmaf(s_l[c], s_w[c], l);
     s_inv = 1.0f / l;
   }
   __syncthreads();
-  const float inv = s_inv;
-  const int64_t p = rope_row(a.pos[t], a.rope_rows);
-  const float* po = a.part_o + ((size_t)t * a.nchunks * a.heads + h) * a.D;  // chunk c at + c * heads * D
-  const size_t cstride = (size_t)a.heads * a.D;
-  for (int d4 = tid; d4 < a.D / 4; d4 += blockDim.x) {
-    const int d = 4 * d4;
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int c0 = 0; c0 < a.nchunks; c0 += 8) {
-      float4 ov[8];
-      float wv[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int c = c0 + u;
-        wv[u] = c < a.nchunks ? s_w[c] : 0.f;
-        ov[u] = wv[u] != 0.f ? *reinterpret_cast<const float4*>(po + c * cstride + d) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        if (wv[u] == 0.f) continue;
-        v[0] += ov[u].x * wv[u];
-        v[1] += ov[u].y * wv[u];
-        v[2] += ov[u].z * wv[u];
-        v[3] += ov[u].w * wv[u];
-      }
-    }
+  if (col) {
+    const float inv = s_inv;
 #pragma unroll
     for (int i = 0; i < 4; ++i) v[i] = bf16r(v[i] * inv);
     if (d >= a.nope) {
