@@ -630,9 +630,13 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   DSV41_TRY(launch(router_kernel, dim3(cdiv(E, 8), cdiv(M, 8)), dim3(256), router_smem, st, ra));
   RouteArgs rt = {M, E, TK, (int)a->route_softmax, logits, ptr<const float>(a->bias),
                   ptr<int32_t>(a->ids), ptr<float>(a->wts)};
-  DSV41_TRY(launch(route_kernel, dim3(M), dim3(256), 0, st, rt));
   PlanArgs pl = {M, E, TK, ptr<const int32_t>(a->ids), n_u, u_expert, u_off, picks};
-  DSV41_TRY(launch(moe_plan_kernel, dim3(1), dim3(512), 0, st, pl));
+  if (M <= kRoutePlanRows) {
+    DSV41_TRY(launch2(route_plan_kernel, dim3(1), dim3(512), 0, st, rt, pl));
+  } else {
+    DSV41_TRY(launch(route_kernel, dim3(M), dim3(256), 0, st, rt));
+    DSV41_TRY(launch(moe_plan_kernel, dim3(1), dim3(512), 0, st, pl));
+  }
   // ---- shared expert
   mark(a->events, 4, st);
   DSV41_TRY(dense_go(gs, x8, x8s, st));

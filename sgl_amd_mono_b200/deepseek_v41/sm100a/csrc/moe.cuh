@@ -103,26 +103,25 @@ struct RouteArgs {
   float* wts;           // [M, topk]
 };
 
-// A CTA of 256 threads a row: the scores in parallel (one expert a thread, two when E > 256),
-// then warp 0 selects the top-k with experts e = lane + 32 i.
-__global__ void __launch_bounds__(256) route_kernel(const RouteArgs a) {
-  __shared__ float s_val[512], s_orig[512];
-  const int t = blockIdx.x, lane = threadIdx.x & 31;
-  pdl_wait();
-  for (int e = threadIdx.x; e < a.E; e += blockDim.x) {
-    const float l = a.logits[(size_t)t * a.E + e];
-    if (a.softmax) {
-      s_val[e] = isnan(l) ? -INFINITY : l;
-      s_orig[e] = l;
-    } else {
-      const float sc = route_score(l);
-      s_orig[e] = isnan(sc) ? 0.f : sc;
-      const float v = __fadd_rn(sc, a.bias[e]);
-      s_val[e] = isnan(v) ? -INFINITY : v;
-    }
+// The selection value (NaN -> -inf) and the original score of (row t, expert e) into the row's
+// shared-memory arrays.
+__device__ __forceinline__ void route_score_one(const RouteArgs& a, int t, int e, float* s_val, float* s_orig) {
+  const float l = a.logits[(size_t)t * a.E + e];
+  if (a.softmax) {
+    s_val[e] = isnan(l) ? -INFINITY : l;
+    s_orig[e] = l;
+  } else {
+    const float sc = route_score(l);
+    s_orig[e] = isnan(sc) ? 0.f : sc;
+    const float v = __fadd_rn(sc, a.bias[e]);
+    s_val[e] = isnan(v) ? -INFINITY : v;
   }
-  __syncthreads();
-  if (threadIdx.x >= 32) return;
+}
+
+// One warp selects row t's top-k from its scores (experts e = lane + 32 i, E <= 512) and writes
+// ids / wts; lane k < topk also leaves its id in s_ids[k] when s_ids is given.
+__device__ __forceinline__ void route_select(const RouteArgs& a, int t, const float* s_val, const float* s_orig,
+                                             int lane, int* s_ids) {
   constexpr int kMaxPer = 16;  // E <= 512
   const int per = (a.E + 31) / 32;
   float val[kMaxPer], orig[kMaxPer];
@@ -194,6 +193,18 @@ __global__ void __launch_bounds__(256) route_kernel(const RouteArgs a) {
     a.ids[(size_t)t * a.topk + lane] = my_id;
     a.wts[(size_t)t * a.topk + lane] = __fmul_rn(my_w, scale);
   }
+  if (s_ids != nullptr && lane < a.topk) s_ids[lane] = my_id;
+}
+
+// A CTA of 256 threads a row: the scores in parallel (one expert a thread, two when E > 256),
+// then warp 0 selects the top-k.
+__global__ void __launch_bounds__(256) route_kernel(const RouteArgs a) {
+  __shared__ float s_val[512], s_orig[512];
+  const int t = blockIdx.x;
+  pdl_wait();
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x) route_score_one(a, t, e, s_val, s_orig);
+  __syncthreads();
+  if (threadIdx.x < 32) route_select(a, t, s_val, s_orig, threadIdx.x, nullptr);
   pdl_launch();
 }
 
@@ -211,14 +222,10 @@ struct PlanArgs {
 // a block-wide inclusive scan of (picks, union flag) an expert, then each pick's rank among the
 // earlier picks of its expert from the ids staged in shared memory.
 constexpr int kPlanMaxPicks = 48 * 32;
-__global__ void __launch_bounds__(512) moe_plan_kernel(const PlanArgs a) {
-  __shared__ int cnt[512], s_off[512], s_uf[512];
-  __shared__ int s_ids[kPlanMaxPicks];
-  pdl_wait();
+// The plan of the P = M topk picks whose ids sit in s_ids; s_ids filled and cnt zeroed by the
+// caller before a barrier. 512 threads.
+__device__ __forceinline__ void plan_picks(const PlanArgs& a, const int* s_ids, int* cnt, int* s_off, int* s_uf) {
   const int P = a.M * a.topk, tid = threadIdx.x;
-  cnt[tid] = 0;
-  for (int p = tid; p < P; p += blockDim.x) s_ids[p] = a.ids[p];
-  __syncthreads();
   for (int p = tid; p < P; p += blockDim.x) atomicAdd(&cnt[s_ids[p]], 1);
   __syncthreads();
   // inclusive scans (Hillis-Steele) of the counts and of the union flags over experts
@@ -252,6 +259,45 @@ __global__ void __launch_bounds__(512) moe_plan_kernel(const PlanArgs a) {
     for (int q = 0; q < p; ++q) before += (s_ids[q] == e);
     a.picks[cnt[e] + before] = p;
   }
+}
+
+__global__ void __launch_bounds__(512) moe_plan_kernel(const PlanArgs a) {
+  __shared__ int cnt[512], s_off[512], s_uf[512];
+  __shared__ int s_ids[kPlanMaxPicks];
+  pdl_wait();
+  const int P = a.M * a.topk, tid = threadIdx.x;
+  cnt[tid] = 0;
+  for (int p = tid; p < P; p += blockDim.x) s_ids[p] = a.ids[p];
+  __syncthreads();
+  plan_picks(a, s_ids, cnt, s_off, s_uf);
+  pdl_launch();
+}
+
+// Routing and the plan in one CTA of 512 threads for M <= kRoutePlanRows (E <= 512, topk <= 32):
+// every row's scores in parallel, warp t selects row t's top-k (ids into shared memory as well
+// as global), then the plan of those picks. Saves the small-M decode one launch boundary; the
+// arithmetic is route_kernel's and moe_plan_kernel's.
+constexpr int kRoutePlanRows = 8;
+__global__ void __launch_bounds__(512) route_plan_kernel(const RouteArgs r, const PlanArgs a) {
+  __shared__ float s_val[kRoutePlanRows * 512], s_orig[kRoutePlanRows * 512];
+  __shared__ int cnt[512], s_off[512], s_uf[512];
+  __shared__ int s_ids[kRoutePlanRows * 32];
+  pdl_wait();
+  const int tid = threadIdx.x, warp = tid >> 5;
+  cnt[tid] = 0;
+  // M E <= 8 x 512: a thread's (up to) 8 scores unrolled, so their loads and math overlap
+#pragma unroll
+  for (int j = 0; j < kRoutePlanRows; ++j) {
+    const int i = tid + 512 * j;
+    if (i < r.M * r.E) {
+      const int t = i / r.E;
+      route_score_one(r, t, i - t * r.E, s_val + 512 * t, s_orig + 512 * t);
+    }
+  }
+  __syncthreads();
+  if (warp < r.M) route_select(r, warp, s_val + 512 * warp, s_orig + 512 * warp, tid & 31, s_ids + warp * r.topk);
+  __syncthreads();
+  plan_picks(a, s_ids, cnt, s_off, s_uf);
   pdl_launch();
 }
 
