@@ -18,6 +18,10 @@ scaling: the same M rows at every N; ``value`` = M / the max-over-ranks layer ti
 NCCL variant of the all-reduces (all-gather + rank-order sum) and the exchanges alone are
 timed beside it, at the headline M.
 
+``config.configs`` carries the other BASELINE configs as sections: 3 (K2i -> top-2048 -> the
+sparse layer), 5 (the verify step's pieces) and 4 (a 40-layer decode step, 16 rows at context
+16384, chained layers in one CUDA graph; at N > 1 with the NCCL variant beside it).
+
 ``--impl reference`` times the reference path's CPU restatement (the repository's oracle:
 torch fp32/fp64 on the host cores, all threads) on a bounded sample of the same workload.
 """
@@ -314,6 +318,7 @@ def run_ours(args, world, rank, local):
     if not args.skip_configs:
         other["3"] = run_config3(args, runner, layers, world, stream, hbm_peak)
         other["5"] = run_config5(args, runner, layers, world, rank, stream, hbm_peak)
+        other["4"] = run_config4(args, runner, layers, world, stream, hbm_peak)
         runner.check()
     tp_extra = tp_comparison(args, runner, layers, steps_by_m[M], bufs_by_m[M], M, world, stream) if tp > 1 else None
 
@@ -597,6 +602,53 @@ def run_config5(args, runner, layers, world, rank, stream, hbm_peak):
             "step_us_target_layer_draft_head": round(step_ms * 1e3, 2),
             "note": "the draft layer has the target layer's shapes and cost (config 5's 1-layer draft); "
                     "a 40-layer target adds 39 more layer_us"}
+
+
+def run_config4(args, runner, layers, world, stream, hbm_peak):
+    """a full 40-layer decode step, 16 rows at KV context 16384, the layers
+    chained as the model runs them (layer j + 1's K1 takes layer j's K2 outputs: x, residual,
+    post, comb, pre), each layer with its own paged KV cache, the weights cycling over the bound
+    layer copies (each larger than L2). One CUDA graph holds the 40 K1 + K2 launches; at TP > 1
+    the step is also timed with the NCCL variant of the two all-reduces a layer."""
+    from sgl_amd_mono_b200.deepseek_v41 import roofline, synth
+    from sgl_amd_mono_b200.deepseek_v41.sm100a.runner import MonoRunner
+
+    M, ctx, n_layers = 16, 16384, 40
+    s, dev = runner.s, runner.dev
+    caches = [synth.make_step(s, M, ctx, args.seed + 700 + j, dev) for j in range(n_layers)]
+
+    def chain(r, record=None):
+        b = r.buffers(M, ctx)
+        for j, st in enumerate(caches):
+            if j > 0:
+                st = dict(st, res=b["res2"], x=b["out"], post=b["post_f"], comb=b["comb_f"], pre=b["pre_f"])
+            r.k1(layers[j % len(layers)], st, M)
+            r.k2(layers[j % len(layers)], st, M, b)
+            if record is not None:
+                record.append((int(torch.unique(b["ids"][:M]).numel()), int(b["klen"][:M].sum().item())))
+        return b
+
+    seen = []
+    b = chain(runner, seen)  # eager: buffers, scratch and the layers' routing for the byte count
+    torch.cuda.synchronize()
+    finite = bool(torch.isfinite(b["out"].float()).all().item())
+    reps = max(3, min(args.steps, 10))
+    ms = _graph_time(args, [lambda: chain(runner)], world, stream, reps=reps)
+    step_bytes = sum(roofline.layer_bytes(s, u, k)["total"] for u, k in seen)
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    out = {"workload": f"config4: {n_layers}-layer decode step (chained layers, own KV caches, weights cycling "
+                       f"over {len(layers)} bound copies), {M} rows, ctx {ctx}, tp{s.tp}",
+           "rows": M, "layers": n_layers, "us_per_step": round(ms * 1e3, 1),
+           "us_per_layer": round(ms * 1e3 / n_layers, 2), "tokens_s": round(M / (ms * 1e-3), 1),
+           "algorithmic_GB_per_step": round(step_bytes / 1e9, 3), "GBs": round(gbs, 1),
+           "frac_hbm": round(gbs / hbm_peak, 4), "outputs_finite": finite, "replays": reps}
+    if s.tp > 1:
+        nccl = MonoRunner(s, dev, rank=runner.rank, group=None, allreduce="nccl")
+        ms_n = _graph_time(args, [lambda: chain(nccl)], world, stream, reps=reps)
+        out["us_per_step_nccl_variant"] = round(ms_n * 1e3, 1)
+        del nccl
+    runner.check()
+    return out
 
 
 def tp_comparison(args, runner, layers, steps, bufs, M, world, stream):
