@@ -347,11 +347,16 @@ struct CombineArgs {
 };
 
 // One CTA a (row, head): the chunks' weights 2^(m_c - m) (0 for an empty chunk) go to shared
-// memory first; then each thread sums 4 dims over the chunks in order, with 16 chunks' loads in
-// flight, while one otherwise idle thread sums the denominator in chunk order (the same sums, in
-// the same order, as one chunk at a time).
+// memory first; then each thread sums 4 dims over the chunks in order, B chunks' loads a batch,
+// while one otherwise idle thread sums the denominator in chunk order (the same sums, in the same
+// order, as one chunk at a time, for either B).
+// B = 16 (many CTAs: 12 resident an SM at ptxas's 32 registers, which keeps only a few of a
+// thread's loads in flight; occupancy hides the rest). B = 32 when the grid is one CTA an SM or
+// less and there are more than 16 chunks (M = 1: 64 CTAs over 57 chunks): one CTA an SM lets
+// ptxas hold all 32 loads of a batch in registers (209): 2 batches of round trips a head.
 constexpr int kCombineThreads = 160;
-__global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(const CombineArgs a) {
+template <int B>
+__global__ void __launch_bounds__(kCombineThreads, B == 32 ? 1 : 12) attn_combine_kernel(const CombineArgs a) {
   extern __shared__ float s_w[];  // [nchunks] weights, then [nchunks] the chunks' sums of p
   float* s_l = s_w + a.nchunks;
   __shared__ float s_red[kCombineThreads / 32];
@@ -391,20 +396,20 @@ __global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(const Com
   const bool col = d < a.D;
   float v[4] = {0.f, 0.f, 0.f, 0.f};
   if (col) {
-    for (int c0 = 0; c0 < a.nchunks; c0 += 16) {
-      float4 ov[16];
-      float wv[16];
-      // (loads unconditional, so all 16 are in flight: a chunk past the end or without keys --
+    for (int c0 = 0; c0 < a.nchunks; c0 += B) {
+      float4 ov[B];
+      float wv[B];
+      // (loads unconditional, so all B are in flight: a chunk past the end or without keys --
       // whose partial was never written, but is allocated -- reads its slot and is skipped below)
 #pragma unroll
-      for (int u = 0; u < 16; ++u) {
+      for (int u = 0; u < B; ++u) {
         const int c = min(c0 + u, a.nchunks - 1);
         wv[u] = c0 + u < a.nchunks ? s_w[c] : 0.f;
         const uint4 r = ldg_stream(po + c * cstride + d);  // (volatile: issued here, in order)
         ov[u] = make_float4(__uint_as_float(r.x), __uint_as_float(r.y), __uint_as_float(r.z), __uint_as_float(r.w));
       }
 #pragma unroll
-      for (int u = 0; u < 16; ++u) {  // (selects, not branches: a skipped chunk leaves v as it is)
+      for (int u = 0; u < B; ++u) {  // (selects, not branches: a skipped chunk leaves v as it is)
         const bool on = wv[u] != 0.f;
         v[0] = on ? fmaf(ov[u].x, wv[u], v[0]) : v[0];
         v[1] = on ? fmaf(ov[u].y, wv[u], v[1]) : v[1];

@@ -588,7 +588,9 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   cb.part_o = part_o; cb.part_ml = part_ml; cb.sink = ptr<const float>(a->sink);
   cb.cos_sin = ptr<const float>(a->cos_sin); cb.pos = ptr<const int64_t>(a->pos); cb.xo = xo;
   cb.rope_rows = a->rope_rows;
-  DSV41_TRY(launch(attn_combine_kernel, dim3(M * heads), dim3(kCombineThreads), nchunks * 8, st, cb));
+  DSV41_TRY(nchunks > 16 && M * heads <= sms
+                ? launch(attn_combine_kernel<32>, dim3(M * heads), dim3(kCombineThreads), nchunks * 8, st, cb)
+                : launch(attn_combine_kernel<16>, dim3(M * heads), dim3(kCombineThreads), nchunks * 8, st, cb));
   // ---- wo_a -> X8B -> wo_b -> partial -> reduce
   mark(a->events, 1, st);
   DSV41_TRY(gemv_go(ga, st));

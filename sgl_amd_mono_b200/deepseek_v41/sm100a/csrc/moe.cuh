@@ -124,7 +124,10 @@ __device__ __forceinline__ void route_select(const RouteArgs& a, int t, const fl
                                              int lane, int* s_ids) {
   constexpr int kMaxPer = 16;  // E <= 512
   const int per = (a.E + 31) / 32;
+  // (every loop over a lane's values runs to the compile-time kMaxPer, guarded by i < per, so
+  // val / orig stay in registers instead of a local-memory frame indexed at run time)
   float val[kMaxPer], orig[kMaxPer];
+#pragma unroll
   for (int i = 0; i < kMaxPer; ++i) {
     const int e = lane + 32 * i;
     const bool in = i < per && e < a.E;
@@ -134,15 +137,16 @@ __device__ __forceinline__ void route_select(const RouteArgs& a, int t, const fl
   float my_w = 0.f;
   int my_id = 0;
   float total = 0.f;
-  double ex[32];
+  double tot = 0.0, mine = 0.0;  // softmax: the picks' exps summed in pick order; lane k's own exp
   float first = 0.f;
   for (int k = 0; k < a.topk; ++k) {
     // the best (value, lowest id) of the lane, then of the warp
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int i = 0; i < per; ++i) {
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
       const int e = lane + 32 * i;
-      if (e < a.E && (val[i] > bv || (val[i] == bv && e < bi))) {
+      if (i < per && e < a.E && (val[i] > bv || (val[i] == bv && e < bi))) {
         bv = val[i];
         bi = e;
       }
@@ -160,7 +164,8 @@ __device__ __forceinline__ void route_select(const RouteArgs& a, int t, const fl
     float ow = 0.f;
     if ((bi & 31) == lane) {
       const int i = bi >> 5;
-      for (int q = 0; q < per; ++q)
+#pragma unroll
+      for (int q = 0; q < kMaxPer; ++q)
         if (q == i) {
           ow = orig[q];
           val[q] = __int_as_float(0x7fc00000);
@@ -169,7 +174,9 @@ __device__ __forceinline__ void route_select(const RouteArgs& a, int t, const fl
     ow = __shfl_sync(0xffffffffu, ow, bi & 31);
     if (a.softmax) {
       if (k == 0) first = ow;
-      ex[k] = det_exp(__dadd_rn((double)ow, -(double)first));
+      const double ex = det_exp(__dadd_rn((double)ow, -(double)first));
+      tot = __dadd_rn(tot, ex);
+      if (lane == k) mine = ex;
     } else {
       total = __fadd_rn(total, ow);
     }
@@ -179,12 +186,7 @@ __device__ __forceinline__ void route_select(const RouteArgs& a, int t, const fl
     }
   }
   if (a.softmax) {
-    double tot = 0.0;
-    for (int k = 0; k < a.topk; ++k) tot = __dadd_rn(tot, ex[k]);
     if (lane < a.topk) {
-      double mine = 0.0;
-      for (int k = 0; k < a.topk; ++k)
-        if (k == lane) mine = ex[k];
       a.ids[(size_t)t * a.topk + lane] = my_id;
       a.wts[(size_t)t * a.topk + lane] = (float)__ddiv_rn(mine, tot);
     }
