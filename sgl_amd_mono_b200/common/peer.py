@@ -179,5 +179,12 @@ class PeerBuffer:
             raise DeviceGuardError(f"rank {self.rank}: {msg or 'device guard fired'}")
 
     def close(self) -> None:
-        """Unmap the peers' regions and free this rank's (after the last launch using them)."""
+        """Unmap the peers' regions and free this rank's. Collective: this rank's queued work
+        is finished first (a device synchronize), then every rank meets at a barrier, so no
+        rank frees its region while another rank's last exchange may still push into it or
+        poll its flags."""
+        if torch.cuda.is_available() and torch.cuda.is_initialized():
+            torch.cuda.synchronize()
+        if dist.is_available() and dist.is_initialized():
+            dist.barrier(group=self.group)
         self._release()

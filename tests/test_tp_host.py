@@ -90,6 +90,36 @@ def _refuse(rank, world, port, where):
         dist.destroy_process_group()
 
 
+def _close_order(rank, world, port, q):
+    import time
+    _init(rank, world, port)
+    try:
+        nat = FakeNative(rank)
+        pb = P.PeerBuffer(64, None, rank, world, "cpu", native=nat)
+        if rank == 1:
+            time.sleep(1.0)  # rank 1's last exchange is still queued when rank 0 closes
+        entered = time.time()
+        pb.close()
+        released = time.time()
+        q.put((rank, entered, released, list(nat.freed)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_close_waits_for_every_rank_gloo():
+    """No rank frees its region before every rank has reached close()."""
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    pc = mp.start_processes(_close_order, args=(2, _free_port(), q), nprocs=2, start_method="spawn", join=False)
+    got = sorted([q.get(), q.get()])
+    while not pc.join():
+        pass
+    (_, e0, r0, f0), (_, e1, r1, f1) = got
+    assert f0 == [0x1000] and f1 == [0x2000]
+    assert r0 >= e1 - 0.05, (r0, e1)  # rank 0 released only after rank 1 arrived (clock slack)
+    assert r0 - e0 > 0.5
+
+
 def test_peer_handshake_gloo():
     mp.start_processes(_handshake, args=(2, _free_port()), nprocs=2, start_method="spawn")
 

@@ -16,6 +16,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 DSV41_ESCRATCH = -3
+ARRAY_BYTES = 4 << 20  # DSV41_NOALLOC_SCRATCH_BYTES
 
 
 def _noalloc(args):
@@ -45,18 +46,50 @@ def _args(w, codes, x, y):
 def test_noalloc_matches_scratch_entry_two_calls():
     from sgl_amd_mono_b200.common import ext
     from sgl_amd_mono_b200.deepseek_v41.sm100a import ops
-    # two shapes whose plans split K (partials in the library array), back to back
-    for M, N, K, seed in ((16, 1600, 4096, 1), (8, 4096, 8192, 2)):
+    # two shapes whose plans split K (partials in the library array), queued back to back on one
+    # stream with no host sync between them -- the ordering the shared array is safe under --
+    # then one sync and both compared
+    cases = [(16, 1600, 4096, 1), (8, 4096, 8192, 2)]
+    inputs, wants, gots = [], [], []
+    for M, N, K, seed in cases:
         w, codes, x = _case(M, N, K, seed)
         a = _args(w, codes, x, torch.empty(1, device="cuda"))
         assert ext.query("dsv41_gemv_fp8_scratch_bytes", a) > 0, "the case must use K-slice partials"
-        want = ops.gemv_fp8(x, w, codes)
+        wants.append(ops.gemv_fp8(x, w, codes))
+        inputs.append((w, codes, x))
+    torch.cuda.synchronize()
+    for (w, codes, x), (M, N, K, _) in zip(inputs, cases):
         got = torch.full((M, N), float("nan"), device="cuda")
         rc = _noalloc(_args(w, codes, x, got))
-        torch.cuda.synchronize()
         assert rc == 0, rc
+        gots.append(got)
+    torch.cuda.synchronize()
+    for got, want in zip(gots, wants):
         # the same kernel, plan and slice order: the same bits
         assert torch.equal(got, want), (got - want).abs().max().item()
+
+
+def test_noalloc_array_edge():
+    """A shape whose partials fill the array exactly is served (and equals the scratch entry);
+    one 8 rows wider is refused before any launch."""
+    from sgl_amd_mono_b200.common import ext
+    from sgl_amd_mono_b200.deepseek_v41.sm100a import ops
+    M, N, K = 32, 8192, 4096
+    w, codes, x = _case(M, N, K, 4)
+    need = ext.query("dsv41_gemv_fp8_scratch_bytes", _args(w, codes, x, torch.empty(1, device="cuda")))
+    assert need == ARRAY_BYTES, (need, "the plan of this shape no longer fills the array exactly")
+    want = ops.gemv_fp8(x, w, codes)
+    got = torch.full((M, N), float("nan"), device="cuda")
+    assert _noalloc(_args(w, codes, x, got)) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    N2 = N + 8
+    w2, codes2, x2 = _case(M, N2, K, 5)
+    assert ext.query("dsv41_gemv_fp8_scratch_bytes", _args(w2, codes2, x2, torch.empty(1, device="cuda"))) > ARRAY_BYTES
+    y = torch.zeros(M, N2, device="cuda")
+    assert _noalloc(_args(w2, codes2, x2, y)) == DSV41_ESCRATCH
+    torch.cuda.synchronize()
+    assert bool((y == 0).all())
 
 
 def test_noalloc_refuses_partials_over_the_array():
