@@ -50,6 +50,20 @@ UNIT = "tokens/s"
 EXPERT_DRAM_BYTES_PER_UNIT = (1.774859e9 + 27.109376e6 + 0.887746e9 + 14.774784e6) / 199
 
 
+REF_SAMPLE_ROWS = 4  # rows of the step's M the reference arm's CPU oracle runs a step
+TARGET_LAYERS = 40  # config 5's target model depth
+DRAFT_WINDOW = 128  # the draft's attention window (the reference's WINDOW, draft.py:30)
+
+
+def workload_config(args, world):
+    """The workload both arms report, identical for the GPU path and the reference arm (what was
+    measured goes to ``detail``)."""
+    return {"workload": f"config2: one MoE decode layer (K1 + K2), {args.rows} rows, ctx {args.ctx}",
+            "rows": args.rows, "ctx": args.ctx, "tp": world, "parallelism": f"tp{world}",
+            "allreduce": "in-kernel peer push, rank-order fp32 sum" if world > 1 else "none (tp1)",
+            "l2": f"inputs larger than L2: steps alternate {args.layers} layer copies of > 126 MB each"}
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -109,7 +123,7 @@ class Clocks:
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={self.QUERY}",
-                                       "--format=csv,noheader,nounits", "-lms", "50"],
+                                       "--format=csv,noheader,nounits", "-lms", "20"],
                                       stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
@@ -195,14 +209,24 @@ def cpu_layer(w, step, shape, rows: int) -> float:
     return time.perf_counter() - t0
 
 
-def cpu_inputs(args, shape):
-    """Config-2 weights and a one-row step on the host (drawn on the GPU when there is one)."""
+def cpu_inputs(args, shape, rows):
+    """Config-2 weights and a ``rows``-row step on the host (drawn on the GPU when there is one,
+    with the GPU arm's seeds: the headline step of layer copy 0)."""
     from sgl_amd_mono_b200.deepseek_v41 import synth
     dev = torch.device("cuda") if torch.cuda.is_available() else torch.device("cpu")
-    w = synth.make_layer(shape, args.seed, dev, positions=args.ctx + 8)
-    step = synth.make_step(shape, 1, args.ctx, args.seed + 1000, dev)
+    positions = max(args.ctx, 32768) + 8
+    w = synth.make_layer(shape, args.seed, dev, positions=positions)
+    step = synth.make_step(shape, rows, args.ctx, args.seed + rows, dev)
     cpu = lambda d: {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in d.items()}  # noqa: E731
     return cpu(w), cpu(step)
+
+
+def sample_rows(step, rows, first):
+    """Rows first .. first + rows (mod M) of a step, as a step of their own (the cache shared)."""
+    M = step["res"].shape[0]
+    idx = torch.tensor([(first + i) % M for i in range(rows)])
+    return {k: (v[idx] if torch.is_tensor(v) and k != "cache" and v.dim() > 0 and v.shape[0] == M else v)
+            for k, v in step.items()}
 
 
 def run_reference(args, world, rank):
@@ -211,19 +235,23 @@ def run_reference(args, world, rank):
         return
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    w, step = cpu_inputs(args, CONFIG2)
-    for _ in range(args.warmup):
-        cpu_layer(w, step, CONFIG2, 1)
-    ts = [cpu_layer(w, step, CONFIG2, 1) for _ in range(args.steps)]
+    w, step = cpu_inputs(args, CONFIG2, args.rows)
+    k = min(REF_SAMPLE_ROWS, args.rows)
+    for i in range(args.warmup):
+        cpu_layer(w, sample_rows(step, k, k * i), CONFIG2, k)
+    ts = [cpu_layer(w, sample_rows(step, k, k * (args.warmup + i)), CONFIG2, k) for i in range(args.steps)]
     t = sum(ts) / len(ts)
-    v = 1.0 / t
-    sample = f"1 decode row of config 2 (ctx {args.ctx}), one layer, a step; torch CPU, {threads} threads"
+    v = k / t
+    sample = (f"{k} of the step's {args.rows} decode rows a step (rotating through the rows), the whole layer "
+              f"for them (ctx {args.ctx}); the reference path's CPU restatement (torch fp32/fp64), {threads} threads")
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic (random-init, seeded)",
-        "config": {"workload": "config2: one MoE decode layer, ctx %d" % args.ctx, "rows": 1,
-                   "reference_kind": "port (the repository's CPU oracle of the reference path)"},
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic (random-init, seeded)",
+        "config": workload_config(args, world),
+        "detail": {"reference_kind": "port (the repository's CPU oracle of the reference path: the reference's "
+                                     "own kernels are FlyDSL for gfx950 and cannot run here)",
+                   "sample_rows": k},
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -321,6 +349,8 @@ def run_ours(args, world, rank, local):
         other["4"] = run_config4(args, runner, layers, world, stream, hbm_peak)
         runner.check()
     tp_extra = tp_comparison(args, runner, layers, steps_by_m[M], bufs_by_m[M], M, world, stream) if tp > 1 else None
+    parity = (tp_parity(args, steps_by_m[M][0], bufs_by_m[M][0], M, world, rank, dev, positions) if tp > 1 else
+              "tp1: the -m gpu tests check these kernels against the oracle")
 
     # ---- stage timelines (eager launches, CUDA events at stage boundaries on the stream)
     n1, n2 = len(abi.K1_STAGES), len(abi.K2_STAGES)
@@ -418,11 +448,12 @@ def run_ours(args, world, rank, local):
         torch.set_num_threads(threads)
         W = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in layers[0].w.items()}
         S = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in steps_by_m[M][0].items()}
-        cpu_layer(W, S, shape, 1)
-        t_cpu = min(cpu_layer(W, S, shape, 1) for _ in range(2))
-        cpu = {"value": 1.0 / t_cpu, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"1 decode row of the same layer (ctx {args.ctx}), best of 2 after a warm-up; "
-                         f"torch CPU oracle, {threads} threads"}
+        k = min(REF_SAMPLE_ROWS, M)
+        cpu_layer(W, sample_rows(S, k, 0), shape, k)
+        t_cpu = min(cpu_layer(W, sample_rows(S, k, k * (i + 1)), shape, k) for i in range(2))
+        cpu = {"value": k / t_cpu, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{k} of the step's {M} decode rows, the whole layer for them (ctx {args.ctx}), best of 2 "
+                         f"after a warm-up; the reference path's CPU restatement (torch), {threads} threads"}
         del W, S
 
     if rank == 0:
@@ -432,18 +463,16 @@ def run_ours(args, world, rank, local):
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "fp8/mxfp4 weights, bf16 activations",
             "data": "synthetic (random-init, seeded)",
-            "config": {"workload": f"config2: one MoE decode layer (K1 + K2), {M} rows, ctx {args.ctx}",
-                       "rows": M, "ctx": args.ctx, "tp": tp, "parallelism": f"tp{tp}",
-                       "allreduce": "in-kernel peer push, rank-order fp32 sum" if tp > 1 else "none (tp1)",
+            "config": workload_config(args, world),
+            "detail": {"algorithmic_MB_per_step": results[M]["algorithmic_MB"],
                        "tp_comparison": tp_extra,
                        "configs": other,
-                       "l2": f"steps alternate {args.layers} layer copies; a step reads "
-                             f"{results[M]['algorithmic_MB']} MB (> 126 MB L2)",
                        "layer_roofline": {"GBs": results[M]["GBs"], "frac": results[M]["frac_hbm"],
                                           "peak_GBs": hbm_peak, "peak": peak_src},
                        "sweep": {str(k): {kk: vv for kk, vv in v.items() if kk != "clocks"}
                                  for k, v in results.items()},
                        "stages_us": {k: round(v * 1e3, 2) for k, v in stage_ms.items()}},
+            "parity": parity,
             "roofline": {"bound": "hbm", "kernel": "routed experts (gate/up + act + down)",
                          "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4),
@@ -569,6 +598,19 @@ def run_config5(args, runner, layers, world, rank, stream, hbm_peak):
         runner.k2(L, st, M, b)
 
     ms_layer = _graph_time(args, [lambda i=i: layer(i) for i in range(2)], world, stream, reps=20)
+    # the draft: its own layer (config-2 shapes, its own weights) over the same 48 rows, each
+    # seeing the draft's window of 128 keys plus its causal prefix of the block (the
+    # reference's draft reads WINDOW 128 + the block, draft.py:30-31, 173-195)
+    draft_L = runner.bind(synth.make_layer(s, args.seed + 4242, dev, positions=ctx + 8, rank=runner.rank),
+                          tag="draft")
+    dsteps = [synth.make_step(s, M, DRAFT_WINDOW + P, args.seed + 520 + i, dev, per_req=P) for i in range(2)]
+
+    def draft(i):
+        st = dsteps[i]
+        b = runner.k1(draft_L, st, M)
+        runner.k2(draft_L, st, M, b)
+
+    ms_draft = _graph_time(args, [lambda i=i: draft(i) for i in range(2)], world, stream, reps=20)
     vl = V // world
     g = torch.Generator(device=dev).manual_seed(args.seed + 600)
     heads = [(torch.randn(vl, s.hidden, generator=g, device=dev) * 0.02).to(torch.bfloat16) for _ in range(2)]
@@ -592,16 +634,19 @@ def run_config5(args, runner, layers, world, rank, stream, hbm_peak):
 
     ms_head = _graph_time(args, [lambda i=i: head(i) for i in range(2)], world, stream)
     head_bytes = vl * s.hidden * 2
-    step_ms = 2 * ms_layer + ms_head  # one target layer + the one-layer draft + the head
-    return {"workload": f"config5: verify step pieces, {M} rows (8 x {P}), ctx {ctx} causal blocks, "
-                        f"LM head {V} x {s.hidden} bf16, tp{runner.s.tp}",
-            "rows": M, "layer_us": round(ms_layer * 1e3, 2), "draft_us": round(ms_layer * 1e3, 2),
+    step_ms = TARGET_LAYERS * ms_layer + ms_draft + ms_head
+    del draft_L, dsteps
+    return {"workload": f"config5: verify step, {M} rows (8 x {P}), ctx {ctx} causal blocks, a {TARGET_LAYERS}-layer "
+                        f"target, the 1-layer draft (window {DRAFT_WINDOW} + the block), LM head {V} x {s.hidden} "
+                        f"bf16 + argmax + greedy acceptance, tp{runner.s.tp}",
+            "rows": M, "target_layer_us": round(ms_layer * 1e3, 2), "draft_us": round(ms_draft * 1e3, 2),
             "lm_head_argmax_accept_us": round(ms_head * 1e3, 2),
             "lm_head_GBs": round(head_bytes / (ms_head * 1e-3) / 1e9, 1),
             "lm_head_frac_hbm": round(head_bytes / (ms_head * 1e-3) / 1e9 / hbm_peak, 4),
-            "step_us_target_layer_draft_head": round(step_ms * 1e3, 2),
-            "note": "the draft layer has the target layer's shapes and cost (config 5's 1-layer draft); "
-                    "a 40-layer target adds 39 more layer_us"}
+            "verify_step_us": round(step_ms * 1e3, 1),
+            "verify_tokens_s": round(M / (step_ms * 1e-3), 1),
+            "note": f"verify_step_us = {TARGET_LAYERS} x target_layer_us (each target layer CUDA-graph timed on its own "
+                    "copy of the weights) + draft_us + lm_head_argmax_accept_us"}
 
 
 def run_config4(args, runner, layers, world, stream, hbm_peak):
@@ -649,6 +694,45 @@ def run_config4(args, runner, layers, world, stream, hbm_peak):
         del nccl
     runner.check()
     return out
+
+
+def tp_parity(args, step, b, M, world, rank, dev, positions):
+    """At TP > 1: the layer's output on every rank (the all-reduced MoE output of the headline
+    step of layer copy 0) against a TP = 1 run of the same full layer and step on rank 0, and
+    every rank's output against rank 0's. Bounds: the MoE output within the reference's
+    ffn.moe.rel (1.5e-2) of the TP = 1 output, the routed expert sets equal on >= 95 % of rows
+    (a TP = N attention output sums N bf16 partials where TP = 1 has one, so a row whose 8th and
+    9th expert scores lie within that rounding can route differently), every rank bit-identical."""
+    import torch.distributed as dist
+
+    from sgl_amd_mono_b200.deepseek_v41 import synth
+    from sgl_amd_mono_b200.deepseek_v41.shapes import CONFIG2
+    from sgl_amd_mono_b200.deepseek_v41.sm100a.runner import MonoRunner
+
+    torch.cuda.synchronize()
+    out, ids = b["out"][:M].clone(), b["ids"][:M].clone()
+    gathered = [torch.empty_like(out) for _ in range(world)]
+    dist.all_gather(gathered, out)
+    res = None
+    if rank == 0:
+        r1 = MonoRunner(CONFIG2, dev)
+        L1 = r1.bind(synth.make_layer(CONFIG2, args.seed, dev, positions=positions), tag="tp1 parity")
+        st = dict(step, cache=step["cache"].clone())
+        b1 = r1.k1(L1, st, M)
+        r1.k2(L1, st, M, b1)
+        torch.cuda.synchronize()
+        o1 = b1["out"][:M].float()
+        rel = float((out.float() - o1).norm() / o1.norm())
+        same_sets = float((ids.sort(1).values == b1["ids"][:M].sort(1).values).all(1).float().mean())
+        ranks_equal = all(torch.equal(g, out) for g in gathered)
+        ok = rel < 1.5e-2 and same_sets >= 0.95 and ranks_equal
+        res = {"status": "ok" if ok else "FAILED", "vs_tp1_moe_rel": round(rel, 6),
+               "vs_tp1_expert_sets_equal_rows": round(same_sets, 4), "ranks_bit_identical": ranks_equal,
+               "bounds": "moe rel < 1.5e-2, expert sets equal on >= 95 % of rows, ranks identical"}
+        del r1, L1, b1, st
+        torch.cuda.synchronize()
+    dist.barrier()
+    return res
 
 
 def tp_comparison(args, runner, layers, steps, bufs, M, world, stream):

@@ -30,6 +30,15 @@ extern "C" {
 int dsv41_version(void);
 int dsv41_arch(void);
 
+/* Tuning switches of the launch sequences, for comparisons and tests (each also read once
+ * from its environment variable): "attn_tc" 1/0 (DSV41_ATTN=mma: 0) the tcgen05 attention core
+ * or the mma.sync one; "attn_pair" 1/0 (DSV41_ATTN_PAIR) a row's two 32-head tiles as one CTA
+ * pair sharing key tiles, or two lone CTAs; "dense_min_m" >= 1 (DSV41_DENSE_MIN_M, 16) the
+ * smallest M whose MXFP8-input projections run on the tcgen05 dense kernel; "pdl" 1/0
+ * (DSV41_PDL) programmatic dependent launch. Takes effect at the next launch; DSV41_EINVAL for
+ * an unknown name or value. No counterpart in the reference (its variants are build keys). */
+int dsv41_set_option(const char* name, int64_t value);
+
 /* ---------------------------------------------------------------- FP8 GEMV
  * y[m][n] = sum_k x[m][k] * dequant(W)[n][k] in fp32: W e4m3 [N, K] row-major with one
  * E8M0 code per 128 x 128 block, x bf16 [M, x_ld]. Rows n use x columns
@@ -48,9 +57,11 @@ int dsv41_gemv_fp8(const Dsv41GemvArgs* a, void* stream);
  * partials go to a library-owned device array of DSV41_NOALLOC_SCRATCH_BYTES (held by every
  * GPU that loads the library until exit) instead of caller scratch; scratch and
  * scratch_bytes are ignored. A shape whose partials exceed the array returns DSV41_ESCRATCH.
- * The first call on a device resolves the array's address there; make it before any stream
- * capture. All calls share the array: calls that overlap on the GPU race. No counterpart in
- * the reference (its launches take caller buffers only). */
+ * The first call in each CUDA context (each device's primary context, a driver-API caller's
+ * own context, a new primary context after cudaDeviceReset) resolves the array's address in
+ * that context, so make the first call in a context before any stream capture in it. All
+ * calls share the array: calls that overlap on the GPU race. No counterpart in the reference
+ * (its launches take caller buffers only). */
 #define DSV41_NOALLOC_SCRATCH_BYTES (4 << 20)
 int dsv41_gemv_fp8_noalloc(const Dsv41GemvArgs* a, void* stream);
 

@@ -40,7 +40,7 @@ def fold_post(res, x, post, comb):
     v = v + c[:, 1, :, None] * res[:, 1:2, :]
     v = v + c[:, 2, :, None] * res[:, 2:3, :]
     # the last term as one fused multiply-add: the exact product plus v, rounded once
-    v = (c[:, 3, :, None].double() * res[:, 3:4, :].double() + v.double()).float()
+    v = N.fma_f32(c[:, 3, :, None], res[:, 3:4, :], v)
     return bf(v)
 
 
@@ -80,9 +80,33 @@ def seam(res, x, post, comb, pre_prev, hc_fn, hc_scale, hc_base, norm_w, *, fold
     for _ in range(SINKHORN - 1):
         cv = cv / (cv.sum(2, keepdim=True) + HC_EPS)
         cv = cv / (cv.sum(1, keepdim=True) + HC_EPS)
-    r = 1.0 / torch.sqrt((lin.double() ** 2).sum(1).float() / float(H) + RMS_EPS)
+    r = 1.0 / torch.sqrt(seam_sumsq(lin).float() / float(H) + RMS_EPS)
     normed = bf((lin * r[:, None]) * f32(norm_w))
     return rn, normed, pre, post_o, cv
+
+
+def seam_sumsq(lin, threads=256):
+    """fp64 sum of squares of the bf16-valued rows of lin [M, H] (H a multiple of 8) in the
+    seam norm's fixed order: thread t of ``threads`` takes the 8 columns at 8 t + 8 threads k
+    for k = 0, 1, ... in column order; each 32-thread warp folds by an xor-butterfly; the warp
+    sums add in warp order from 0. The squares are exact, so only the order is pinned (the
+    reference's norm, ``seam.py:325-378``, sums in its own lane order)."""
+    M, H = lin.shape
+    v = lin.double().numpy() ** 2
+    per = threads * 8
+    acc = np.zeros((M, threads))
+    for k in range(-(-H // per)):
+        chunk = np.zeros((M, per))
+        c0 = k * per
+        chunk[:, : min(per, H - c0)] = v[:, c0:c0 + per]
+        chunk = chunk.reshape(M, threads, 8)
+        for i in range(8):
+            acc = acc + chunk[:, :, i]
+    warps = butterfly32(acc.reshape(M, threads // 32, 32))
+    tot = np.zeros(M)
+    for w in range(threads // 32):
+        tot = tot + warps[:, w]
+    return torch.from_numpy(tot)
 
 
 # ---------------------------------------------------------------- dense GEMVs

@@ -24,6 +24,29 @@ def bf16_round(x: torch.Tensor) -> torch.Tensor:
 
 
 # ---------------------------------------------------------------- E8M0 codes
+def fma_f32(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor) -> torch.Tensor:
+    """fp32 fused multiply-add a * b + c with one rounding (IEEE fmaf, round to nearest even):
+    the product of two fp32 values is exact in fp64; the fp64 sum s and its exact error e
+    (Knuth's TwoSum) give a * b + c = s + e exactly, and rounding s to fp32 is the single
+    rounding of the exact value unless s sits exactly on an fp32 tie, where e's sign decides."""
+    a, b, c = (torch.broadcast_to(t.float(), torch.broadcast_shapes(a.shape, b.shape, c.shape)).double().numpy()
+               for t in (a, b, c))
+    p = a * b
+    s = p + c
+    bp = s - p
+    e = (p - (s - bp)) + (c - bp)
+    f = s.astype(np.float32)
+    lo = np.nextafter(f, np.float32(-np.inf)).astype(np.float64)
+    hi = np.nextafter(f, np.float32(np.inf)).astype(np.float64)
+    fd = f.astype(np.float64)
+    # s on the midpoint between f and a neighbour: the exact value lies on e's side of it
+    go_up = (s == (fd + hi) / 2) & (e > 0)  # s rounded down to f, the exact value is above s
+    go_dn = (s == (fd + lo) / 2) & (e < 0)  # s rounded up to f, the exact value is below s
+    out = np.where(go_up, np.nextafter(f, np.float32(np.inf)), f)
+    out = np.where(go_dn, np.nextafter(f, np.float32(-np.inf)), out)
+    return torch.from_numpy(np.ascontiguousarray(out.astype(np.float32)))
+
+
 def code_ceil(v: torch.Tensor) -> torch.Tensor:
     """Biased exponent of the smallest power of two >= v (v > 0): exponent bits plus one if
     any mantissa bit is set (``mx.py:26-32``, ``check_ffn.py:87-90``). int32."""

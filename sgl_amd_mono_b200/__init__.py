@@ -1,14 +1,16 @@
-"""Monokernels for SGLang on NVIDIA B200 (sm_100a): the DeepSeek-V4.1 decode and
-speculative-verify layer as a few hand-written CUDA launches a layer, including both TP
-all-reduces, behind the reference plugin's surface (omirosh/sgl-amd-mono,
-``sgl_amd_mono/__init__.py``).
+"""A CUDA backend for SGLang's monokernel plugin interface on NVIDIA B200 (sm_100a).
 
-SGLang holds the interface (``sglang.srt.monokernels``). This package holds the CUDA device
-runtime (``common``: the C-ABI loader, peer exchange regions) and, per model, its specs and
-their forwards (``<model>/spec.py``, ``<model>/draft.py``) and its kernels per ISA
-(``<model>/sm100a/``). SGLang loads the package as a general plugin (``pyproject.toml``: the
-``sglang.srt.plugins`` entry point), which registers each spec with SGLang's monokernel
-framework.
+It runs DeepSeek-V4.1's decode and speculative-verify layers through hand-written sm_100a
+kernels, a handful of launches a layer with both tensor-parallel all-reduces done inside the
+kernels over NVLink peer memory, and registers under the backend name ``"cuda"`` through the
+same plugin surface the reference project exposes (omirosh/sgl-amd-mono,
+``sgl_amd_mono/__init__.py``): ``BACKEND``, ``SPECS`` keyed by Hugging Face architecture, and
+``register_specs``, which SGLang calls through the ``sglang.srt.plugins`` entry point declared
+in ``pyproject.toml``.
+
+Layout: ``common/`` holds what every model shares (the ctypes loader of the C-ABI library, the
+peer-memory exchange regions); ``deepseek_v41/`` holds the model's specs, forwards and glue, with
+its kernels, C-ABI and launch runner under ``deepseek_v41/sm100a/``.
 """
 
 __version__ = "0.1.0.dev0"

@@ -68,3 +68,12 @@ def launch_count() -> int:
     f.restype = ctypes.c_int64
     f.argtypes = []
     return int(f())
+
+
+def set_option(name: str, value: int) -> None:
+    """``dsv41_set_option``: a launch-sequence tuning switch ("attn_tc", "attn_pair",
+    "dense_min_m", "pdl"), raising on an unknown name or value."""
+    f = lib().dsv41_set_option
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_char_p, ctypes.c_int64]
+    check(f(name.encode(), int(value)), f"dsv41_set_option({name!r}, {value})")

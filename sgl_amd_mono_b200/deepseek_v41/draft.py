@@ -1,12 +1,13 @@
-"""DeepSeek-V4.1's DSpark draft on sm_100a: its spec and forward (the reference's
-``deepseek_v41/draft.py``, same interface, CUDA kernels).
+"""The DSpark draft of DeepSeek-V4.1 on sm_100a: the draft model's spec and forward, behind the
+interface of the reference's ``deepseek_v41/draft.py``.
 
-SGLang attaches the draft model as it does the target: a routed draft step (a block of rows a
-request, run as a TARGET_VERIFY batch) runs ``_Draft.forward``, which takes and returns what
-``DeepseekV4ForCausalLMDSpark.forward`` does. Each stage is the target's K1 and K2 on the
-draft's route and window, then SGLang's ``hc_post``; the head's combine reads the last stage's
-pre, as SGLang's forward does. The kernels take the draft's widths as launch arguments (its
-expert count and top-k included), so the draft needs no kernels of its own.
+The draft runs as its own routed step: SGLang hands ``_Draft.forward`` a verify-shaped batch
+(each request contributes its block of draft rows) and expects back what
+``DeepseekV4ForCausalLMDSpark.forward`` would return. Here every draft stage is one K1 + K2
+launch pair -- the target's own kernels, given the draft's expert count, top-k and attention
+window as launch-time widths -- followed by SGLang's ``hc_post``; the head then combines the
+last stage's residual copies with that stage's pre, as SGLang does. No kernel is specific to
+the draft.
 """
 
 from __future__ import annotations

@@ -2,9 +2,10 @@
 
 The reference (omirosh/sgl-amd-mono, ``deepseek_v41/__init__.py:12-39``) builds for
 DeepSeek-V4.1-Flash; the benchmark configs use other widths, so every width is a field.
-Config bindings for what BASELINE.json leaves open (q_lora rank, wo_a groups, the 64 RoPE
-dims, FP8 shared expert, power-of-two 128 x 128 dense scales) follow the shape binding of
-the build's survey and are recorded in DESIGN.md.
+The widths the benchmark configs leave open are chosen here: q_lora 1024 (hidden / 4, as the
+reference model), wo_a in 8 groups of 1024, 64 bf16 RoPE dims beside the 512 FP8 latent dims of
+a KV record, an FP8 shared expert, and power-of-two (E8M0) scales per 128 x 128 block of the
+dense FP8 weights.
 """
 
 from __future__ import annotations

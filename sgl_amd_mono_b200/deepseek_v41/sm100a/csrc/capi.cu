@@ -19,6 +19,7 @@
 #include "epilogue.cuh"
 #include "front.cuh"
 #include "gemv.cuh"
+#include "gemv_entry.cuh"
 #include "k2i.cuh"
 #include "lmhead.cuh"
 #include "moe.cuh"
@@ -58,46 +59,50 @@ int sm_count() {
   return cached[dev];
 }
 
-// The attention core: tcgen05 (default) or the mma.sync split kernel (DSV41_ATTN=mma).
-bool use_tc_attention() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("DSV41_ATTN");
-    v = (e && e[0] == 'm') ? 0 : 1;
+// Tuning switches: read once from the environment, overridable through dsv41_set_option.
+struct Option {
+  const char* name;  // dsv41_set_option's name
+  const char* env;
+  int64_t dflt;
+  std::atomic<int64_t> value;
+  std::atomic<bool> set;
+};
+// The attention core: tcgen05 (1, default) or the mma.sync split kernel (0; DSV41_ATTN=mma).
+// A row's two 32-head tiles as one CTA pair sharing key tiles (1, default), or two lone CTAs that
+// each gather every key (0; DSV41_ATTN_PAIR=0), for comparison.
+// The smallest M whose MXFP8-input GEMVs run on the tcgen05 dense kernel (DSV41_DENSE_MIN_M, 16).
+// Programmatic dependent launch between the layer's kernels (DSV41_PDL=0 turns it off).
+Option g_options[] = {
+    {"attn_tc", "DSV41_ATTN", 1, {0}, {false}},
+    {"attn_pair", "DSV41_ATTN_PAIR", 1, {0}, {false}},
+    {"dense_min_m", "DSV41_DENSE_MIN_M", 16, {0}, {false}},
+    {"pdl", "DSV41_PDL", 1, {0}, {false}},
+};
+enum { kOptAttnTc, kOptAttnPair, kOptDenseMinM, kOptPdl };
+
+int64_t option(int i) {
+  Option& o = g_options[i];
+  if (!o.set.load(std::memory_order_acquire)) {
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!o.set.load(std::memory_order_relaxed)) {
+      int64_t v = o.dflt;
+      if (const char* e = getenv(o.env)) {
+        if (i == kOptAttnTc) v = e[0] == 'm' ? 0 : 1;
+        else if (i == kOptDenseMinM) v = std::max(1, atoi(e));
+        else v = e[0] == '0' ? 0 : 1;
+      }
+      o.value.store(v, std::memory_order_relaxed);
+      o.set.store(true, std::memory_order_release);
+    }
   }
-  return v == 1;
+  return o.value.load(std::memory_order_relaxed);
 }
 
-// A row's two 32-head tiles as one CTA pair sharing key tiles (default), or two lone CTAs that
-// each gather every key (DSV41_ATTN_PAIR=0), for comparison.
-bool use_attn_pair() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("DSV41_ATTN_PAIR");
-    v = (e && e[0] == '0') ? 0 : 1;
-  }
-  return v == 1;
-}
-
-// The smallest M whose MXFP8-input GEMVs run on the tcgen05 dense kernel (DSV41_DENSE_MIN_M,
-// default 16).
-int dense_min_rows() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("DSV41_DENSE_MIN_M");
-    v = e ? std::max(1, atoi(e)) : 16;
-  }
-  return v;
-}
-
-bool use_pdl() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("DSV41_PDL");
-    v = (e && e[0] == '0') ? 0 : 1;
-  }
-  return v == 1;
-}
+bool use_tc_attention() { return option(kOptAttnTc) == 1; }
+bool use_attn_pair() { return option(kOptAttnPair) == 1; }
+int dense_min_rows() { return (int)option(kOptDenseMinM); }
+bool use_pdl() { return option(kOptPdl) == 1; }
 
 int launch_status() {
   cudaError_t e = cudaGetLastError();
@@ -261,18 +266,6 @@ cudaError_t dense_go(const GemvArgs& g, const uint8_t* x8, const uint8_t* xs, cu
                  DnSmem::kBytes, st, m, d);
 }
 
-// y[m][n] = sum over K slices of partials p[ks][m][n], in slice order.
-__global__ void sum_slices_kernel(const float* __restrict__ p, float* __restrict__ y, int slices,
-                                  int total) {
-  pdl_wait();
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
-    float v = p[i];
-    for (int s = 1; s < slices; ++s) v += p[(size_t)s * total + i];
-    y[i] = v;
-  }
-  pdl_launch();
-}
-
 // Bump allocation over the caller's scratch; with a null base it only measures.
 struct Carver {
   uint8_t* base;
@@ -302,20 +295,6 @@ int grid_for(int64_t work, int per_block) {
   do {                                        \
     if ((expr) != cudaSuccess) return launch_status(); \
   } while (0)
-
-// ------------------------------------------------------------------ GEMV entry
-GemvArgs plan_of(const Dsv41GemvArgs* a, float* out) {
-  return gemv_plan(ptr<const uint8_t>(a->w), ptr<const uint8_t>(a->codes),
-                   ptr<const __nv_bfloat16>(a->x), out, (int)a->M, (int)a->N, (int)a->K,
-                   (int)a->x_ld, (int)a->x_group_rows, sm_count());
-}
-
-bool gemv_args_ok(const Dsv41GemvArgs* a) {
-  return a && a->w && a->codes && a->x && a->y && a->M >= 1 && a->M <= 48 && a->N >= 1 &&
-         a->K >= 128 && a->K % 128 == 0 && a->x_ld >= a->K && a->x_ld % 4 == 0 &&
-         (a->x_group_rows == 0 || (a->x_group_rows % 16 == 0 && a->N % a->x_group_rows == 0)) &&
-         a->w % 16 == 0 && a->x % 8 == 0;
-}
 
 // ------------------------------------------------------------------ K1
 bool k1_ok(const Dsv41K1Args* a) {
@@ -694,28 +673,34 @@ int dsv41_device_error(void) {
 }
 
 int dsv41_version(void) { return 1; }
+
+int dsv41_set_option(const char* name, int64_t value) {
+  if (!name) return DSV41_EINVAL;
+  for (int i = 0; i < (int)(sizeof(g_options) / sizeof(g_options[0])); ++i) {
+    Option& o = g_options[i];
+    if (strcmp(name, o.name) != 0) continue;
+    if (i == kOptDenseMinM ? value < 1 : (value != 0 && value != 1)) return DSV41_EINVAL;
+    o.value.store(value, std::memory_order_relaxed);
+    o.set.store(true, std::memory_order_release);
+    return DSV41_OK;
+  }
+  return DSV41_EINVAL;
+}
 int dsv41_arch(void) { return 100; }
 
 int64_t dsv41_gemv_fp8_scratch_bytes(const Dsv41GemvArgs* a) {
-  if (!gemv_args_ok(a)) return DSV41_EINVAL;
-  GemvArgs g = plan_of(a, nullptr);
-  return g.kslices > 1 ? (int64_t)g.kslices * a->M * a->N * 4 : 0;
+  if (!gemv_entry_args_ok(a)) return DSV41_EINVAL;
+  return gemv_entry_partials_bytes(gemv_entry_plan(a, sm_count()));
 }
 
 int dsv41_gemv_fp8(const Dsv41GemvArgs* a, void* stream) {
-  if (!gemv_args_ok(a)) return DSV41_EINVAL;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  GemvArgs g = plan_of(a, ptr<float>(a->y));
-  if (g.kslices > 1) {
-    const int64_t need = (int64_t)g.kslices * a->M * a->N * 4;
-    if (!a->scratch || a->scratch_bytes < need) return DSV41_ESCRATCH;
-    g.out = ptr<float>(a->scratch);
-  }
-  if (gemv_launch(g, st, false) != cudaSuccess) return launch_status();
-  if (g.kslices > 1) {
-    const int total = (int)(a->M * a->N);
-    sum_slices_kernel<<<grid_for(total, 256), 256, 0, st>>>(g.out, ptr<float>(a->y), g.kslices, total);
-  }
+  if (!gemv_entry_args_ok(a)) return DSV41_EINVAL;
+  const GemvArgs g = gemv_entry_plan(a, sm_count());
+  const int64_t need = gemv_entry_partials_bytes(g);
+  if (need > 0 && (!a->scratch || a->scratch_bytes < need)) return DSV41_ESCRATCH;
+  if (gemv_entry_launch(g, ptr<float>(a->y), ptr<float>(a->scratch), reinterpret_cast<cudaStream_t>(stream)) !=
+      cudaSuccess)
+    return launch_status();
   return launch_status();
 }
 

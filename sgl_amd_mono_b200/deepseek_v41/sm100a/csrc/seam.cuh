@@ -154,7 +154,7 @@ __device__ __forceinline__ void mx_group_store(const float (&v)[8], bool vllm, u
 }
 
 __global__ void __launch_bounds__(256) seam_gate_norm_kernel(const SeamArgs a) {
-  __shared__ float red[8];
+  __shared__ double red[8];
   __shared__ float tot_s;
   __shared__ float gsum[8][kPart];
   const int t = blockIdx.x, H = a.H, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -217,25 +217,28 @@ __global__ void __launch_bounds__(256) seam_gate_norm_kernel(const SeamArgs a) {
     }
     if (lane < 16) a.comb_out[t * 16 + lane] = cv;
   }
-  // ---- norm: 8 consecutive columns a thread
-  float ss = 0.f;
+  // ---- norm: 8 consecutive columns a thread. The sum of squares is fp64 (each bf16 square
+  // exact) in a fixed order -- a thread's columns in order, an xor-butterfly in each warp, the
+  // warps in order -- and rounded once to fp32, so the scale and the normed row are bit-exact
+  // (the oracle's seam_sumsq follows the same order).
+  double ss = 0.0;
   for (int c = tid * 8; c < H; c += blockDim.x * 8) {
     const uint4 w = *reinterpret_cast<const uint4*>(a.lin + (size_t)t * H + c);
     const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float lo = __uint_as_float(ws[i] << 16), hi = __uint_as_float(ws[i] & 0xffff0000u);
-      ss = fmaf(lo, lo, ss);
-      ss = fmaf(hi, hi, ss);
+      const double lo = __uint_as_float(ws[i] << 16), hi = __uint_as_float(ws[i] & 0xffff0000u);
+      ss = __dadd_rn(ss, __dmul_rn(lo, lo));
+      ss = __dadd_rn(ss, __dmul_rn(hi, hi));
     }
   }
-  ss = warp_sum(ss);
+  ss = warp_sum_d(ss);
   if ((tid & 31) == 0) red[tid >> 5] = ss;
   __syncthreads();
   if (tid == 0) {
-    float s = 0.f;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += red[w];
-    tot_s = s;
+    double s = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s = __dadd_rn(s, red[w]);
+    tot_s = (float)s;
   }
   __syncthreads();
   const float r = 1.0f / sqrtf(tot_s / (float)H + kRmsEps);

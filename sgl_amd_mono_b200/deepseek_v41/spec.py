@@ -40,7 +40,7 @@ from . import CANDIDATES, ENVELOPE, HF_CONFIG
 
 MAX_ROWS = 48  # the rows a launch takes at most
 ISA = "sm_100a"
-RESIDENT_BLOCKS = 2 * 148  # the persistent kernels' CTAs: two an SM
+RESIDENT_BLOCKS = 2 * 148  # DeviceLimits.resident_blocks: CTAs a launch keeps resident (two an SM)
 
 _SHARED = ("gate_proj", "up_proj", "down_proj")
 # the checkpoint's shared expert tensors, as the model loader names them
