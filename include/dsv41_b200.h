@@ -35,7 +35,9 @@ int dsv41_arch(void);
  * or the mma.sync one; "attn_pair" 1/0 (DSV41_ATTN_PAIR) a row's two 32-head tiles as one CTA
  * pair sharing key tiles, or two lone CTAs; "dense_min_m" >= 1 (DSV41_DENSE_MIN_M, 16) the
  * smallest M whose MXFP8-input projections run on the tcgen05 dense kernel; "pdl" 1/0
- * (DSV41_PDL) programmatic dependent launch. Takes effect at the next launch; DSV41_EINVAL for
+ * (DSV41_PDL) programmatic dependent launch; "attn_bulk" 0/1 (DSV41_ATTN_BULK) the tcgen05
+ * attention's producer gathering each key tile's records into registers (default; "attn_pair"
+ * then chooses pair or lone CTAs), or staging them in shared memory by bulk copies (lone CTAs). Takes effect at the next launch; DSV41_EINVAL for
  * an unknown name or value. No counterpart in the reference (its variants are build keys). */
 int dsv41_set_option(const char* name, int64_t value);
 

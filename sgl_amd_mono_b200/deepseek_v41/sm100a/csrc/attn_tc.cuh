@@ -91,24 +91,32 @@ struct AttnTcArgs {
   int head_tiles;
 };
 
-template <int D>
+// Shared memory of a CTA: TS f16 key tiles, Q, P, the softmax's reductions, the key metadata and
+// (the staged producer, STG > 0) STG staging stages of raw FP8 records.
+template <int D, int TS = kTcStages, int STG = 0>
 struct TcSmem {
   static constexpr int kTileBytes = kTcKeys * D * 2;
   static constexpr int kQBytes = 32 * D * 2;
   static constexpr int kPBytes = kTcKeys * 32 * 2;
-  static constexpr int kTile0 = 0;                      // kTcStages tiles
-  static constexpr int kQ = kTcStages * kTileBytes;     // (the QK's padded rows of the last tile read Q)
+  static constexpr int kRecBytes = D - 64 + 128;       // a record's data row (nope e4m3, rope bf16)
+  static constexpr int kStageBytes = kTcKeys * kRecBytes;
+  static constexpr int kTile0 = 0;                      // TS tiles
+  static constexpr int kQ = TS * kTileBytes;            // (the QK's padded rows of the last tile read Q)
   static constexpr int kP = kQ + kQBytes;
   static constexpr int kRed = kP + 4 * kPBytes;      // float [4 warps][64 heads]
   static constexpr int kM = kRed + 4 * 64 * 4;       // float [64]: the used max of each head
   static constexpr int kAlpha = kM + 64 * 4;         // float [64]: the rescale of the reference max
   static constexpr int kMetaStages = 3;
   static constexpr int kMeta = kAlpha + 64 * 4;      // [3 stages][64 keys]: record pointer, then 8 codes
-  static constexpr int kBar = kMeta + kMetaStages * 64 * 16;  // uint64 mbarriers
-  static constexpr int kNumBars = 2 * kTcStages + 9;
-  static constexpr int kMisc = kBar + kNumBars * 8;  // tmem base, abort flag
-  static constexpr int kBytes = kMisc + 16 + 1024;  // + slack to align the base to 1 KB
+  static constexpr int kStage = kMeta + kMetaStages * 64 * 16;  // STG staging stages (16-byte aligned)
+  static constexpr int kBar = kStage + STG * kStageBytes;       // uint64 mbarriers
+  static constexpr int kNumBars = 2 * TS + 9 + 2 * STG;
+  static constexpr int kMisc = kBar + kNumBars * 8;  // tmem base, abort flag, then [STG] live-key masks
+  static constexpr int kBytes = kMisc + 32 + 1024;  // + slack to align the base to 1 KB
+  static_assert(kStage % 16 == 0 && kStageBytes % 16 == 0, "bulk copy destinations are 16-byte aligned");
 };
+constexpr int kTcBulkStages = 2;  // the staged producer: f16 tiles in flight
+constexpr int kTcStaging = 2;     // and FP8 record staging stages
 
 __device__ __forceinline__ uint64_t umma_sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
   return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
@@ -268,6 +276,17 @@ __device__ __forceinline__ bool softmax_any(bool v) {
   return r != 0;
 }
 __device__ __forceinline__ void softmax_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// One arrival on a CTA-local mbarrier that also raises its expected transaction bytes.
+__device__ __forceinline__ void tc_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+// bytes of global memory into this CTA's shared memory, counted on its mbarrier bar as they land
+// (a plain bulk copy, no multicast; addresses and size multiples of 16 bytes)
+__device__ __forceinline__ void tc_bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
 // The maximum of v over the warp's 32 lanes, in every lane (one instruction on sm_100a).
 __device__ __forceinline__ float warp_max_f32(float v) {
   float r;
@@ -318,13 +337,23 @@ __device__ __forceinline__ uint32_t cvt_f16x2(float lo, float hi) {
 // CTA rank r) into its own tile, then one thread copies that half into the peer's; a tile is full
 // after this CTA's 7 producer warps and the peer's copy (an arrival raising the expected bytes,
 // then the bytes) arrived, and free after both CTAs' PV finished with it (2 commit arrivals).
-template <int NOPE, bool PAIR>
+//
+// BULK (lone CTAs): the producer stages each tile's raw records in shared memory first. One warp
+// reads the tile's key-table entries, finds the runs of consecutive slots of one page (a row's
+// window keys are whole runs), and fetches each run with one cp.async.bulk into a staging stage
+// (kTcStaging stages, counted on the stage's mbarrier); six warps convert the staged FP8 records
+// into the f16 tile (kTcBulkStages tiles) with the same arithmetic as the gathering producers, so
+// all three producers give the MMAs the same tiles and the outputs the same bits.
+template <int NOPE, bool PAIR, bool BULK = false>
 __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs A) {
+  static_assert(!(PAIR && BULK), "the staged producer runs lone CTAs");
   constexpr int D = NOPE + 64;
   constexpr int DG = D / 8;                 // 16-byte core columns a row
   constexpr int NBLK = (D + 127) / 128;     // 128-dim PV blocks
   constexpr int CHUNKS = (NOPE + 128) / 16; // 16-byte chunks of a record's data
-  using L = TcSmem<D>;
+  constexpr int TS = BULK ? kTcBulkStages : kTcStages;  // f16 key tiles in flight
+  constexpr int STG = BULK ? kTcStaging : 0;            // raw record staging stages
+  using L = TcSmem<D, TS, STG>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);  // swizzle atoms: 1 KB
   const AttnArgs& a = A.a;
@@ -335,17 +364,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
   const int h0 = 32 * ht;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
-  // bars: 0,1 tile full; 2,3 tile free; 4,5 S ready; 6,7 S consumed; 8,9 P ready; 10,11 PV
-  // done; 12 MMA drain (pairs by the sub-block's parity)
+  // bars: TS tile full; TS tile free; 2 S ready; 2 S consumed; 2 P ready; 2 PV done; 1 MMA
+  // drain; STG staging full; STG staging empty (S and P pairs by the sub-block's parity)
   auto bar = [&](int i) { return smem_u32(bars + i); };
-  // tile stage ts = j % 3 (parity (j / 3) & 1); S and P buffers s = j & 1 (parity (j >> 1) & 1)
+  // tile stage ts = j % TS (parity (j / TS) & 1); S and P buffers s = j & 1 (parity (j >> 1) & 1)
   auto b_full = [&](int ts) { return bar(ts); };                     // producers -> MMA
-  auto b_free = [&](int ts) { return bar(kTcStages + ts); };         // PV done with the tile
-  auto b_sready = [&](int sb) { return bar(2 * kTcStages + sb); };   // QK -> softmax
-  auto b_scons = [&](int sb) { return bar(2 * kTcStages + 2 + sb); }; // softmax holds S
-  auto b_pready = [&](int sb) { return bar(2 * kTcStages + 4 + sb); }; // softmax -> PV
-  auto b_pvdone = [&](int sb) { return bar(2 * kTcStages + 6 + sb); }; // PV(j) complete
-  const uint32_t b_drain = bar(2 * kTcStages + 8);
+  auto b_free = [&](int ts) { return bar(TS + ts); };                // PV done with the tile
+  auto b_sready = [&](int sb) { return bar(2 * TS + sb); };          // QK -> softmax
+  auto b_scons = [&](int sb) { return bar(2 * TS + 2 + sb); };       // softmax holds S
+  auto b_pready = [&](int sb) { return bar(2 * TS + 4 + sb); };      // softmax -> PV
+  auto b_pvdone = [&](int sb) { return bar(2 * TS + 6 + sb); };      // PV(j) complete
+  const uint32_t b_drain = bar(2 * TS + 8);
+  auto b_sfull = [&](int st) { return bar(2 * TS + 9 + st); };       // staging: records landed
+  auto b_sempty = [&](int st) { return bar(2 * TS + 9 + STG + st); };  // staging: converted
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
   uint32_t* tmem_base = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   float* red = reinterpret_cast<float*>(smem + L::kRed);
@@ -372,9 +403,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
     *reinterpret_cast<uint4*>(smem + L::kQ + sw_off<32>(h, 8 * c)) = v;
   }
   if (tid == 0) {
-    for (int ts = 0; ts < kTcStages; ++ts) {
-      mbar_init(b_full(ts), PAIR ? 8 : 7);  // the producer warps (+ the peer's copy of its half)
+    for (int ts = 0; ts < TS; ++ts) {
+      // the producer warps (+ the peer's copy of its half; the staged producer's 6 converters)
+      mbar_init(b_full(ts), BULK ? 6 : PAIR ? 8 : 7);
       mbar_init(b_free(ts), PAIR ? 2 : 1);
+    }
+    for (int st = 0; st < STG; ++st) {
+      mbar_init(b_sfull(st), 1);   // the copy warp's arrival with the stage's bytes
+      mbar_init(b_sempty(st), 6);  // the converters
     }
     for (int sb = 0; sb < 2; ++sb) {
       mbar_init(b_sready(sb), 1);
@@ -408,7 +444,177 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
   // (2 NH: the head pass's columns, then the tail pass's)
   const uint32_t tm_s = tmem, tm_o = tmem + 64;
 
-  if (warp >= 5) {
+  if (BULK && warp == 11) {
+    // ================= staged producer: the record copies (one warp; lane l: keys l and 32 + l)
+    // Per tile j: tile j + 1's records located (their scale-code words loaded), tile j + 2's
+    // key-table entries loaded, then -- once stage j % STG is converted -- tile j's metadata
+    // published and its runs fetched: a key starts a run unless it continues the previous key's
+    // record (the next slot of the same page); a run's start lane copies the whole run.
+    uint64_t* meta_c = reinterpret_cast<uint64_t*>(smem + L::kMeta + L::kMetaStages * 64 * 8);  // [stage][64]
+    constexpr int RB = L::kRecBytes;
+    const bool has_b = lane < kTcKeys - 32;
+    uint64_t* live_mask = reinterpret_cast<uint64_t*>(smem + L::kMisc + 8);  // [STG] keys with a record
+    auto kt_load = [&](int j, int i) {
+      const int k = k0 + j * kTcKeys + i;
+      return (i < kTcKeys && k < k1) ? a.kt[(size_t)t * a.keys_ld + k] : -1;
+    };
+    auto locate = [&](int v, const uint8_t*& p, uint64_t& c) {
+      p = nullptr;
+      c = 0;
+      const bool comp = v < 0 && v != -1 && a.comp != nullptr;
+      if (v >= 0 || comp) {
+        const int sl = v & 0x7fffffff;
+        const int blk = comp ? a.comp_blk : a.swa_blk;
+        const uint8_t* page = (comp ? a.comp : a.swa) + (int64_t)(sl / blk) * (comp ? a.comp_stride : a.swa_stride);
+        const int off = sl % blk;
+        p = page + (size_t)off * RB;
+        c = *reinterpret_cast<const uint64_t*>(page + (size_t)blk * RB + (size_t)off * 8);
+      }
+    };
+    const uint8_t *pa = nullptr, *pb = nullptr;
+    uint64_t ca = 0, cb = 0;
+    int va = -1, vb = -1;
+    if (nsub > 0) {
+      locate(kt_load(0, lane), pa, ca);
+      locate(kt_load(0, 32 + lane), pb, cb);
+      va = kt_load(1, lane);
+      vb = kt_load(1, 32 + lane);
+    }
+    int issued = 0;  // tiles whose copies went out
+    for (int j = 0; j < nsub; ++j) {
+      const int st = j % STG;
+      const uint8_t *na = nullptr, *nb = nullptr;
+      uint64_t nca = 0, ncb = 0;
+      if (j + 1 < nsub) {
+        locate(va, na, nca);
+        locate(vb, nb, ncb);
+        va = kt_load(j + 2, lane);
+        vb = kt_load(j + 2, 32 + lane);
+      }
+      if (j >= STG && !__all_sync(0xffffffffu, mbar_wait(b_sempty(st), ((j / STG) - 1) & 1, abort))) break;
+      if (lane == 0) TC_TRACE(j, 14);
+      meta_c[st * 64 + lane] = ca;
+      if (has_b) meta_c[st * 64 + 32 + lane] = cb;
+      // runs: key i breaks a run when it is masked or does not continue key i - 1's record
+      const uint8_t* prev_a = reinterpret_cast<const uint8_t*>(
+          __shfl_up_sync(0xffffffffu, reinterpret_cast<unsigned long long>(pa), 1));
+      const uint8_t* last_a = reinterpret_cast<const uint8_t*>(
+          __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(pa), 31));
+      const uint8_t* prev_b = reinterpret_cast<const uint8_t*>(
+          __shfl_up_sync(0xffffffffu, reinterpret_cast<unsigned long long>(pb), 1));
+      if (lane == 0) {
+        prev_a = nullptr;
+        prev_b = last_a;
+      }
+      const bool start_a = pa != nullptr && !(prev_a != nullptr && pa == prev_a + RB);
+      const bool start_b = has_b && pb != nullptr && !(prev_b != nullptr && pb == prev_b + RB);
+      const uint32_t brk_a = __ballot_sync(0xffffffffu, start_a || pa == nullptr);
+      const uint32_t brk_b = __ballot_sync(0xffffffffu, !has_b || start_b || pb == nullptr);
+      const uint64_t brk = (uint64_t)brk_a | ((uint64_t)brk_b << 32);  // bits kTcKeys .. 63 set
+      const uint32_t va_mask = __ballot_sync(0xffffffffu, pa != nullptr);
+      const uint32_t vb_mask = __ballot_sync(0xffffffffu, has_b && pb != nullptr);
+      const uint32_t nvalid = __popc(va_mask) + __popc(vb_mask);
+      if (lane == 0) live_mask[st] = (uint64_t)va_mask | ((uint64_t)vb_mask << 32);
+      __syncwarp();
+      if (lane == 0) tc_expect_tx(b_sfull(st), nvalid * (uint32_t)RB);  // (arrives: 0 bytes completes)
+      __syncwarp();
+      const uint32_t stage = smem_u32(smem + L::kStage + st * L::kStageBytes);
+      auto run_copy = [&](int i, const uint8_t* p) {
+        const uint64_t above = brk & ~((2ull << i) - 1);
+        const int len = __ffsll((long long)above) - 1 - i;
+        tc_bulk_load(stage + (uint32_t)(i * RB), p, (uint32_t)(len * RB), b_sfull(st));
+      };
+      if (start_a) run_copy(lane, pa);
+      if (start_b) run_copy(32 + lane, pb);
+      if (lane == 0) TC_TRACE(j, 15);
+      issued = j + 1;
+      pa = na;
+      pb = nb;
+      ca = nca;
+      cb = ncb;
+    }
+    // no copy may still be landing when the CTA leaves (after an abort the converters stopped
+    // consuming): wait, bounded, for the last issued phase of each stage
+    for (int st = 0; st < STG; ++st) {
+      const int last = issued - 1 - ((issued - 1 - st) % STG + STG) % STG;  // largest tile < issued in stage st
+      if (last < 0) continue;
+      for (uint32_t it = 0; it < kTcWaitPolls && !mbar_try(b_sfull(st), (last / STG) & 1); ++it) {
+      }
+    }
+  } else if (BULK && warp >= 5) {
+    // ================= staged producer: conversion (warps 5-10) of the staged records into the
+    // f16 tile, the gathering producers' arithmetic; item e = (key e / CHUNKS, chunk e % CHUNKS),
+    // consecutive threads on consecutive 16-byte chunks of a record
+    const uint64_t* meta_c = reinterpret_cast<const uint64_t*>(smem + L::kMeta + L::kMetaStages * 64 * 8);
+    const uint64_t* live_mask = reinterpret_cast<const uint64_t*>(smem + L::kMisc + 8);
+    // warp w converts keys 8 w .. 8 w + 7: item i of a lane = flat index lane + 32 i of the warp's
+    // 8 x CHUNKS chunks (key f / CHUNKS, chunk f % CHUNKS); all of a lane's loads go out first
+    constexpr int kItemsB = 8 * CHUNKS / 32;
+    static_assert(8 * CHUNKS % 32 == 0 && 6 * 8 == kTcKeys, "six warps of 8 keys, whole items");
+    const int kbase = 8 * (warp - 5);
+    for (int j = 0; j < nsub; ++j) {
+      const int st = j % STG, ts = j % TS;
+      if (!mbar_wait(b_sfull(st), (j / STG) & 1, abort)) break;
+      if (tid == 160) TC_TRACE(j, 4);
+      if (j >= TS && !mbar_wait(b_free(ts), ((j / TS) - 1) & 1, abort)) break;
+      if (tid == 160) TC_TRACE(j, 0);
+      const uint8_t* stage = smem + L::kStage + st * L::kStageBytes;
+      uint8_t* tile = smem + L::kTile0 + ts * L::kTileBytes;
+      const uint64_t live = live_mask[st];
+      uint4 raw[kItemsB];
+#pragma unroll
+      for (int i = 0; i < kItemsB; ++i) {
+        const int f = lane + 32 * i, key = kbase + f / CHUNKS, c = f % CHUNKS;
+        raw[i] = ((live >> key) & 1) ? *reinterpret_cast<const uint4*>(stage + key * L::kRecBytes + 16 * c)
+                                     : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int i = 0; i < kItemsB; ++i) {
+        const int f = lane + 32 * i, key = kbase + f / CHUNKS, c = f % CHUNKS;
+        const int b0 = 16 * c;
+        const bool is_live = (live >> key) & 1;
+        if (b0 < NOPE) {
+          uint4 o0 = make_uint4(0, 0, 0, 0), o1 = o0;
+          if (is_live) {
+            const int cd = (int)((meta_c[st * 64 + key] >> (8 * (b0 / 64))) & 0xff);
+            const uint32_t w[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+            uint32_t r[8];
+            if (e4m3_f16_scale_ok(cd)) {
+              const uint32_t s2 = e4m3_f16_scale(cd);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) e4m3x4_f16x2_scaled(w[q], s2, r[2 * q], r[2 * q + 1]);
+            } else {
+              const float sc = pow2c(cd);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float2 fl = e4m3x2_float2(w[q] & 0xffff), fh = e4m3x2_float2(w[q] >> 16);
+                r[2 * q] = pack_f16x2(fl.x * sc, fl.y * sc);
+                r[2 * q + 1] = pack_f16x2(fh.x * sc, fh.y * sc);
+              }
+            }
+            o0 = make_uint4(r[0], r[1], r[2], r[3]);
+            o1 = make_uint4(r[4], r[5], r[6], r[7]);
+          }
+          *reinterpret_cast<uint4*>(tile + sw_off<kTcKeys>(key, b0)) = o0;
+          *reinterpret_cast<uint4*>(tile + sw_off<kTcKeys>(key, b0 + 8)) = o1;
+        } else {
+          uint4 o0 = make_uint4(0, 0, 0, 0);
+          if (is_live)
+            o0 = make_uint4(bf16x2_to_f16x2(raw[i].x), bf16x2_to_f16x2(raw[i].y), bf16x2_to_f16x2(raw[i].z),
+                            bf16x2_to_f16x2(raw[i].w));
+          *reinterpret_cast<uint4*>(tile + sw_off<kTcKeys>(key, NOPE + (b0 - NOPE) / 2)) = o0;
+        }
+      }
+      fence_async_smem();  // the MMA (async proxy) reads the tile
+      __syncwarp();
+      if (tid == 160) TC_TRACE(j, 1);
+      if (lane == 0) {
+        mbar_arrive(b_full(ts));
+        mbar_arrive(b_sempty(st));
+      }
+    }
+  } else if (warp >= 5) {
+    if constexpr (!BULK) {
     // ================= producers
     // Per tile: the metadata threads publish their key (record pointer, the 8 scale codes;
     // null = masked) into shared memory; then each conversion warp converts units of 8 keys x 4
@@ -486,7 +692,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
       }
     };
     auto convert = [&](int j, const uint4 (&raw)[kItems]) {
-      const int ts = j % kTcStages, ms = j % kStages;
+      const int ts = j % TS, ms = j % kStages;
       const int tile_off = L::kTile0 + ts * L::kTileBytes;
       // into this CTA's tile (a pair's half then goes to the peer by one bulk copy, below)
       auto put = [&](int off, const uint4& v) { *reinterpret_cast<uint4*>(smem + tile_off + off) = v; };
@@ -502,14 +708,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
             const int cd = (int)((meta_c[ms * 64 + key] >> (8 * (b0 / 64))) & 0xff);
             const uint32_t w[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
             uint32_t r[8];
-            if (cd >= 113 && cd <= 134) {
-              const uint32_t s1 = (uint32_t)(cd - 112) << 10;
-              const uint32_t s2 = s1 | (s1 << 16);
+            if (e4m3_f16_scale_ok(cd)) {
+              const uint32_t s2 = e4m3_f16_scale(cd);
 #pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                r[2 * q] = hmul2_bits(e4m3x2_f16(w[q] & 0xffff), s2);
-                r[2 * q + 1] = hmul2_bits(e4m3x2_f16(w[q] >> 16), s2);
-              }
+              for (int q = 0; q < 4; ++q) e4m3x4_f16x2_scaled(w[q], s2, r[2 * q], r[2 * q + 1]);
             } else {
               const float sc = pow2c(cd);
 #pragma unroll
@@ -556,10 +758,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
     // one tile: once its stage is free, convert it (a pair first: its chunks were loaded two
     // tiles ago), publish and issue tile j + kAhead's loads into nxt, locate tile j + kAhead + 1
     auto step = [&](int j, const uint4 (&cur)[kItems], uint4 (&nxt)[kItems]) {
-      const int ts = j % kTcStages, fpar = ((j / kTcStages) - 1) & 1;
+      const int ts = j % TS, fpar = ((j / TS) - 1) & 1;
       // the stage is free (PV(j - 3) done), for every producer alike; and every producer is past
       // tile j - 1's conversion (its metadata stage is rewritten next)
-      if (!producers_all(j < kTcStages || (PAIR ? mbar_wait_cl(b_free(ts), fpar, abort)
+      if (!producers_all(j < TS || (PAIR ? mbar_wait_cl(b_free(ts), fpar, abort)
                                                 : mbar_wait(b_free(ts), fpar, abort))))
         return false;
       if (ptid == 0) TC_TRACE(j, 0);
@@ -629,6 +831,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
         if (j + 1 < nsub && !step(j + 1, buf1, buf0)) break;
       }
     }
+    }  // !BULK
   } else if (warp == 4) {
     // ================= MMA issue (one elected thread)
     // QK(j) needs tile j and S[j & 1] consumed by softmax(j - 2); PV(j) needs P(j) (written
@@ -638,7 +841,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
       const uint32_t id_qk = umma_idesc(64, NH, 0, 0);
       const uint32_t id_pv = umma_idesc(128, 2 * NH, 1, 1);
       auto issue_qk = [&](int j) {
-        const uint32_t tile = s_tile0 + (j % kTcStages) * L::kTileBytes;
+        const uint32_t tile = s_tile0 + (j % TS) * L::kTileBytes;
         const uint32_t dst = tm_s + 32 * (j & 1);
         // K-major, 128-byte swizzle: K step ks = 16 dims, byte 32 (ks % 4) of chunk ks / 4's rows
         // (tile chunks (kTcKeys / 8) KB apart, Q's 4 KB); 8-row groups 1 KB apart
@@ -650,12 +853,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
         TC_TRACE(j, 11);
       };
       auto qk_ready = [&](int j) {  // tile j loaded and S[j & 1] consumed by softmax(j - 2)
-        const int ts = j % kTcStages, tpar = (j / kTcStages) & 1;
+        const int ts = j % TS, tpar = (j / TS) & 1;
         return (PAIR ? mbar_test_cl(b_full(ts), tpar) : mbar_test(b_full(ts), tpar)) &&
                (j < 2 || mbar_test(b_scons(j & 1), ((j - 2) >> 1) & 1));
       };
       auto wait_qk = [&](int j) {
-        const int ts = j % kTcStages, tpar = (j / kTcStages) & 1;
+        const int ts = j % TS, tpar = (j / TS) & 1;
         return (PAIR ? mbar_wait_cl(b_full(ts), tpar, abort) : mbar_wait(b_full(ts), tpar, abort)) &&
                (j < 2 || mbar_wait(b_scons(j & 1), ((j - 2) >> 1) & 1, abort));
       };
@@ -686,7 +889,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
         TC_TRACE(j, 3);
         tc_fence_after();
         // PV: O += V^T P^T, P^T's columns the f16 head of p (0 .. NH - 1), then its tail
-        const uint32_t tile = s_tile0 + (j % kTcStages) * L::kTileBytes;
+        const uint32_t tile = s_tile0 + (j % TS) * L::kTileBytes;
         const uint32_t pt = s_p + 2 * s * L::kPBytes;
         // A = V^T, MN-major, 128-byte swizzle: a 128-dim block = 2 chunks (kTcKeys / 8) KB apart
         // (lbo), K step ks = key groups 2 ks, 2 ks + 1 (1 KB apart: sbo); B = P^T, no swizzle
@@ -702,9 +905,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const AttnTcArgs
                      db0 + (uint64_t)(ks * db_step), id_pv, j > 0 || ks > 0);
         }
         if (PAIR)
-          umma_commit_pair(b_free(j % kTcStages));  // the tile is free, in both CTAs
+          umma_commit_pair(b_free(j % TS));  // the tile is free, in both CTAs
         else
-          umma_commit(b_free(j % kTcStages));  // the tile is free
+          umma_commit(b_free(j % TS));  // the tile is free
         umma_commit(b_pvdone(s));  // P[s] free; O holds sub-blocks 0 .. j
         if (!qk_done) {
           ok = wait_qk(j + 1);

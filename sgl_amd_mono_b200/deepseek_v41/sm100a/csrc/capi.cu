@@ -72,13 +72,18 @@ struct Option {
 // each gather every key (0; DSV41_ATTN_PAIR=0), for comparison.
 // The smallest M whose MXFP8-input GEMVs run on the tcgen05 dense kernel (DSV41_DENSE_MIN_M, 16).
 // Programmatic dependent launch between the layer's kernels (DSV41_PDL=0 turns it off).
+// The tcgen05 attention's producer staging each tile's records by bulk copies (1; lone CTAs), or
+// gathering them into registers (0, default; DSV41_ATTN_BULK=1 turns staging on). Measured at
+// config 2, M = 48: staged 469 us against the gathering pair's 386 us (two f16 tile stages beside
+// the staging ring put each tile's conversion on the MMA's critical path).
 Option g_options[] = {
     {"attn_tc", "DSV41_ATTN", 1, {0}, {false}},
     {"attn_pair", "DSV41_ATTN_PAIR", 1, {0}, {false}},
     {"dense_min_m", "DSV41_DENSE_MIN_M", 16, {0}, {false}},
     {"pdl", "DSV41_PDL", 1, {0}, {false}},
+    {"attn_bulk", "DSV41_ATTN_BULK", 0, {0}, {false}},
 };
-enum { kOptAttnTc, kOptAttnPair, kOptDenseMinM, kOptPdl };
+enum { kOptAttnTc, kOptAttnPair, kOptDenseMinM, kOptPdl, kOptAttnBulk };
 
 int64_t option(int i) {
   Option& o = g_options[i];
@@ -90,6 +95,7 @@ int64_t option(int i) {
       if (const char* e = getenv(o.env)) {
         if (i == kOptAttnTc) v = e[0] == 'm' ? 0 : 1;
         else if (i == kOptDenseMinM) v = std::max(1, atoi(e));
+        else if (i == kOptAttnBulk) v = e[0] == '1' ? 1 : 0;
         else v = e[0] == '0' ? 0 : 1;
       }
       o.value.store(v, std::memory_order_relaxed);
@@ -103,6 +109,7 @@ bool use_tc_attention() { return option(kOptAttnTc) == 1; }
 bool use_attn_pair() { return option(kOptAttnPair) == 1; }
 int dense_min_rows() { return (int)option(kOptDenseMinM); }
 bool use_pdl() { return option(kOptPdl) == 1; }
+bool use_attn_bulk() { return option(kOptAttnBulk) == 1; }
 
 int launch_status() {
   cudaError_t e = cudaGetLastError();
@@ -550,15 +557,21 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   mark(a->events, 0, st);
   if (tc) {
     AttnTcArgs ta = {at, heads >= 32 ? 32 : std::max(16, cdiv(heads, 16) * 16), head_tiles};
-    // a row's two head tiles share their key tiles as a CTA pair
-    const bool pair = head_tiles == 2 && use_attn_pair();
+    // the staged producer (lone CTAs), or a row's two head tiles sharing their key tiles as a
+    // CTA pair, or lone gathering CTAs
+    const bool bulk = use_attn_bulk();
+    const bool pair = !bulk && head_tiles == 2 && use_attn_pair();
     const dim3 grid(M * nchunks * head_tiles), block(kTcThreads);
+    using S576 = TcSmem<576, kTcBulkStages, kTcStaging>;
+    using S512 = TcSmem<512, kTcBulkStages, kTcStaging>;
     if (nope == 512)
-      DSV41_TRY(pair ? launch(attn_tc_kernel<512, true>, grid, block, TcSmem<576>::kBytes, st, ta, 2)
-                     : launch(attn_tc_kernel<512, false>, grid, block, TcSmem<576>::kBytes, st, ta));
+      DSV41_TRY(bulk ? launch(attn_tc_kernel<512, false, true>, grid, block, S576::kBytes, st, ta)
+                : pair ? launch(attn_tc_kernel<512, true>, grid, block, TcSmem<576>::kBytes, st, ta, 2)
+                       : launch(attn_tc_kernel<512, false>, grid, block, TcSmem<576>::kBytes, st, ta));
     else
-      DSV41_TRY(pair ? launch(attn_tc_kernel<448, true>, grid, block, TcSmem<512>::kBytes, st, ta, 2)
-                     : launch(attn_tc_kernel<448, false>, grid, block, TcSmem<512>::kBytes, st, ta));
+      DSV41_TRY(bulk ? launch(attn_tc_kernel<448, false, true>, grid, block, S512::kBytes, st, ta)
+                : pair ? launch(attn_tc_kernel<448, true>, grid, block, TcSmem<512>::kBytes, st, ta, 2)
+                       : launch(attn_tc_kernel<448, false>, grid, block, TcSmem<512>::kBytes, st, ta));
   } else {
     DSV41_TRY(launch(attn_split_kernel, dim3(M * nchunks * head_tiles), dim3(256), attn_smem_bytes(D), st, at));
   }

@@ -246,6 +246,27 @@ __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
   return r;
 }
 
+// Four e4m3 bytes of w (byte 0 lowest) -> two f16x2 words {b0, b1}, {b2, b3}, each times the f16x2
+// factor s2 (both halves the same power of two, 2^8 x the wanted scale), by integer ops and one f16
+// multiply a word: an e4m3 byte s.eeee.mmm placed as the f16 bits s.0eeee.mmm0000000 is its value
+// times 2^-8 exactly, normal and subnormal alike (e4m3 bias 7, f16 bias 15: exponent fields that
+// differ by 8; subnormal mantissas alike), so the multiply by s2 rounds the exact product once --
+// the bits cvt.rn.f16x2.e4m3x2 and a multiply by the scale give. (e4m3 NaN, 0x7f / 0xff, becomes a
+// finite value: the KV records never hold it.)
+__device__ __forceinline__ void e4m3x4_f16x2_scaled(uint32_t w, uint32_t s2, uint32_t& lo, uint32_t& hi) {
+  uint32_t z0, z1;
+  asm("prmt.b32 %0, %1, 0, 0x1404;" : "=r"(z0) : "r"(w));  // {0, b0, 0, b1}
+  asm("prmt.b32 %0, %1, 0, 0x3424;" : "=r"(z1) : "r"(w));  // {0, b2, 0, b3}
+  lo = hmul2_bits(((z0 >> 1) & 0x3F803F80u) | (z0 & 0x80008000u), s2);
+  hi = hmul2_bits(((z1 >> 1) & 0x3F803F80u) | (z1 & 0x80008000u), s2);
+}
+// The f16x2 factor of e4m3x4_f16x2_scaled for an E8M0 scale code: 2^8 x 2^(code - 127), a
+// normal f16 for codes 105 .. 134.
+__device__ __forceinline__ bool e4m3_f16_scale_ok(int code) { return code >= 105 && code <= 134; }
+__device__ __forceinline__ uint32_t e4m3_f16_scale(int code) {
+  const uint32_t s1 = (uint32_t)(code - 104) << 10;
+  return s1 | (s1 << 16);
+}
 __device__ __forceinline__ float2 e4m3x2_float2(uint32_t two) {
   const uint32_t h = e4m3x2_f16(two);
   return __half22float2(*reinterpret_cast<const __half2*>(&h));

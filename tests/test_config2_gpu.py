@@ -1,8 +1,8 @@
 """K1 + K2 at BASELINE config-2 shapes -- the kernel configurations ``bench.py`` times -- on the
 GPU against the CPU oracle, stage by stage.
 
-Config 2 is hidden 4096, 64 heads of 512 + 64 dims (so the tcgen05 attention runs as a CTA
-pair over the row's two 32-head tiles, ``attn_tc_kernel<512, PAIR>``), q_lora 1024, 8 wo_a
+Config 2 is hidden 4096, 64 heads of 512 + 64 dims (so the tcgen05 attention runs over the
+row's two 32-head tiles, ``attn_tc_kernel<512, ...>``), q_lora 1024, 8 wo_a
 groups of 1024, 256 routed experts top-8 with intermediate 2048 (the expert kernel's K slices
 and row groups) and a shared expert of 2048. Rows M = 1 (the CUDA-core GEMVs), 16 and 48 (the
 tcgen05 dense projections), at KV context 1536.
@@ -13,7 +13,8 @@ gates (pre, post, comb) within 1e-6; q cos 0.99999 / rel 5e-3; the attention out
 0.9998 (and rel 1e-3) against the exact oracle attention of the GPU's own q; wo_a rel 5e-3,
 wo_b rel 1e-3; the FFN seam's gates rel 1e-4; router logits, routing ids and weights
 bit-exact; the MoE partial cos 0.9999 / rel 1.5e-2. Each stage's oracle runs on the GPU's own
-inputs to that stage. The CTA-pair attention and the two lone CTAs give the same bits.
+inputs to that stage. The attention's three producers -- records gathered by a CTA pair (the
+default), staged by bulk copies, or gathered by lone CTAs -- give the same bits.
 Every check runs and the failures are reported together.
 """
 
@@ -73,6 +74,7 @@ def layer2():
     W = cpu(w)
     yield s, r, L, W
     ext.set_option("attn_pair", 1)
+    ext.set_option("attn_bulk", 0)
 
 
 @pytest.mark.parametrize("M", [1, 16, 48])
@@ -82,12 +84,19 @@ def test_config2_stages(layer2, M):
     s, r, L, W = layer2
     step = synth.make_step(s, M, CTX, 900 + M, DEV)
     cache0 = step["cache"].clone()
+    ext.set_option("attn_bulk", 0)
     ext.set_option("attn_pair", 1)
     b = r.k1(L, step, M)
     r.k2(L, step, M, b)
     torch.cuda.synchronize()
     B = cpu(b)
-    # the same K2 with the row's two head tiles as lone CTAs
+    # the same K2 with the other producers: records staged by bulk copies, then gathered by lone
+    # CTAs
+    ext.set_option("attn_bulk", 1)
+    r.k2(L, step, M, b)
+    torch.cuda.synchronize()
+    staged = cpu(b)
+    ext.set_option("attn_bulk", 0)
     ext.set_option("attn_pair", 0)
     r.k2(L, step, M, b)
     torch.cuda.synchronize()
@@ -134,8 +143,9 @@ def test_config2_stages(layer2, M):
                       nope, s.rope, 8)
     gx = B["xo"].float()
     c("attention cos >= 0.9998, rel < 1e-3", cos(gx, xo) >= 0.9998 and rel(gx, xo) < 1e-3, (cos(gx, xo), rel(gx, xo)))
-    c("pair == lone CTAs", torch.equal(B["xo"], lone["xo"]) and torch.equal(B["out"], lone["out"]),
-      maxabs(B["xo"], lone["xo"]))
+    for name, other in (("staged", staged), ("lone", lone)):
+        c(f"pair == {name} CTAs", torch.equal(B["xo"], other["xo"]) and torch.equal(B["out"], other["out"]),
+          maxabs(B["xo"], other["xo"]))
     # ---- wo_a -> X8B, wo_b
     _, x8b, x8bs = OL.wo_a(gx, W["woa"], W["woa_s"], s.groups_local, s.o_rank)
     wr = rel(N.mxfp8_dequant(B["x8b"], B["x8bs"]), N.mxfp8_dequant(x8b, x8bs))
