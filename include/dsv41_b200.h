@@ -35,10 +35,12 @@ int dsv41_arch(void);
  * or the mma.sync one; "attn_pair" 1/0 (DSV41_ATTN_PAIR) a row's two 32-head tiles as one CTA
  * pair sharing key tiles, or two lone CTAs; "dense_min_m" >= 1 (DSV41_DENSE_MIN_M, 16) the
  * smallest M whose MXFP8-input projections run on the tcgen05 dense kernel; "pdl" 1/0
- * (DSV41_PDL) programmatic dependent launch; "attn_bulk" 0/1 (DSV41_ATTN_BULK) the tcgen05
- * attention's producer gathering each key tile's records into registers (default; "attn_pair"
- * then chooses pair or lone CTAs), or staging them in shared memory by bulk copies (lone CTAs). Takes effect at the next launch; DSV41_EINVAL for
- * an unknown name or value. No counterpart in the reference (its variants are build keys). */
+ * (DSV41_PDL) programmatic dependent launch; "fused_allreduce" 1/0 (DSV41_FUSED_AR) K2's two
+ * TP all-reduces fused into the kernels producing their partials, or the standalone exchange
+ * kernel after each; "attn_bulk" 0/1 (DSV41_ATTN_BULK) the tcgen05 attention's producer
+ * gathering each key tile's records into registers (default; "attn_pair" then chooses pair or
+ * lone CTAs), or staging them in shared memory by bulk copies (lone CTAs). Takes effect at the
+ * next launch; DSV41_EINVAL for an unknown name or value. No counterpart in the reference (its variants are build keys). */
 int dsv41_set_option(const char* name, int64_t value);
 
 /* ---------------------------------------------------------------- FP8 GEMV
@@ -203,7 +205,8 @@ int dsv41_map_compact(const Dsv41MapCompactArgs* a, void* stream);
 
 /* ---------------------------------------------------------------- TP exchange regions
  * One region a rank (guard words, failure flags, per-CTA arrival flags, two parities of
- * tp data slots of cap bf16 elements); replaces common/peer.py:114-156 (PeerBuffer) and the
+ * tp data slots of cap bf16 elements, then two parities of tp LL slots of cap / 2 8-byte
+ * words); replaces common/peer.py:114-156 (PeerBuffer) and the
  * guard block of common/guard.py:20-40. Construction is collective in the caller: every
  * rank allocates its region, the 64-byte IPC handles are exchanged, and every rank opens the
  * others'. dsv41_peer_region_bytes: the size of a region for tp ranks and cap elements. */
@@ -230,6 +233,14 @@ typedef struct {
   int64_t n, tp, rank, peers, cap, src, dst, deadline_ns, site, skip_push;
 } Dsv41AllReduceArgs;
 int dsv41_allreduce(const Dsv41AllReduceArgs* a, void* stream);
+
+/* The same all-reduce as LL stores: every 8-byte word of the exchange carries an epoch beside two
+ * bf16 values, so a reader polls the data itself -- no fence and arrival-flag round trip. The
+ * exchange K2 fuses into its two producing kernels at tp > 1 (wo_b's epilogue, the MoE combine);
+ * this entry runs it alone. Same arguments, result bits and guard words as dsv41_allreduce. The
+ * reference's {value, tag} mailbox (common/sync.py:109-188) and its in-kernel pushes
+ * (stages/seam.py:382-425, stages/moe.py:1156-1184, 1247-1268). */
+int dsv41_allreduce_ll(const Dsv41AllReduceArgs* a, void* stream);
 
 /* out = bf16(rank-order fp32 sum of parts[r]), parts [tp][n] bf16 contiguous: the reduction
  * step of the NCCL variant (all-gather, then this); bit-identical to dsv41_allreduce.

@@ -82,8 +82,9 @@ Option g_options[] = {
     {"dense_min_m", "DSV41_DENSE_MIN_M", 16, {0}, {false}},
     {"pdl", "DSV41_PDL", 1, {0}, {false}},
     {"attn_bulk", "DSV41_ATTN_BULK", 0, {0}, {false}},
+    {"fused_allreduce", "DSV41_FUSED_AR", 1, {0}, {false}},
 };
-enum { kOptAttnTc, kOptAttnPair, kOptDenseMinM, kOptPdl, kOptAttnBulk };
+enum { kOptAttnTc, kOptAttnPair, kOptDenseMinM, kOptPdl, kOptAttnBulk, kOptFusedAr };
 
 int64_t option(int i) {
   Option& o = g_options[i];
@@ -110,6 +111,10 @@ bool use_attn_pair() { return option(kOptAttnPair) == 1; }
 int dense_min_rows() { return (int)option(kOptDenseMinM); }
 bool use_pdl() { return option(kOptPdl) == 1; }
 bool use_attn_bulk() { return option(kOptAttnBulk) == 1; }
+// TP > 1: both all-reduces fused into the kernels that produce the partials (wo_b's epilogue, the
+// MoE combine) as LL peer stores (1, default), or the standalone exchange kernel after each (0;
+// DSV41_FUSED_AR=0).
+bool use_fused_allreduce() { return option(kOptFusedAr) == 1; }
 
 int launch_status() {
   cudaError_t e = cudaGetLastError();
@@ -236,6 +241,23 @@ cudaError_t launch(Kern kernel, dim3 grid, dim3 block, int smem, cudaStream_t st
     cfg.numAttrs = 2;
   }
   return cudaLaunchKernelEx(&cfg, kernel, args);
+}
+
+// The same with any kernel parameters (no cluster).
+template <typename... Exp, typename... Act>
+cudaError_t launch_n(void (*kernel)(Exp...), dim3 grid, dim3 block, int smem, cudaStream_t st, Act&&... args) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = use_pdl() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Act>(args)...);
 }
 
 // The same with two kernel parameters (a tensor map, then the arguments).
@@ -544,6 +566,16 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
 
   const int phase = (int)a->phase, tp = (int)a->tp, rank = (int)a->rank;
   const __nv_bfloat16* reduced = attn;
+  // the fused exchanges: every CTA resident (a thread pushes all its groups before it waits)
+  const bool fused = tp > 1 && phase == 0 && use_fused_allreduce();
+  auto exchange = [&](int site, __nv_bfloat16* dst) {
+    PeerLL x = {};
+    x.peers = ptr<const int64_t>(a->peers); x.tp = tp; x.rank = rank; x.site = site;
+    x.skip = a->inject == site; x.cap = a->peer_cap; x.deadline_ns = deadline_or_default(a->deadline_ns);
+    x.reduced = dst;
+    return x;
+  };
+  const int xgrid = std::min(grid_for((int64_t)M * H / 8, 256), 4 * sms);
   if (phase != 2) {
   // ---- attention
   AttnArgs at = {};
@@ -590,10 +622,13 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   DSV41_TRY(launch(finalize_kernel, dim3(grid_for((int64_t)M * G * O / 8, 256)), dim3(256), 0, st, fa));
   DSV41_TRY(dense_go(gb, x8b, x8bs, st));
   FinalizeArgs fb = {M, H, gb.kslices, gb.out, attn_part, nullptr, nullptr};
-  DSV41_TRY(launch(finalize_kernel, dim3(grid_for((int64_t)M * H / 8, 256)), dim3(256), 0, st, fb));
+  if (fused) fb.x = exchange(1, attn);  // + the attention all-reduce into attn
+  DSV41_TRY(launch(finalize_kernel, dim3(fused ? xgrid : grid_for((int64_t)M * H / 8, 256)), dim3(256), 0, st, fb));
   mark(a->events, 2, st);
   if (phase == 1) return launch_status();
-  if (tp > 1) {
+  if (fused) {
+    // reduced in the wo_b epilogue
+  } else if (tp > 1) {
     // the attention all-reduce (site 1)
     DSV41_TRY(allreduce_go(M * H, tp, rank, a->peers, a->peer_cap, attn_part, attn, a->deadline_ns, 1,
                            a->inject == 1, st));
@@ -658,10 +693,13 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
                       dim3(kMxThreads), MxSmem::kBytes, st, m2, td));
   }
   CombineMoeArgs cm = {M, H, TK, ed.kslices, gd.kslices, ed.out, ptr<const float>(a->wts), gd.out, moe_part};
+  if (fused) cm.x = exchange(2, ptr<__nv_bfloat16>(a->out));  // + the MoE all-reduce into out
   mark(a->events, 6, st);
-  DSV41_TRY(launch(moe_combine_kernel, dim3(grid_for((int64_t)M * H / 8, 256)), dim3(256), 0, st, cm));
+  DSV41_TRY(launch(moe_combine_kernel, dim3(fused ? xgrid : grid_for((int64_t)M * H / 8, 256)), dim3(256), 0, st, cm));
   if (phase == 2) return launch_status();
-  if (tp > 1) {
+  if (fused) {
+    // reduced in the combine
+  } else if (tp > 1) {
     // the MoE all-reduce (site 2)
     DSV41_TRY(allreduce_go(M * H, tp, rank, a->peers, a->peer_cap, moe_part, ptr<void>(a->out), a->deadline_ns,
                            2, a->inject == 2, st));
@@ -844,6 +882,21 @@ int dsv41_allreduce(const Dsv41AllReduceArgs* a, void* stream) {
   DSV41_TRY(allreduce_go((int)a->n, (int)a->tp, (int)a->rank, a->peers, a->cap, ptr<const void>(a->src),
                          ptr<void>(a->dst), a->deadline_ns, (int)a->site, (int)a->skip_push,
                          reinterpret_cast<cudaStream_t>(stream)));
+  return launch_status();
+}
+
+int dsv41_allreduce_ll(const Dsv41AllReduceArgs* a, void* stream) {
+  if (!a || a->tp < 1 || a->tp > kPeerMaxTp || a->rank < 0 || a->rank >= a->tp || !a->peers || !a->src ||
+      !a->dst || a->n < 8 || a->n % 8 || a->cap < a->n || a->cap % 8 || a->n > (1LL << 30) || a->src % 16 ||
+      a->dst % 16)
+    return DSV41_EINVAL;
+  PeerLL x = {};
+  x.peers = ptr<const int64_t>(a->peers); x.tp = (int)a->tp; x.rank = (int)a->rank; x.site = (int)a->site;
+  x.skip = (int)a->skip_push; x.cap = a->cap; x.deadline_ns = deadline_or_default(a->deadline_ns);
+  x.reduced = ptr<__nv_bfloat16>(a->dst);
+  const int grid = std::min(grid_for(a->n / 8, 256), 4 * sm_count());
+  DSV41_TRY(launch_n(allreduce_ll_kernel, dim3(grid), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), x,
+                     ptr<const __nv_bfloat16>(a->src), (int)a->n));
   return launch_status();
 }
 

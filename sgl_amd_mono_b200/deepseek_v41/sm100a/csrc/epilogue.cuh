@@ -3,6 +3,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "peer.cuh"
 
 namespace dsv41 {
 
@@ -12,11 +13,16 @@ struct FinalizeArgs {
   __nv_bfloat16* out;     // [M, N] bf16(sum) (or the dequantized MXFP8 when q8 is set)
   uint8_t* q8;            // optional [M, N] e4m3 (vLLM rule)
   uint8_t* q8s;           // [M, N / 32]
+  PeerLL x;               // x.peers set: out is this rank's partial of a TP all-reduce into x.reduced
 };
 
-// A thread = 8 consecutive columns (4 threads a 32-group when requantizing).
+// A thread = 8 consecutive columns (4 threads a 32-group when requantizing). With an exchange
+// (wo_b's epilogue at tp > 1: the attention all-reduce), each thread pushes its groups to every
+// rank, then reduces the same groups from every rank (peer.cuh's fused exchange).
 __global__ void finalize_kernel(const FinalizeArgs a) {
   pdl_wait();
+  int xfail = 1;
+  const uint32_t e = a.x.peers ? ll_begin(a.x, &xfail) : 0u;
   const int g8 = a.N / 8;
   const int total = a.M * g8, padded = (total + 31) / 32 * 32;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < padded; i += gridDim.x * blockDim.x) {
@@ -51,6 +57,16 @@ __global__ void finalize_kernel(const FinalizeArgs a) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) o[q] = pack_bf16x2(v[2 * q], v[2 * q + 1]);
     if (live) *reinterpret_cast<uint4*>(a.out + (size_t)t * a.N + c) = make_uint4(o[0], o[1], o[2], o[3]);
+    if (live && !xfail) ll_push(a.x, e, i, o);
+  }
+  if (a.x.peers) {
+    if (!xfail)
+      for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        uint32_t o[4];
+        if (!ll_reduce(a.x, e, i, o)) break;
+        reinterpret_cast<uint4*>(a.x.reduced)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    ll_end(a.x, e);
   }
   pdl_launch();
 }

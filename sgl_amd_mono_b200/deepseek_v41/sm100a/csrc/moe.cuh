@@ -13,6 +13,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "peer.cuh"
 #include "detmath.cuh"
 
 namespace dsv41 {
@@ -429,6 +430,7 @@ struct CombineMoeArgs {
   const float* wts;      // [M, topk]
   const float* shared;   // [shared_slices][M][H] shared down partials
   __nv_bfloat16* out;    // [M, H]: bf16(routed + shared)
+  PeerLL x;              // x.peers set: out is this rank's partial of the MoE all-reduce into x.reduced
 };
 
 // routed = bf16(routed + bf16(y_k w_k)) in top-k order; out = bf16(routed + bf16(shared)). A
@@ -436,6 +438,8 @@ struct CombineMoeArgs {
 // together (each pick's slices still added in slice order).
 __global__ void moe_combine_kernel(const CombineMoeArgs a) {
   pdl_wait();
+  int xfail = 1;
+  const uint32_t e = a.x.peers ? ll_begin(a.x, &xfail) : 0u;
   const int g8 = a.H / 8;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.M * g8; i += gridDim.x * blockDim.x) {
     const int t = i / g8, n = (i % g8) * 8;
@@ -478,6 +482,17 @@ __global__ void moe_combine_kernel(const CombineMoeArgs a) {
     for (int q = 0; q < 4; ++q)
       o[q] = pack_bf16x2(routed[2 * q] + bf16r(sh[2 * q]), routed[2 * q + 1] + bf16r(sh[2 * q + 1]));
     *reinterpret_cast<uint4*>(a.out + (size_t)t * a.H + n) = make_uint4(o[0], o[1], o[2], o[3]);
+    if (!xfail) ll_push(a.x, e, i, o);
+  }
+  // tp > 1: the MoE all-reduce of this kernel's groups (peer.cuh's fused exchange)
+  if (a.x.peers) {
+    if (!xfail)
+      for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.M * g8; i += gridDim.x * blockDim.x) {
+        uint32_t o[4];
+        if (!ll_reduce(a.x, e, i, o)) break;
+        reinterpret_cast<uint4*>(a.x.reduced)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    ll_end(a.x, e);
   }
   pdl_launch();
 }

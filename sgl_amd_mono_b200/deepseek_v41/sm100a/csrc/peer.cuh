@@ -12,6 +12,16 @@
 //   [256, 288)    failure flags: rank r writes word r of every rank's region when it fails
 //   [512, +4 * kPeerMaxTp * kArBlocks)   arrival flags [src rank][CTA], the sequence number
 //   [kPeerDataOff, ...)  data slots [parity][src rank][cap] bf16
+//   then LL slots [parity][src rank][cap / 2] 8-byte words {bf16x2, epoch}: the fused exchange
+//
+// The fused exchange (the wo_b epilogue and the MoE combine, ll_* below) needs no arrival flags:
+// every 8-byte word carries its exchange's epoch beside two bf16 values, written by one 8-byte
+// store, so a reader that sees the epoch sees the data (the reference's {value, tag} mailbox,
+// sync.py:109-188). A producing thread stores its values into slot [e & 1][rank] of every rank's
+// region, then polls its own region's slots of every rank for the same elements and sums them in
+// rank order. Parity reuse is safe as above: a rank writes exchange e + 2 only after its kernel of
+// exchange e + 1 completed, which needed every rank's pushes of e + 1, each made after that
+// rank's kernel of exchange e (its reads included) completed.
 //
 // Sequence numbers only grow, so a waiter accepts any flag >= its own; the data of exchange e
 // lives in parity e & 1, which no rank can overwrite before every rank has finished reading it
@@ -35,7 +45,7 @@ constexpr int kArriveOff = 512;
 constexpr int kPeerDataOff = 8192;
 
 __host__ __device__ inline int64_t peer_region_bytes(int tp, int64_t cap) {
-  return kPeerDataOff + 2LL * tp * cap * 2;
+  return kPeerDataOff + 2LL * tp * cap * 2 + 2LL * tp * cap * 4;
 }
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
@@ -164,6 +174,144 @@ __global__ void __launch_bounds__(256) allreduce_kernel(const AllReduceArgs a) {
       atomicExch(words + kGuardSeq, e);
     }
   }
+  pdl_launch();
+}
+
+// ------------------------------------------------------------------ the fused (LL) exchange
+struct PeerLL {
+  const int64_t* peers;   // [tp] regions as mapped here; null: no exchange (tp 1, or a split phase)
+  int tp, rank, site, skip;  // skip: the fault-injection hook (publish nothing at this site)
+  int64_t cap;            // elements a slot holds (a multiple of 8, >= the exchange's elements)
+  int64_t deadline_ns;
+  __nv_bfloat16* reduced; // [n] the rank-order sum
+};
+
+__device__ __forceinline__ uint64_t* ll_slot(int64_t base, int par, int tp, int src, int64_t cap) {
+  return reinterpret_cast<uint64_t*>(base + kPeerDataOff + 4LL * tp * cap) + (int64_t)(par * tp + src) * (cap / 2);
+}
+__device__ __forceinline__ void st_ll2(uint64_t* p, uint32_t w0, uint32_t w1, uint32_t e) {
+  asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(((uint64_t)e << 32) | w0),
+               "l"(((uint64_t)e << 32) | w1)
+               : "memory");
+}
+__device__ __forceinline__ void ld_ll2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+// The CTA's view of the exchange: its epoch, and whether the region has failed (sticky: any
+// error word or any rank's failure flag). Thread 0 reads, the block shares (a barrier inside).
+__device__ inline uint32_t ll_begin(const PeerLL& x, int* fail) {
+  __shared__ uint32_t s_e;
+  __shared__ int s_f;
+  if (threadIdx.x == 0) {
+    const int64_t me = x.peers[x.rank];
+    uint32_t* words = peer_words(me);
+    s_e = __ldcg(words + kGuardSeq) + 1u;
+    uint32_t f = __ldcg(words + kErrDeadline) | __ldcg(words + kErrPeer) | __ldcg(words + kErrFault);
+    for (int r = 0; r < x.tp; ++r) f |= __ldcg(peer_words(me + kFailOff) + r);
+    s_f = f != 0;
+    if (!s_f && x.skip) atomicExch(words + kErrFault, 1u);  // the hook: this rank stalls
+  }
+  __syncthreads();
+  *fail = s_f || x.skip;
+  return s_e;
+}
+
+// This thread's 8 values (4 bf16x2 words) of element group i8 into slot [e & 1][rank] of every
+// rank's region.
+__device__ __forceinline__ void ll_push(const PeerLL& x, uint32_t e, int64_t i8, const uint32_t (&w)[4]) {
+  const int par = (int)(e & 1u);
+  for (int r = 0; r < x.tp; ++r) {
+    uint64_t* p = ll_slot(x.peers[r], par, x.tp, x.rank, x.cap) + 4 * i8;
+    st_ll2(p, w[0], w[1], e);
+    st_ll2(p + 2, w[2], w[3], e);
+  }
+}
+
+// Every rank's values of element group i8 from this rank's region, summed in rank order in fp32
+// and rounded once to bf16, into o. Each wait gives up at the deadline or on another rank's
+// failure flag (checked every 64 polls): it records the site, raises this rank's failure flag in
+// every region and returns false.
+__device__ inline bool ll_reduce(const PeerLL& x, uint32_t e, int64_t i8, uint32_t (&o)[4]) {
+  const int par = (int)(e & 1u);
+  const int64_t me = x.peers[x.rank];
+  float acc[8];
+  uint64_t t0 = 0;
+  for (int r = 0; r < x.tp; ++r) {
+    const uint64_t* p = ll_slot(me, par, x.tp, r, x.cap) + 4 * i8;
+    uint64_t v[4];
+    for (uint32_t it = 1;; ++it) {
+      ld_ll2(p, v[0], v[1]);
+      ld_ll2(p + 2, v[2], v[3]);
+      if ((uint32_t)(v[0] >> 32) == e && (uint32_t)(v[1] >> 32) == e && (uint32_t)(v[2] >> 32) == e &&
+          (uint32_t)(v[3] >> 32) == e)
+        break;
+      if ((it & 63) != 0) continue;
+      // another rank failed (or another thread of this rank gave up: its flag is raised here too)
+      bool failed = false;
+      for (int q = 0; q < x.tp; ++q)
+        if (q != x.rank) failed |= ld_acquire_sys(peer_words(me + kFailOff) + q) != 0;
+      if (failed) {
+        atomicExch(peer_words(me) + kErrPeer, 1u);
+        return false;
+      }
+      if (ld_acquire_sys(peer_words(me + kFailOff) + x.rank) != 0) return false;
+      const uint64_t now = global_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > (uint64_t)x.deadline_ns || it == 0xffffffc0u) {
+        atomicCAS(peer_words(me) + kErrDeadline, 0u, (uint32_t)x.site);
+        for (int q = 0; q < x.tp; ++q) st_release_sys(peer_words(x.peers[q] + kFailOff) + x.rank, 1u);
+        return false;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t d = (uint32_t)v[q];
+      const float lo = __uint_as_float(d << 16), hi = __uint_as_float(d & 0xFFFF0000u);
+      acc[2 * q] = r ? acc[2 * q] + lo : lo;
+      acc[2 * q + 1] = r ? acc[2 * q + 1] + hi : hi;
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) o[q] = pack_bf16x2(acc[2 * q], acc[2 * q + 1]);
+  return true;
+}
+
+// The exchange's end: the last CTA of the grid advances the sequence (after every CTA's reads).
+__device__ inline void ll_end(const PeerLL& x, uint32_t e) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t* words = peer_words(x.peers[x.rank]);
+    __threadfence();
+    if (atomicAdd(words + kGuardDone, 1u) == gridDim.x - 1) {
+      atomicExch(words + kGuardDone, 0u);
+      __threadfence();
+      atomicExch(words + kGuardSeq, e);
+    }
+  }
+}
+
+// The standalone LL exchange (dsv41_allreduce_ll): dst = bf16(rank-order sum of every rank's src),
+// a thread a group of 8 elements; every thread pushes all its groups before it waits for any.
+__global__ void __launch_bounds__(256) allreduce_ll_kernel(const PeerLL x, const __nv_bfloat16* src, int n) {
+  pdl_wait();
+  int fail = 0;
+  const uint32_t e = ll_begin(x, &fail);
+  const int groups = n / 8;
+  if (!fail) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < groups; i += gridDim.x * blockDim.x) {
+      const uint4 v = reinterpret_cast<const uint4*>(src)[i];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      ll_push(x, e, i, w);
+    }
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < groups; i += gridDim.x * blockDim.x) {
+      uint32_t o[4];
+      if (!ll_reduce(x, e, i, o)) break;
+      reinterpret_cast<uint4*>(x.reduced)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  ll_end(x, e);
   pdl_launch();
 }
 

@@ -1,7 +1,8 @@
 """The TP exchange on the GPU.
 
-One GPU: ``dsv41_allreduce`` as rank 0 of 2 with the other rank emulated by the host (its
-slot and arrival flags written before the launch, so no kernel waits on another kernel):
+One GPU: ``dsv41_allreduce`` (and ``dsv41_allreduce_ll``, the LL exchange K2 fuses into its
+producing kernels) as rank 0 of 2 with the other rank emulated by the host (its slot and arrival
+flags, or its tagged LL words, written before the launch, so no kernel waits on another kernel):
 the result is the rank-order fp32 sum rounded once, bit for bit, over consecutive exchanges
 of both parities; a wait that nothing satisfies gives up at its deadline, records its site,
 raises the failure flags, and later exchanges on the failed region do nothing; the context
@@ -113,6 +114,80 @@ def test_allreduce_deadline_gives_up_and_sticks():
     assert time.perf_counter() - t0 < 0.15
     assert (dst.cpu() == 7.0).all() and _words(r0)[3] == 7
     # the context is still usable
+    x = torch.arange(1000, device=dev, dtype=torch.float32)
+    assert float(x.sum()) == 499500.0
+
+
+def _ll_slot_words(region, par, tp, src, cap):
+    off = 8192 + 4 * tp * cap + (par * tp + src) * (cap // 2) * 8
+    return region[off:off + (cap // 2) * 8].view(torch.int64)
+
+
+def _ll_words(vals_bf16, tag):
+    """LL words of a bf16 vector: {bf16x2 of elements 2k, 2k + 1 (low 32 bits), tag (high)}."""
+    bits = vals_bf16.view(torch.int16).to(torch.int64) & 0xFFFF
+    pair = bits[0::2] | (bits[1::2] << 16)
+    return pair | (int(tag) << 32)
+
+
+def _allreduce_ll(table, tp, rank, cap, src, dst, deadline_ns=2_000_000_000, site=1, skip=0):
+    from sgl_amd_mono_b200.common import ext
+    from sgl_amd_mono_b200.deepseek_v41.sm100a import abi
+    a = abi.AllReduceArgs(n=src.numel(), tp=tp, rank=rank, peers=table.data_ptr(), cap=cap, src=src.data_ptr(),
+                          dst=dst.data_ptr(), deadline_ns=deadline_ns, site=site, skip_push=skip)
+    ext.call("dsv41_allreduce_ll", a, torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.parametrize("n", [4096, 48 * 4096, 8])
+def test_allreduce_ll_emulated_peer_bit_exact(n):
+    """The fused exchange's LL protocol as rank 0 of 2, rank 1 emulated by the host: its words
+    (tag = the exchange's epoch) written into rank 0's LL slot before the launch."""
+    dev = torch.device("cuda", 0)
+    cap = 48 * 4096
+    r0, r1 = _regions(2, cap, dev)
+    table = torch.tensor([r0.data_ptr(), r1.data_ptr()], dtype=torch.int64, device=dev)
+    g = torch.Generator(device=dev).manual_seed(n + 1)
+    for e in (1, 2, 3):
+        p0 = (torch.randn(n, generator=g, device=dev) * 3).to(torch.bfloat16)
+        p1 = (torch.randn(n, generator=g, device=dev) * 3).to(torch.bfloat16)
+        _ll_slot_words(r0, e & 1, 2, 1, cap)[: n // 2] = _ll_words(p1, e)
+        dst = torch.empty(n, dtype=torch.bfloat16, device=dev)
+        _allreduce_ll(table, 2, 0, cap, p0, dst)
+        torch.cuda.synchronize()
+        assert torch.equal(dst.cpu(), OL.all_reduce([p0.cpu(), p1.cpu()])), e
+        # pushed into the peer's slot (and its own), tagged with the epoch
+        assert torch.equal(_ll_slot_words(r1, e & 1, 2, 0, cap)[: n // 2], _ll_words(p0, e))
+        assert torch.equal(_ll_slot_words(r0, e & 1, 2, 0, cap)[: n // 2], _ll_words(p0, e))
+        w = _words(r0)
+        assert w[0] == e and w[1] == 0 and w[3:6] == [0, 0, 0]
+
+
+def test_allreduce_ll_deadline_gives_up_and_sticks():
+    from sgl_amd_mono_b200.common.peer import Native
+    dev = torch.device("cuda", 0)
+    cap = 4096
+    r0, r1 = _regions(2, cap, dev)
+    table = torch.tensor([r0.data_ptr(), r1.data_ptr()], dtype=torch.int64, device=dev)
+    src = torch.ones(cap, dtype=torch.bfloat16, device=dev)
+    dst = torch.full((cap,), 7.0, dtype=torch.bfloat16, device=dev)
+    t0 = time.perf_counter()
+    _allreduce_ll(table, 2, 0, cap, src, dst, deadline_ns=200_000_000, site=7)  # rank 1 never writes
+    torch.cuda.synchronize()
+    took = time.perf_counter() - t0
+    assert 0.15 < took < 5.0, took
+    w = _words(r0)
+    assert w[3] == 7 and w[0] == 1
+    assert r0[256:288].view(torch.int32).cpu()[0] == 1 and r1[256:288].view(torch.int32).cpu()[0] == 1
+    assert (dst.cpu() == 7.0).all()
+    rc, words = Native().status(r0.data_ptr())
+    assert rc == -4 and words[3] == 7
+    # sticky: the next exchange on the failed region does nothing and returns at once
+    _ll_slot_words(r0, 0, 2, 1, cap)[: cap // 2] = _ll_words(src, 2)
+    t0 = time.perf_counter()
+    _allreduce_ll(table, 2, 0, cap, src, dst, deadline_ns=200_000_000, site=8)
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 0.15
+    assert (dst.cpu() == 7.0).all() and _words(r0)[3] == 7
     x = torch.arange(1000, device=dev, dtype=torch.float32)
     assert float(x.sum()) == 499500.0
 
