@@ -178,6 +178,26 @@ typedef struct {
 } Dsv41K2iArgs;
 int dsv41_k2i(const Dsv41K2iArgs* a, void* stream);
 
+/* The indexer's FP4 query of decode rows, K2i's q / qscale / w inputs, from wq_b's output q
+ * [M, heads, 128] bf16, the layer's RoPE table cos_sin [rope_rows, rope] fp32 (rope / 2 cos, then
+ * rope / 2 sin) at positions pos [M] int64, the normed rows x [M, hidden] bf16 and the head weight
+ * projection wp [heads, hidden] bf16 with its scale (weight_scale_f32: the fp32 bit pattern):
+ * head weights w_out [M, heads] bf16 = bf16(fp32(x . wp[h]) * scale), the dot summed as the
+ * router's logits (exact products, fp64 in a fixed order); GPT-J RoPE on each head's last rope
+ * dims (separate fp32 products); MXFP4 per 32 dims (E8M0 = the ceiling power of two of
+ * amax / 6, E2M1 round to nearest even) into q_out [M, heads, 64] and qscale [M, 1, 4, 16, 4]
+ * (head h's chunk c at [c, h % 16, h / 16]). heads 16..64 in 16s, dim 128; scratch >= M * heads
+ * * 4 bytes. Replaces SGLang's index_q_rope_pack_weights with its split-K head-weight GEMV
+ * (called at deepseek_v41/spec.py:744-763 of the reference). */
+typedef struct {
+  int64_t M, heads, dim, rope, hidden;
+  int64_t q, cos_sin, rope_rows, pos, x, wp, weight_scale_f32;
+  int64_t q_out, qscale, w_out;
+  int64_t scratch, scratch_bytes;
+} Dsv41IndexQueryArgs;
+int64_t dsv41_index_query_scratch_bytes(const Dsv41IndexQueryArgs* a);
+int dsv41_index_query(const Dsv41IndexQueryArgs* a, void* stream);
+
 /* Top-k of each row's first n[t] values (group > 1: of the maxima of groups of `group`
  * values -- candidate blocks), ties to the lower position, written in ascending position
  * order, -1 padded; optional paged twin page_out = table[owners[t]][pos / page] * page +

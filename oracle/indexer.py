@@ -70,6 +70,60 @@ def index_logits(q, qscale, w, payload, kscale, table, t, cols, entry_rows=PAGE)
     return (s[0] + s[1]).float()
 
 
+# E2M1 magnitudes by code, and the rounding boundaries between neighbours: a value exactly on a
+# boundary goes to the neighbour with the even code (round to nearest even)
+E2M1_MAG = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], dtype=np.float64)
+_E2M1_LOW_TIES = (0.25, 1.25, 2.5, 5.0)   # ties go down (to codes 0, 2, 4, 6)
+_E2M1_HIGH_TIES = (0.75, 1.75, 3.5)       # ties go up (to codes 2, 4, 6)
+
+
+def e2m1_rne(y: np.ndarray) -> np.ndarray:
+    """fp32 values -> E2M1 codes (0..15): magnitude by round to nearest even, saturating at 6;
+    the sign bit from the value's sign (a negative value that rounds to zero is -0), as
+    cvt.rn.satfinite.e2m1x2.f32 encodes."""
+    y = np.asarray(y, dtype=np.float32)
+    m = np.abs(y).astype(np.float64)
+    idx = np.zeros(y.shape, dtype=np.int64)
+    for b in _E2M1_LOW_TIES:
+        idx += m > b
+    for b in _E2M1_HIGH_TIES:
+        idx += m >= b
+    return (idx | (np.signbit(y).astype(np.int64) << 3)).astype(np.uint8)
+
+
+def index_query(q, cos_sin, pos, rope, x, wp, scale):
+    """K2i's FP4 query of decode rows, the contract ``dsv41_index_query`` implements (restating
+    SGLang's ``index_q_rope_pack_weights`` with its split-K head-weight GEMV, called at
+    ``deepseek_v41/spec.py:744-763``; SGLang is absent here, so this contract is ours):
+    head weights bf16(fp32(x . wp[h]) * scale), the dot as ``layer.router_logits`` sums it;
+    GPT-J RoPE on the last ``rope`` dims of each head (e0 = k0 c - k1 s, e1 = k0 s + k1 c, fp32,
+    each product and sum rounded); per 32 dims code = the E8M0 ceiling of fp32(max(amax, 2^-126)
+    / 6) (at most 253), E2M1 of v 2^(127 - code) by ``e2m1_rne``, even dims in the low nibble.
+    q [M, H, 128] bf16-valued, cos_sin [rows, rope] fp32, pos [M], x [M, hidden], wp [H, hidden].
+    Returns (q_out [M, H, 64] u8, qscale [M, 1, 4, 16, 4] u8, w [M, H] bf16)."""
+    from . import layer as OL
+    M, H, D = q.shape
+    hw = OL.router_logits(x, wp)
+    w = (hw * torch.tensor(float(scale), dtype=torch.float32)).to(torch.bfloat16)
+    v = q.float().clone()
+    cs = cos_sin[torch.as_tensor(pos).long().clamp(0, cos_sin.shape[0] - 1)].float()
+    c, s = cs[:, None, : rope // 2], cs[:, None, rope // 2:]
+    k0, k1 = v[..., D - rope::2].clone(), v[..., D - rope + 1::2].clone()
+    v[..., D - rope::2] = k0 * c - k1 * s
+    v[..., D - rope + 1::2] = k0 * s + k1 * c
+    chunks = v.view(M, H, D // 32, 32)
+    q6 = chunks.abs().amax(-1).clamp_min(2.0**-126) / torch.tensor(6.0, dtype=torch.float32)
+    bits = q6.view(torch.int32)
+    code = (((bits >> 23) & 0xFF) + ((bits & 0x7FFFFF) != 0).int()).clamp(max=253)
+    mul = ((254 - code) << 23).view(torch.float32)
+    codes4 = torch.from_numpy(e2m1_rne((chunks * mul[..., None]).numpy())).view(M, H, D // 2, 2)
+    packed = (codes4[..., 0] | (codes4[..., 1] << 4)).contiguous()
+    qs = torch.zeros(M, 1, 4, 16, 4, dtype=torch.uint8)
+    h = torch.arange(H)
+    qs[:, 0, :, h % 16, h // 16] = code.to(torch.uint8).permute(0, 2, 1)
+    return packed, qs, w
+
+
 def topk_rows(logits, bound, k):
     """The k largest of one row's logits[:bound], ties to the lower position (the north
     star's rule for SGLang's ``topk_transform_paged``), as positions in ascending order; every

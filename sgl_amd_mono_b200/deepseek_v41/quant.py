@@ -67,21 +67,3 @@ def kv_records(e: torch.Tensor, nope: int):
     sc = torch.zeros(T, 8, dtype=torch.uint8, device=e.device)
     sc[:, : nope // 64] = code.to(torch.uint8)
     return torch.cat([b.reshape(T, nope), rope], 1), sc
-
-
-def fp4_index_query(q: torch.Tensor, freqs_cis: torch.Tensor, pos: torch.Tensor, rope_dim: int,
-                    w: torch.Tensor) -> tuple:
-    """q [M, H, 128] fp32 -> K2i's query: (E2M1 bytes [M, H, 64], E8M0 codes [M, 1, 4, 16, 4] with
-    head h's chunk c at [c, h % 16, h // 16], head weights [M, H] bf16). GPT-J RoPE (pairs
-    2j, 2j + 1) on the last ``rope_dim`` dims with freqs_cis[pos] (complex, rope_dim / 2)."""
-    M, H, D = q.shape
-    q = q.clone()
-    f = freqs_cis[pos.long()][:, None, : rope_dim // 2]
-    r = q[..., D - rope_dim:].reshape(M, H, rope_dim // 2, 2)
-    rc = torch.view_as_complex(r.contiguous()) * f
-    q[..., D - rope_dim:] = torch.view_as_real(rc).reshape(M, H, rope_dim)
-    packed, codes = quant_mxfp4(q.reshape(M * H, D))
-    qs = torch.zeros(M, 1, 4, 16, 4, dtype=torch.uint8, device=q.device)
-    h = torch.arange(H, device=q.device)
-    qs[:, 0, :, h % 16, h // 16] = codes.view(M, H, 4).permute(0, 2, 1)
-    return packed.view(M, H, D // 2).contiguous(), qs, w.to(torch.bfloat16).contiguous()

@@ -48,6 +48,13 @@ K2iArgs = struct("Dsv41K2iArgs", [
     "logits", "lstride", "reindex", "reindex_chunks",
 ])
 
+IndexQueryArgs = struct("Dsv41IndexQueryArgs", [
+    "M", "heads", "dim", "rope", "hidden",
+    "q", "cos_sin", "rope_rows", "pos", "x", "wp", "weight_scale_f32",
+    "q_out", "qscale", "w_out",
+    "scratch", "scratch_bytes",
+])
+
 TopkArgs = struct("Dsv41TopkArgs", [
     "rows", "k", "vals", "vstride", "n", "group", "out", "page_out", "table", "table_stride", "page",
     "owners",
@@ -80,6 +87,7 @@ STRUCTS = {
     "Dsv41K2Args": K2Args,
     "Dsv41WalkPlanArgs": WalkPlanArgs,
     "Dsv41K2iArgs": K2iArgs,
+    "Dsv41IndexQueryArgs": IndexQueryArgs,
     "Dsv41TopkArgs": TopkArgs,
     "Dsv41ReindexArgs": ReindexArgs,
     "Dsv41MapCompactArgs": MapCompactArgs,

@@ -20,6 +20,7 @@
 #include "front.cuh"
 #include "gemv.cuh"
 #include "gemv_entry.cuh"
+#include "index_query.cuh"
 #include "k2i.cuh"
 #include "lmhead.cuh"
 #include "moe.cuh"
@@ -752,6 +753,38 @@ int dsv41_gemv_fp8(const Dsv41GemvArgs* a, void* stream) {
   if (gemv_entry_launch(g, ptr<float>(a->y), ptr<float>(a->scratch), reinterpret_cast<cudaStream_t>(stream)) !=
       cudaSuccess)
     return launch_status();
+  return launch_status();
+}
+
+static bool index_query_ok(const Dsv41IndexQueryArgs* a) {
+  return a && a->M >= 1 && a->M <= 48 && a->heads >= 16 && a->heads <= 64 && a->heads % 16 == 0 && a->dim == 128 &&
+         a->rope >= 2 && a->rope % 2 == 0 && a->rope <= a->dim && a->hidden >= 256 && a->hidden % 256 == 0 &&
+         a->hidden <= 16384 && a->q && a->cos_sin && a->rope_rows >= 1 && a->pos && a->x && a->wp && a->q_out &&
+         a->qscale && a->w_out && a->q % 16 == 0 && a->x % 16 == 0 && a->wp % 16 == 0 && a->q_out % 16 == 0;
+}
+
+int64_t dsv41_index_query_scratch_bytes(const Dsv41IndexQueryArgs* a) {
+  if (!index_query_ok(a)) return DSV41_EINVAL;
+  return a->M * a->heads * 4;
+}
+
+int dsv41_index_query(const Dsv41IndexQueryArgs* a, void* stream) {
+  if (!index_query_ok(a)) return DSV41_EINVAL;
+  if (!a->scratch || a->scratch_bytes < a->M * a->heads * 4 || a->scratch % 16) return DSV41_ESCRATCH;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int M = (int)a->M, heads = (int)a->heads, hidden = (int)a->hidden;
+  float* hw = ptr<float>(a->scratch);
+  // the head weights' dots: the router's exact fixed-order fp64 sums, heads as its experts
+  const int smem = 16 * hidden <= 200 * 1024 ? 16 * hidden : 0;
+  RouterArgs ra = {M, heads, hidden, ptr<const __nv_bfloat16>(a->x), ptr<const __nv_bfloat16>(a->wp), hw, smem > 0};
+  DSV41_TRY(launch(router_kernel, dim3(cdiv(heads, 8), cdiv(M, 8)), dim3(256), smem, st, ra));
+  float scale;
+  const uint32_t sb = (uint32_t)a->weight_scale_f32;
+  memcpy(&scale, &sb, 4);
+  IndexQueryArgs q = {M, heads, (int)a->dim, (int)a->rope, ptr<const __nv_bfloat16>(a->q), ptr<const float>(a->cos_sin),
+                      a->rope_rows, ptr<const int64_t>(a->pos), hw, scale, ptr<uint8_t>(a->q_out),
+                      ptr<uint8_t>(a->qscale), ptr<__nv_bfloat16>(a->w_out)};
+  DSV41_TRY(launch(index_query_kernel, dim3(M), dim3(256), 0, st, q));
   return launch_status();
 }
 

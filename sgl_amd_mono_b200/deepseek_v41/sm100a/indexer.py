@@ -68,8 +68,38 @@ class K2iRunner:
         self.cand_bound = torch.empty(MAX_ROWS, **i32)
         self.compact_pos = torch.empty(MAX_ROWS, topk, **i32)
         self.plans = {r: torch.zeros(ctas, 4, **i32) for r in (1, 2)}
+        self._query: dict[int, tuple] = {}  # per index head count: q, qscale, w, scratch
         t = torch.arange(MAX_ROWS)
         self.owners = torch.stack([t // p * p for p in range(1, MAX_ROWS + 1)]).to(**i32)
+
+    # ------------------------------------------------------------ query
+    def query(self, *, q: torch.Tensor, cos_sin: torch.Tensor, pos: torch.Tensor, x: torch.Tensor,
+              wp: torch.Tensor, scale: float) -> tuple:
+        """The FP4 query of decode rows (``dsv41_index_query``) from wq_b's output q [rows,
+        heads * 128] bf16, the layer's RoPE table, the rows' positions, their normed rows x and
+        the head weight projection wp [heads, hidden] bf16 with its scale: (q [rows, heads, 64]
+        E2M1 pairs, qscale [rows, 1, 4, 16, 4], w [rows, heads] bf16), views of buffers this
+        runner keeps per head count (first call outside graph capture)."""
+        import struct
+        M, H, hidden = x.shape[0], wp.shape[0], x.shape[1]
+        if q.dtype != torch.bfloat16 or q.numel() != M * H * 128 or not q.is_contiguous():
+            raise RuntimeError(f"K2i query: wq_b output {tuple(q.shape)} {q.dtype}, want [{M}, {H * 128}] bf16")
+        if x.dtype != torch.bfloat16 or wp.dtype != torch.bfloat16 or tuple(wp.shape) != (H, hidden):
+            raise RuntimeError(f"K2i query: x {tuple(x.shape)} {x.dtype}, weights_proj {tuple(wp.shape)} {wp.dtype}")
+        if H not in self._query:
+            u8 = dict(dtype=torch.uint8, device=self.dev)
+            self._query[H] = (torch.empty(MAX_ROWS, H, 64, **u8), torch.zeros(MAX_ROWS, 1, 4, 16, 4, **u8),
+                              torch.empty(MAX_ROWS, H, dtype=torch.bfloat16, device=self.dev),
+                              torch.empty(MAX_ROWS * H * 4, **u8))
+        q_out, qscale, w_out, scratch = self._query[H]
+        bits = struct.unpack("<I", struct.pack("<f", float(scale)))[0]
+        a = abi.IndexQueryArgs(M=M, heads=H, dim=128, rope=cos_sin.shape[1], hidden=hidden, q=_p(q),
+                               cos_sin=_p(cos_sin), rope_rows=cos_sin.shape[0], pos=_p(pos),
+                               x=_p(x.contiguous()), wp=_p(wp.contiguous()), weight_scale_f32=bits,
+                               q_out=_p(q_out), qscale=_p(qscale), w_out=_p(w_out), scratch=_p(scratch),
+                               scratch_bytes=scratch.numel())
+        ext.call("dsv41_index_query", a, _stream())
+        return q_out[:M], qscale[:M], w_out[:M]
 
     # ------------------------------------------------------------ plan
     def walk_plan(self, *, ratio: int, bounds: torch.Tensor, rows: int, per_req: int) -> torch.Tensor:

@@ -347,28 +347,27 @@ def _select(*, runner, L, plan, backend, positions, pos, forward_batch, M, b) ->
         k2i.walk_plan(ratio=r, bounds=bounds, rows=M, per_req=per_req)
         plan.state["k2i plan", r] = True
     published = k2i.select(kind=kind, rows=M, per_req=per_req, ratio=r,
-                           query=_index_query(attn, b["normed_a"][:M], b["qr"][:M], pos), plane=L.plane,
+                           query=_index_query(k2i, attn, L, b["normed_a"][:M], b["qr"][:M], pos), plane=L.plane,
                            page_table=meta.page_table, bounds=bounds, raw_out=raw_idx, page_out=page_idx,
                            candidates=plan.state.get("k2i candidates") if kind == "reindex" else None)
     if kind == "producer":
         plan.state["k2i candidates"] = published
 
 
-def _index_query(attn, x: torch.Tensor, q_lora: torch.Tensor, pos: torch.Tensor) -> tuple:
-    """The indexer's FP4 query of decode rows, as K2i reads it: q = wq_b(q_lora), GPT-J RoPE
-    on each head's last rope_head_dim dims, MXFP4 per 32 dims (E8M0 = the ceil power of two of
-    amax / 6); head weights = weights_proj(x) x head_weight_scale in bf16. SGLang's fused
-    query op (the reference reads ``index_q_rope_pack_weights_flydsl``) is not available to
-    this build; this restatement runs as torch ops on the device."""
-    from .quant import fp4_index_query
-
+def _index_query(k2i, attn, L: _Layer, x: torch.Tensor, q_lora: torch.Tensor, pos: torch.Tensor) -> tuple:
+    """The indexer's FP4 query of decode rows, as K2i reads it (the reference's
+    ``_index_query``, ``spec.py:744-763``): q = SGLang's wq_b(q_lora), then one C-ABI call
+    (``dsv41_index_query``) in place of SGLang's fused ``index_q_rope_pack_weights`` and its
+    split-K head-weight GEMV: GPT-J RoPE on each head's last rope_head_dim dims, MXFP4 per 32
+    dims, head weights = weights_proj(x) x head_weight_scale in bf16."""
     ix = attn.indexer
+    if ix.rope_head_dim != L.w["cos_sin"].shape[1]:
+        raise RuntimeError(f"monokernel: layer {L.i}: index RoPE of {ix.rope_head_dim} dims, the layer's table "
+                           f"{L.w['cos_sin'].shape[1]}")
     q = ix.wq_b(q_lora)
     q = q[0] if isinstance(q, tuple) else q
-    w = ix.weights_proj(x)
-    w = w[0] if isinstance(w, tuple) else w
-    return fp4_index_query(q.float().view(x.shape[0], ix.n_heads, -1), attn.freqs_cis, pos, ix.rope_head_dim,
-                           w.float() * ix.head_weight_scale)
+    return k2i.query(q=q.contiguous(), cos_sin=L.w["cos_sin"], pos=pos, x=x, wp=ix.weights_proj.weight,
+                     scale=ix.head_weight_scale)
 
 
 def _index_plane(L: _Layer, M: int, meta) -> tuple:
