@@ -37,7 +37,9 @@ int dsv41_arch(void);
  * smallest M whose MXFP8-input projections run on the tcgen05 dense kernel; "pdl" 1/0
  * (DSV41_PDL) programmatic dependent launch; "fused_allreduce" 1/0 (DSV41_FUSED_AR) K2's two
  * TP all-reduces fused into the kernels producing their partials, or the standalone exchange
- * kernel after each; "attn_bulk" 0/1 (DSV41_ATTN_BULK) the tcgen05 attention's producer
+ * kernel after each; "k1_persistent" 0/1 (DSV41_K1_PERSISTENT) K1 as one persistent launch
+ * when M is below "dense_min_m" (its six stages separated by grid barriers), or its launch
+ * sequence (default); "attn_bulk" 0/1 (DSV41_ATTN_BULK) the tcgen05 attention's producer
  * gathering each key tile's records into registers (default; "attn_pair" then chooses pair or
  * lone CTAs), or staging them in shared memory by bulk copies (lone CTAs). Takes effect at the
  * next launch; DSV41_EINVAL for an unknown name or value. No counterpart in the reference (its variants are build keys). */

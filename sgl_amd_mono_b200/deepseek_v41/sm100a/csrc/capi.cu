@@ -9,6 +9,7 @@
 #include <atomic>
 #include <cmath>
 #include <map>
+#include <tuple>
 #include <mutex>
 #include <cstdlib>
 
@@ -21,6 +22,7 @@
 #include "gemv.cuh"
 #include "gemv_entry.cuh"
 #include "index_query.cuh"
+#include "k1_persistent.cuh"
 #include "k2i.cuh"
 #include "lmhead.cuh"
 #include "moe.cuh"
@@ -84,8 +86,9 @@ Option g_options[] = {
     {"pdl", "DSV41_PDL", 1, {0}, {false}},
     {"attn_bulk", "DSV41_ATTN_BULK", 0, {0}, {false}},
     {"fused_allreduce", "DSV41_FUSED_AR", 1, {0}, {false}},
+    {"k1_persistent", "DSV41_K1_PERSISTENT", 0, {0}, {false}},
 };
-enum { kOptAttnTc, kOptAttnPair, kOptDenseMinM, kOptPdl, kOptAttnBulk, kOptFusedAr };
+enum { kOptAttnTc, kOptAttnPair, kOptDenseMinM, kOptPdl, kOptAttnBulk, kOptFusedAr, kOptK1Persistent };
 
 int64_t option(int i) {
   Option& o = g_options[i];
@@ -97,7 +100,7 @@ int64_t option(int i) {
       if (const char* e = getenv(o.env)) {
         if (i == kOptAttnTc) v = e[0] == 'm' ? 0 : 1;
         else if (i == kOptDenseMinM) v = std::max(1, atoi(e));
-        else if (i == kOptAttnBulk) v = e[0] == '1' ? 1 : 0;
+        else if (i == kOptAttnBulk || i == kOptK1Persistent) v = e[0] == '1' ? 1 : 0;
         else v = e[0] == '0' ? 0 : 1;
       }
       o.value.store(v, std::memory_order_relaxed);
@@ -116,6 +119,34 @@ bool use_attn_bulk() { return option(kOptAttnBulk) == 1; }
 // MoE combine) as LL peer stores (1, default), or the standalone exchange kernel after each (0;
 // DSV41_FUSED_AR=0).
 bool use_fused_allreduce() { return option(kOptFusedAr) == 1; }
+// K1 as one persistent launch when both its projections run on the CUDA-core GEMV (M below
+// dense_min_rows) (1; DSV41_K1_PERSISTENT=1), or its seven launches (0, default). Measured at
+// config 2 (CUDA-graph replay): K1 47-50 us persistent against 42 us for the seven launches
+// chained by programmatic dependent launch, and the layer 24 us slower at M = 1 -- the five grid
+// barriers cost what the launch boundaries did, and the resident grid keeps K2's first kernel
+// from starting its prologue early.
+bool use_k1_persistent() { return option(kOptK1Persistent) == 1; }
+
+// CTAs of the persistent K1 an SM can hold (0: none fit), a cache per (NT, shared memory).
+int k1p_blocks_per_sm(int nt, int smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int>, int> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_tuple(dev, nt, smem);
+  auto it = done.find(key);
+  if (it != done.end()) return it->second;
+  const void* k = nt == 1 ? reinterpret_cast<const void*>(k1_persistent_kernel<1>)
+                          : reinterpret_cast<const void*>(k1_persistent_kernel<2>);
+  int n = 0;
+  if (ensure_smem(k, smem) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, 256, smem) != cudaSuccess)
+    n = 0;
+  cudaGetLastError();
+  done[key] = std::min(n, 2);
+  return done[key];
+}
 
 int launch_status() {
   cudaError_t e = cudaGetLastError();
@@ -350,6 +381,7 @@ int k1_run(const Dsv41K1Args* a, cudaStream_t st, bool go, int64_t* need) {
   const int QKV = QL + D;
   const int sms = sm_count();
   Carver c{go ? ptr<uint8_t>(a->scratch) : nullptr};
+  auto* k1p_bar = c.take<unsigned>(64);  // the persistent launch's grid-barrier word
   auto* lin = c.take<__nv_bfloat16>((int64_t)M * H);
   auto* part = c.take<float>((int64_t)M * (H / 32) * kPart);
   auto* xq = c.take<__nv_bfloat16>((int64_t)M * H);
@@ -384,12 +416,6 @@ int k1_run(const Dsv41K1Args* a, cudaStream_t st, bool go, int64_t* need) {
   s.norm_w = ptr<const __nv_bfloat16>(a->norm_w);
   s.res_out = res_out; s.pre_out = pre_out; s.post_out = post_out; s.comb_out = comb_out;
   s.normed = normed; s.x8 = x8; s.x8s = x8s; s.xq = xq; s.lin = lin; s.part = part;
-  mark(a->events, 0, st);
-  DSV41_TRY(launch(seam_slice_kernel, dim3(H / kSliceCols), dim3(256), 0, st, s));
-  DSV41_TRY(launch(seam_gate_norm_kernel, dim3(M), dim3(256), 0, st, s));
-  mark(a->events, 1, st);
-  DSV41_TRY(dense_go(g1, x8, x8s, st));
-  mark(a->events, 2, st);
   FrontArgs f = {};
   f.M = M; f.QL = QL; f.KVD = D; f.nope = nope; f.rope = rope; f.kslices = g1.kslices;
   f.index = (int)a->index; f.qkv_part = g1.out;
@@ -399,26 +425,53 @@ int k1_run(const Dsv41K1Args* a, cudaStream_t st, bool go, int64_t* need) {
   f.page_stride = a->page_stride; f.blk = (int)a->blk;
   f.qr = ptr<__nv_bfloat16>(a->qr); f.qx8 = qx8; f.qx8s = qx8s; f.qxq = qxq;
   f.qkv_out = ptr<float>(a->qkv_out);
-  DSV41_TRY(launch(front_qkv_kernel, dim3(M), dim3(256), 0, st, f));
-  if (a->build_kt) {
-    KeyTableArgs k = {};
-    k.M = M; k.swa_width = (int)a->swa_width; k.topk_width = (int)a->topk_width;
-    k.slot = ptr<const int64_t>(a->slot); k.swa_idx = ptr<const int32_t>(a->swa_idx);
-    k.swa_lens = ptr<const int32_t>(a->swa_lens); k.topk = ptr<const int32_t>(a->topk_idx);
-    k.topk_lens = ptr<const int32_t>(a->topk_lens); k.kt = ptr<int32_t>(a->kt);
-    k.klen = ptr<int32_t>(a->klen);
-    const int kt_keys = (int)(a->swa_width + a->topk_width);
-    DSV41_TRY(launch(key_table_kernel, dim3(M, std::max(1, std::min(cdiv(kt_keys, 1024), 16))), dim3(256), 0,
-                     st, k));
-  }
-  mark(a->events, 3, st);
-  DSV41_TRY(dense_go(g2, qx8, qx8s, st));
+  KeyTableArgs k = {};
+  k.M = M; k.swa_width = (int)a->swa_width; k.topk_width = (int)a->topk_width;
+  k.slot = ptr<const int64_t>(a->slot); k.swa_idx = ptr<const int32_t>(a->swa_idx);
+  k.swa_lens = ptr<const int32_t>(a->swa_lens); k.topk = ptr<const int32_t>(a->topk_idx);
+  k.topk_lens = ptr<const int32_t>(a->topk_lens); k.kt = ptr<int32_t>(a->kt);
+  k.klen = ptr<int32_t>(a->klen);
+  const int kt_keys = (int)(a->swa_width + a->topk_width);
+  const int kt_y = std::max(1, std::min(cdiv(kt_keys, 1024), 16));
   QRopeArgs qr = {};
   qr.M = M; qr.heads = heads; qr.D = D; qr.nope = nope; qr.rope = rope; qr.kslices = g2.kslices;
   qr.part = g2.out; qr.cos_sin = ptr<const float>(a->cos_sin); qr.pos = ptr<const int64_t>(a->pos);
   qr.rope_rows = a->rope_rows;
   qr.q = ptr<__nv_bfloat16>(a->q);
-  DSV41_TRY(launch(q_rope_kernel, dim3(cdiv(heads * D / 8, 256), M), dim3(256), 0, st, qr));
+  const int qr_x = cdiv(heads * D / 8, 256);
+
+  // ---- the persistent K1 (both projections on the CUDA-core GEMV)
+  const int nt = cdiv(M, 8);
+  const int p_smem = std::max(kSeamSliceSmem, std::max(gemv_smem_bytes(M, g1.ks_blocks), gemv_smem_bytes(M, g2.ks_blocks)));
+  const int p_bps = use_k1_persistent() && !dense_eligible(g1) && !dense_eligible(g2) && nt <= 2
+                        ? k1p_blocks_per_sm(nt, p_smem) : 0;
+  if (p_bps > 0) {
+    K1PArgs kp = {};
+    kp.s = s; kp.k = k; kp.kt_rows = a->build_kt ? M : 0; kp.kt_y = kt_y;
+    kp.g1 = g1; kp.f = f; kp.g2 = g2; kp.qr = qr; kp.qr_x = qr_x; kp.bar = k1p_bar;
+    const bool aligned = reinterpret_cast<uintptr_t>(g1.w) % 16 == 0 && reinterpret_cast<uintptr_t>(g2.w) % 16 == 0;
+    kp.pf[0] = aligned ? g1.w : nullptr; kp.pf_bytes[0] = (int64_t)QKV * H;
+    kp.pf[1] = aligned ? g2.w : nullptr; kp.pf_bytes[1] = (int64_t)heads * D * QL;
+    mark(a->events, 0, st);
+    DSV41_TRY(cudaMemsetAsync(k1p_bar, 0, 4, st));
+    const dim3 grid(p_bps * sms), block(256);
+    DSV41_TRY(nt == 1 ? launch(k1_persistent_kernel<1>, grid, block, p_smem, st, kp)
+                      : launch(k1_persistent_kernel<2>, grid, block, p_smem, st, kp));
+    for (int i = 1; i <= 4; ++i) mark(a->events, i, st);
+    return launch_status();
+  }
+
+  mark(a->events, 0, st);
+  DSV41_TRY(launch(seam_slice_kernel, dim3(H / kSliceCols), dim3(256), 0, st, s));
+  DSV41_TRY(launch(seam_gate_norm_kernel, dim3(M), dim3(256), 0, st, s));
+  mark(a->events, 1, st);
+  DSV41_TRY(dense_go(g1, x8, x8s, st));
+  mark(a->events, 2, st);
+  DSV41_TRY(launch(front_qkv_kernel, dim3(M), dim3(256), 0, st, f));
+  if (a->build_kt) DSV41_TRY(launch(key_table_kernel, dim3(M, kt_y), dim3(256), 0, st, k));
+  mark(a->events, 3, st);
+  DSV41_TRY(dense_go(g2, qx8, qx8s, st));
+  DSV41_TRY(launch(q_rope_kernel, dim3(qr_x, M), dim3(256), 0, st, qr));
   mark(a->events, 4, st);
   return launch_status();
 }

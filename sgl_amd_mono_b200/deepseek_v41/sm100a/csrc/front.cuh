@@ -30,15 +30,15 @@ struct FrontArgs {
 
 // A record: nope e4m3 bytes, rope bf16, then (in the page's scale rows) nope/64 E8M0 codes in
 // an 8-byte slot. Page layout: blk data rows of (nope + 2 rope) bytes, then blk scale rows.
-__global__ void __launch_bounds__(256) front_qkv_kernel(const FrontArgs a) {
+// Row t (a CTA of 256 threads).
+__device__ __forceinline__ void front_qkv_body(const FrontArgs& a, int t) {
   __shared__ float red[8];
   __shared__ float tot_q;
   __shared__ double ssk[2];
   __shared__ float bmax[2][8];
   __shared__ int codes[8];
-  const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int W = a.QL + a.KVD;
-  pdl_wait();
   // the wqkv_a partials of this thread's values summed over the K slices in order, four slices'
   // loads in flight at a time: q values tid qper + i (qper = QL / 256 <= 4), kv values
   // QL + tid + 64 r (threads tid < 64, r < R <= 12)
@@ -176,6 +176,11 @@ __global__ void __launch_bounds__(256) front_qkv_kernel(const FrontArgs a) {
     }
     if (tid < a.nope / 64) page[(size_t)a.blk * data + (size_t)off * 8 + tid] = (uint8_t)codes[tid];
   }
+}
+
+__global__ void __launch_bounds__(256) front_qkv_kernel(const FrontArgs a) {
+  pdl_wait();
+  front_qkv_body(a, blockIdx.x);
   pdl_launch();
 }
 
@@ -190,11 +195,10 @@ struct QRopeArgs {
 
 // q = bf16(wq_b partials summed); GPT-J RoPE of each head's dims past nope; bf16. A thread = 8
 // consecutive dims (never across a head or the nope boundary: D and nope are multiples of 8).
-__global__ void q_rope_kernel(const QRopeArgs a) {
-  pdl_wait();
-  const int t = blockIdx.y;
+// Block bx of gx along the row's dims, of row t.
+__device__ __forceinline__ void q_rope_body(const QRopeArgs& a, int bx, int gx, int t) {
   const int N = a.heads * a.D;
-  for (int g8 = blockIdx.x * blockDim.x + threadIdx.x; g8 < N / 8; g8 += gridDim.x * blockDim.x) {
+  for (int g8 = bx * blockDim.x + threadIdx.x; g8 < N / 8; g8 += gx * blockDim.x) {
     const int n = 8 * g8;
     float v[8];
     sum_slices8(a.part + (size_t)t * N + n, (size_t)a.M * N, a.kslices, v);
@@ -216,6 +220,11 @@ __global__ void q_rope_kernel(const QRopeArgs a) {
     *reinterpret_cast<uint4*>(a.q + (size_t)t * N + n) =
         make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
   }
+}
+
+__global__ void q_rope_kernel(const QRopeArgs a) {
+  pdl_wait();
+  q_rope_body(a, blockIdx.x, gridDim.x, blockIdx.y);
   pdl_launch();
 }
 
@@ -232,15 +241,14 @@ struct KeyTableArgs {
 
 // K2's key table (front.py:117-143): slot | 1 << 31 for the first ntopk keys (compressed
 // rows), window slots for k in [ntopk, kv_len), -1 past them or for an invalid slot.
-__global__ void key_table_kernel(const KeyTableArgs a) {
-  pdl_wait();
-  const int t = blockIdx.x;
+// Row t, block by of gy along its keys.
+__device__ __forceinline__ void key_table_body(const KeyTableArgs& a, int t, int by, int gy) {
   const bool live = a.slot[t] >= 0;
   const int nswa = live ? min(a.swa_lens[t], a.swa_width) : 0;
   const int ntopk = (live && a.topk_width > 0) ? min(a.topk_lens[t], a.topk_width) : 0;
   const int kv = ntopk + nswa;
   const int keys = a.topk_width + a.swa_width;
-  for (int k = blockIdx.y * blockDim.x + threadIdx.x; k < keys; k += gridDim.y * blockDim.x) {
+  for (int k = by * blockDim.x + threadIdx.x; k < keys; k += gy * blockDim.x) {
     int v = -1;
     if (k < ntopk) {
       const int c = a.topk[(size_t)t * a.topk_width + k];
@@ -251,10 +259,15 @@ __global__ void key_table_kernel(const KeyTableArgs a) {
     }
     a.kt[(size_t)t * keys + k] = v;
   }
-  if (threadIdx.x == 0 && blockIdx.y == 0) {
+  if (threadIdx.x == 0 && by == 0) {
     a.klen[t] = kv;
     a.klen[a.M + t] = ntopk;
   }
+}
+
+__global__ void key_table_kernel(const KeyTableArgs a) {
+  pdl_wait();
+  key_table_body(a, blockIdx.x, blockIdx.y, gridDim.y);
   pdl_launch();
 }
 

@@ -96,12 +96,14 @@ inline GemvArgs gemv_plan(const uint8_t* w, const uint8_t* codes, const __nv_bfl
   return a;
 }
 
+// Work item blk (K slice, row group) of a planned GEMV, by a CTA of 256 threads with
+// gemv_smem_bytes of shared memory. The launch (gemv_fp8_kernel) waits for its inputs after the
+// first weight loads (wait = true); the persistent K1 has waited already.
 template <int NT>
-__global__ void __launch_bounds__(256, 2) gemv_fp8_kernel(const GemvArgs a) {
-  extern __shared__ __align__(16) uint8_t smem[];
+__device__ __forceinline__ void gemv_body(const GemvArgs& a, int blk, uint8_t* smem, bool wait) {
   constexpr int MP = 8 * NT;
-  const int ks = blockIdx.x % a.kslices;
-  const int rg = blockIdx.x / a.kslices;
+  const int ks = blk % a.kslices;
+  const int rg = blk / a.kslices;
   const int nblocks = a.K / 128;
   const int kb0 = ks * a.ks_blocks;
   const int kb1 = min(kb0 + a.ks_blocks, nblocks);
@@ -144,7 +146,7 @@ __global__ void __launch_bounds__(256, 2) gemv_fp8_kernel(const GemvArgs a) {
       }
   }
 
-  pdl_wait();
+  if (wait) pdl_wait();
   // ---- stage x's K slice, permuted into mma slot order and scaled by 2^64
   {
     const int xg = (tile0 * 16) / a.x_group_rows;
@@ -274,6 +276,12 @@ __global__ void __launch_bounds__(256, 2) gemv_fp8_kernel(const GemvArgs a) {
       asm volatile("bar.sync %0, %1;" ::"r"(1 + wt), "r"(wk * 32));
     }
   }
+}
+
+template <int NT>
+__global__ void __launch_bounds__(256, 2) gemv_fp8_kernel(const GemvArgs a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  gemv_body<NT>(a, blockIdx.x, smem, true);
   pdl_launch();
 }
 

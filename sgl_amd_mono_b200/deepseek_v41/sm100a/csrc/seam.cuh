@@ -48,10 +48,15 @@ struct SeamArgs {
   float* part;              // [M, H / 32, 25]
 };
 
-__global__ void __launch_bounds__(256) seam_slice_kernel(const SeamArgs a) {
-  __shared__ float fn[kMix * kHC * kSliceCols];   // this slice's mix weights
-  __shared__ float rs[48 * kHC * kSliceCols];     // R_new of every row (bf16-valued)
-  const int s = blockIdx.x, c0 = s * kSliceCols, H = a.H;
+constexpr int kSeamSliceSmem = (kMix + 48) * kHC * kSliceCols * 4;  // a slice's mix weights, R_new of every row
+
+// One 32-column slice s of every row (a CTA of 256 threads; smem: kSeamSliceSmem bytes). The
+// launch (seam_slice_kernel) waits for its inputs between the mix-weight loads and the rest
+// (wait = true); the persistent K1 has waited already.
+__device__ __forceinline__ void seam_slice_body(const SeamArgs& a, int s, float* smem, bool wait) {
+  float* fn = smem;                               // this slice's mix weights
+  float* rs = smem + kMix * kHC * kSliceCols;     // R_new of every row (bf16-valued)
+  const int c0 = s * kSliceCols, H = a.H;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // mix weights first: they wait on nothing
   for (int e = tid; e < kMix * kHC * kSliceCols; e += blockDim.x) {
@@ -59,7 +64,7 @@ __global__ void __launch_bounds__(256) seam_slice_kernel(const SeamArgs a) {
               c = r % kSliceCols;
     fn[e] = __ldg(a.hc_fn + (size_t)j * kHC * H + (size_t)o * H + c0 + c);
   }
-  pdl_wait();
+  if (wait) pdl_wait();
   // R_new of (row t, column c) and the collapsed layer input: one thread an element, its loads
   // before any store
 #pragma unroll 2
@@ -121,6 +126,11 @@ __global__ void __launch_bounds__(256) seam_slice_kernel(const SeamArgs a) {
     const float sum = warp_transpose_sum(v, lane);
     if (lane < kPart) a.part[((size_t)t * nslices + s) * kPart + lane] = sum;
   }
+}
+
+__global__ void __launch_bounds__(256) seam_slice_kernel(const SeamArgs a) {
+  __shared__ float smem[kSeamSliceSmem / 4];
+  seam_slice_body(a, blockIdx.x, smem, true);
   pdl_launch();
 }
 
@@ -153,12 +163,12 @@ __device__ __forceinline__ void mx_group_store(const float (&v)[8], bool vllm, u
   if (deq) *reinterpret_cast<uint4*>(deq + col) = make_uint4(d[0], d[1], d[2], d[3]);
 }
 
-__global__ void __launch_bounds__(256) seam_gate_norm_kernel(const SeamArgs a) {
+// Row t's gates and norm (a CTA of 256 threads).
+__device__ __forceinline__ void seam_gate_norm_body(const SeamArgs& a, int t) {
   __shared__ double red[8];
   __shared__ float tot_s;
   __shared__ float gsum[8][kPart];
-  const int t = blockIdx.x, H = a.H, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  pdl_wait();
+  const int H = a.H, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // ---- gate: the slices' partials summed in slice order (warp w: a contiguous eighth of the
   // slices, then the eight warp sums in warp order), then one warp computes the gates
   {
@@ -261,6 +271,11 @@ __global__ void __launch_bounds__(256) seam_gate_norm_kernel(const SeamArgs a) {
     if (a.aiter)
       mx_group_store(y, false, a.x8r + (size_t)t * H, a.x8rs + (size_t)t * (H / 32), nullptr, c);
   }
+}
+
+__global__ void __launch_bounds__(256) seam_gate_norm_kernel(const SeamArgs a) {
+  pdl_wait();
+  seam_gate_norm_body(a, blockIdx.x);
   pdl_launch();
 }
 

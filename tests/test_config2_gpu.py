@@ -171,3 +171,27 @@ def test_config2_stages(layer2, M):
     mo = B["out"].float()
     c("moe cos/rel", cos(mo, moe) > 0.9999 and rel(mo, moe) < 0.015, (cos(mo, moe), rel(mo, moe)))
     c.done()
+
+
+@pytest.mark.parametrize("M", [1, 8, 15])
+def test_k1_persistent_equals_launch_sequence(layer2, M):
+    """K1 as one persistent launch (M below the tcgen05 dense threshold) against K1's seven
+    launches: every output bit for bit (the same stage functions, in the same order)."""
+    from sgl_amd_mono_b200.common import ext
+    from sgl_amd_mono_b200.deepseek_v41 import synth
+    s, r, L, W = layer2
+    step = synth.make_step(s, M, CTX, 700 + M, DEV)
+    cache0 = step["cache"].clone()
+    keys = ("res1", "post_a", "comb_a", "pre_a", "normed_a", "x8", "x8s", "qkv", "q", "qx8", "qx8s", "kt", "klen")
+    outs = {}
+    for persistent in (1, 0):
+        ext.set_option("k1_persistent", persistent)
+        step["cache"].copy_(cache0)
+        b = r.k1(L, step, M)
+        torch.cuda.synchronize()
+        outs[persistent] = {k: b[k].clone() for k in keys}
+        outs[persistent]["cache"] = step["cache"].clone()
+    ext.set_option("k1_persistent", 0)
+    assert ext.lib().dsv41_device_error() == 0
+    for k in keys + ("cache",):
+        assert torch.equal(outs[1][k], outs[0][k]), k
