@@ -13,8 +13,11 @@
 //
 // Work item = (K slice, group of 256-row tiles); CTAs loop over items (persistent, one an SM).
 // Roles and pipelines as the routed experts' kernel: warp 0 copies (lane 0 issues, the warp
-// writes the scale atoms), warp 1 issues the MMAs, warps 2-5 stage the item's activations and
-// drain the accumulator. Output: fp32 partials out[kslice][m][n], summed over K slices in order by
+// writes the scale atoms), warp 1 issues the MMAs, warps 2-5 stage the item's activations. The
+// M <= 48 tokens sit in accumulator lanes 0..47, readable by warps 0 and 1 mod 4: warps 4 and 5
+// drain columns 0..127 of lanes 0..31 and 32..63, warps 8 and 9 columns 128..255, and each
+// releases the accumulator once its columns are in registers, before its (uncoalesced, a token
+// row a lane) stores of the partials. Output: fp32 partials out[kslice][m][n], summed over K slices in order by
 // the consumer -- the contract of gemv_fp8_kernel, which it replaces for MXFP8 inputs.
 #pragma once
 
@@ -26,7 +29,7 @@
 namespace dsv41 {
 
 constexpr int kDnStages = 4;
-constexpr int kDnThreads = 192;
+constexpr int kDnThreads = 320;  // 10 warps: copies, MMA, 4 stagers, 2 idle, 2 more drainers
 constexpr int kDnMaxRows = 48;
 constexpr int kDnKsMax = 512;  // K slice bound
 constexpr int kDnGroups = kDnMaxRows / 8;
@@ -217,90 +220,99 @@ __global__ void __launch_bounds__(kDnThreads, 1)
       mbar_wait(drain, 0, abort);
     }
   } else {
-    // ================= activation staging + accumulator drain (warps 2-5, 128 threads, deciding
-    // together through softmax_all: the AND over named barrier 1)
     pdl_wait();
-    const int et = tid - 64;
-    const int q = warp & 3;  // this warp's TMEM lanes: tokens 32 q .. 32 q + 31
-    const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
-    auto stage = [&](const DnWalk& sw, int bi) -> bool {
-      const int bb = bi & 1;
-      if (bi >= 2 && !softmax_all(mbar_wait(b_free(bb), ((bi >> 1) - 1) & 1, abort))) return false;
-      const int k0 = sw.ks * a.ks_len;
-      uint8_t* sa = smem + L::kA + bb * L::kABytes;
-      uint8_t* sf = smem + L::kSfx + bb * L::kSfxBytes;
-      const int kc_n = a.ks_len / 16;
-      for (int i = et; i < 8 * G * kc_n; i += 128) {
-        const int m = i / kc_n, kc = i % kc_n;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (m < a.M) v = ldg16(a.x + (size_t)m * a.x_ld + k0 + 16 * kc);
-        *reinterpret_cast<uint4*>(sa + ((kc >> 3) * G + (m >> 3)) * 1024 + (kc & 7) * 128 + (m & 7) * 16) = v;
-      }
-      // scale atoms, one a K step: token m at lane m % 32, word m / 32, bytes = blocks 0..3
-      for (int i = et; i < ksteps * 32; i += 128) {
-        const int s = i / 32, l = i % 32;
-        uint32_t v[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int m = l + 32 * j;
-          if (m < a.M) v[j] = *reinterpret_cast<const uint32_t*>(a.xs + (size_t)m * (a.x_ld / 32) + k0 / 32 + 4 * s);
-        }
-        *reinterpret_cast<uint4*>(sf + s * 512 + l * 16) = make_uint4(v[0], v[1], v[2], v[3]);
-      }
-      fence_async_smem();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (et == 0) mbar_arrive(b_ready(bb));
-      return true;
-    };
-    DnWalk sw = w;
-    bool s_live = sw.start(a, gridDim.x, blockIdx.x), ok = true;
-    int si = 0;
-    for (; ok && s_live && si < 2; ++si, s_live = sw.next(a)) ok = stage(sw, si);
-    int ti = 0;
-    bool live = ok && w.start(a, gridDim.x, blockIdx.x);
+    // One drain warp's columns col0 .. col0 + 127 of its 32 lanes (tokens 32 q + lane) for every
+    // tile of the current item: into registers, the accumulator released (d_empty counts the
+    // four drain warps), then the stores.
+    const int q = warp & 3;
     const int m = 32 * q + lane;  // this thread's token
-    for (int bi = 0; ok && live; live = w.next(a), ++bi) {
-      float* orow = a.out + ((size_t)w.ks * a.M + (m < a.M ? m : 0)) * a.N;
-      for (int t = w.tile_lo; t < w.tile_hi; ++t, ++ti) {
-        if (!(ok = softmax_all(mbar_wait(d_full, ti & 1, abort)))) break;
+    auto drain = [&](const DnWalk& dw, int& ti, int col0) -> bool {
+      float* orow = a.out + ((size_t)dw.ks * a.M + (m < a.M ? m : 0)) * a.N;
+      for (int t = dw.tile_lo; t < dw.tile_hi; ++t, ++ti) {
+        if (!__all_sync(0xffffffffu, mbar_wait(d_full, ti & 1, abort))) return false;
         tc_fence_after();
-        for (int h = 0; h < 2; ++h) {
-          uint32_t v[128];
-          if (32 * q < a.M) {
+        uint32_t v[128];
+        if (32 * q < a.M) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-              tmem_ld32(t_d + lane_addr + 128 * h + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * c));
-            tmem_wait_ld();
-          }
-          if (h == 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(d_empty);
-          }
-          const int row0 = 256 * t + 128 * h;
-          if (m < a.M) {
+          for (int c = 0; c < 4; ++c)
+            tmem_ld32(t_d + ((uint32_t)(32 * q) << 16) + col0 + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * c));
+          tmem_wait_ld();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(d_empty);
+        const int row0 = 256 * t + col0;
+        if (m < a.M) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int r = row0 + 4 * j;
-              if (r + 3 < a.N)
-                *reinterpret_cast<float4*>(orow + r) =
-                    make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
-                                __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
-              else {
+          for (int j = 0; j < 32; ++j) {
+            const int r = row0 + 4 * j;
+            if (r + 3 < a.N)
+              *reinterpret_cast<float4*>(orow + r) = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                                                 __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+            else {
 #pragma unroll
-                for (int e = 0; e < 4; ++e)
-                  if (r + e < a.N) orow[r + e] = __uint_as_float(v[4 * j + e]);
-              }
+              for (int e = 0; e < 4; ++e)
+                if (r + e < a.N) orow[r + e] = __uint_as_float(v[4 * j + e]);
             }
           }
         }
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (ok && s_live) {
-        ok = stage(sw, si);
-        ++si;
-        s_live = sw.next(a);
+      return true;
+    };
+    if (warp < 6) {
+      // ================= activation staging (warps 2-5, 128 threads, deciding together through
+      // softmax_all: the AND over named barrier 1); warps 4 and 5 also drain columns 0..127
+      const int et = tid - 64;
+      auto stage = [&](const DnWalk& sw, int bi) -> bool {
+        const int bb = bi & 1;
+        if (bi >= 2 && !softmax_all(mbar_wait(b_free(bb), ((bi >> 1) - 1) & 1, abort))) return false;
+        const int k0 = sw.ks * a.ks_len;
+        uint8_t* sa = smem + L::kA + bb * L::kABytes;
+        uint8_t* sf = smem + L::kSfx + bb * L::kSfxBytes;
+        const int kc_n = a.ks_len / 16;
+        for (int i = et; i < 8 * G * kc_n; i += 128) {
+          const int mm = i / kc_n, kc = i % kc_n;
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (mm < a.M) v = ldg16(a.x + (size_t)mm * a.x_ld + k0 + 16 * kc);
+          *reinterpret_cast<uint4*>(sa + ((kc >> 3) * G + (mm >> 3)) * 1024 + (kc & 7) * 128 + (mm & 7) * 16) = v;
+        }
+        // scale atoms, one a K step: token m at lane m % 32, word m / 32, bytes = blocks 0..3
+        for (int i = et; i < ksteps * 32; i += 128) {
+          const int s = i / 32, l = i % 32;
+          uint32_t v[4] = {0, 0, 0, 0};
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int mm = l + 32 * j;
+            if (mm < a.M) v[j] = *reinterpret_cast<const uint32_t*>(a.xs + (size_t)mm * (a.x_ld / 32) + k0 / 32 + 4 * s);
+          }
+          *reinterpret_cast<uint4*>(sf + s * 512 + l * 16) = make_uint4(v[0], v[1], v[2], v[3]);
+        }
+        fence_async_smem();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (et == 0) mbar_arrive(b_ready(bb));
+        return true;
+      };
+      DnWalk sw = w;
+      bool s_live = sw.start(a, gridDim.x, blockIdx.x), ok = true;
+      int si = 0;
+      for (; ok && s_live && si < 2; ++si, s_live = sw.next(a)) ok = stage(sw, si);
+      int ti = 0;
+      bool live = ok && w.start(a, gridDim.x, blockIdx.x);
+      for (int bi = 0; ok && live; live = w.next(a), ++bi) {
+        if (warp >= 4) ok = drain(w, ti, 0);
+        // the item two ahead reuses this item's activation buffers (b_free)
+        ok = softmax_all(ok);
+        if (ok && s_live) {
+          ok = stage(sw, si);
+          ++si;
+          s_live = sw.next(a);
+        }
       }
+    } else if (warp >= 8) {
+      // ================= the drain's other half (columns 128..255)
+      int ti = 0;
+      bool ok = true;
+      for (bool live = w.start(a, gridDim.x, blockIdx.x); ok && live; live = w.next(a)) ok = drain(w, ti, 128);
     }
   }
   // ---- teardown

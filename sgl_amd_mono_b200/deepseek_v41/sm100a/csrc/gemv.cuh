@@ -179,11 +179,28 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, int blk, uint8_t* s
   // ldmatrix row address of this lane: token (lane & 7) of the n-tile, 8 slots at 8 * (lane >> 3)
   const uint32_t lm_off = ((lane & 7) * xs_ld + 8 * (lane >> 3)) * 2;
 
+  // The next row tile's first PF steps are loaded during this tile's last PF steps (when the
+  // steps divide evenly into load slots), so a warp's loads do not drain at tile boundaries. The
+  // warp's E8M0 codes of a tile (one a 128-K block, at most 64) are loaded one a lane with the
+  // tile's first weights (the next tile's with its first cross-tile loads) and read by shuffles.
+  // Token tiles past 2 (M > 16) keep the per-tile loads: their accumulators need the registers.
+  constexpr bool kX = NT <= 2;
+  const bool xt = kX && nsteps % PF == 0;
+  const int ncodes = kX ? kw1 - kw0 : 65;
+  auto codes_of = [&](int it, uint32_t& c0, uint32_t& c1) {
+    const uint8_t* cp = a.codes + (size_t)(((tile0 + wt + it * lanes) * 16) >> 7) * nblocks + kb0 + kw0;
+    c0 = lane < ncodes ? __ldg(cp + lane) : 0u;
+    c1 = 32 + lane < ncodes ? __ldg(cp + 32 + lane) : 0u;
+  };
+  uint32_t cc0 = 0, cc1 = 0, cn0 = 0, cn1 = 0;
+  if (ntiles_local > 0 && ncodes <= 64) codes_of(0, cc0, cc1);
   for (int it = 0; it < ntiles_local; ++it) {
     const int tile = tile0 + wt + it * lanes;
     const int row0 = tile * 16;
-    const uint8_t *p0, *p1;
+    const uint8_t *p0, *p1, *q0 = nullptr, *q1 = nullptr;
     tile_ptrs(it, p0, p1);
+    const bool pf_next = xt && it + 1 < ntiles_local;
+    if (pf_next) tile_ptrs(it + 1, q0, q1);
     const uint8_t* cp = a.codes + (size_t)(row0 >> 7) * nblocks + kb0 + kw0;
     float acc[NT][4];
     float blk[NT][4];
@@ -192,7 +209,7 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, int blk, uint8_t* s
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[n][i] = blk[n][i] = 0.f;
 
-    if (it > 0) {
+    if (it > 0 && !xt) {
 #pragma unroll
       for (int i = 0; i < PF; ++i)
         if (i < nsteps) {
@@ -209,6 +226,11 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, int blk, uint8_t* s
           if (st + PF < nsteps) {
             wa[i] = ldg_stream(p0 + 64 * (st + PF));
             wb[i] = ldg_stream(p1 + 64 * (st + PF));
+          } else if (pf_next) {
+            // (st + PF - nsteps) % PF == i: the next tile's step lands in this slot
+            wa[i] = ldg_stream(q0 + 64 * (st + PF - nsteps));
+            wb[i] = ldg_stream(q1 + 64 * (st + PF - nsteps));
+            if (st + PF == nsteps && ncodes <= 64) codes_of(it + 1, cn0, cn1);
           }
           const uint32_t aw[4] = {A.x, A.y, A.z, A.w};
           const uint32_t bw[4] = {B.x, B.y, B.z, B.w};
@@ -230,7 +252,10 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, int blk, uint8_t* s
             }
           }
           if (st & 1) {
-            const float sc = pow2c(__ldg(cp + (st >> 1))) * 72057594037927936.0f;  // * 2^56
+            const int b = st >> 1;
+            const uint32_t code = ncodes > 64 ? (uint32_t)__ldg(cp + b)
+                                  : __shfl_sync(0xffffffffu, b < 32 ? cc0 : cc1, b & 31);
+            const float sc = pow2c((int)code) * 72057594037927936.0f;  // * 2^56
 #pragma unroll
             for (int n = 0; n < NT; ++n)
 #pragma unroll
@@ -240,6 +265,14 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, int blk, uint8_t* s
               }
           }
         }
+      }
+    }
+    if (ncodes <= 64) {
+      if (pf_next) {
+        cc0 = cn0;
+        cc1 = cn1;
+      } else if (it + 1 < ntiles_local) {
+        codes_of(it + 1, cc0, cc1);
       }
     }
     // ---- K lanes: reduce in lane order through shared memory, then store

@@ -21,8 +21,11 @@
 // sub-partitions (weight row n -> lane n % 32, column n / 32, byte = the K block).
 //
 // CTA (persistent, one an SM): warp 0 issues the copies (one thread), warp 1 allocates TMEM and
-// issues the MMAs (one thread), warps 2-5 stage each pick batch's activations and scale atoms and
-// drain the accumulator (warp w holds picks 32 (w % 4) .. of it). Work item = (expert of the
+// issues the MMAs (one thread), warps 2-5 stage each pick batch's activations and scale atoms.
+// A batch's picks sit in accumulator lanes 0..31, which only warps whose index is 0 mod 4 can
+// read: warp 4 drains columns 0..127 and warp 8 columns 128..255, side by side, and each frees
+// the accumulator once its columns are in registers -- the stores to the partials (one pick row a
+// lane, so uncoalesced) come after. Work item = (expert of the
 // union, K slice, group of 256-row tiles); a batch = up to 32 of the expert's picks. Pipelines: a
 // 4-stage weight ring (full: TMA transaction bytes; empty: MMA commit), two activation buffers
 // (ready: the stagers; free: MMA commit), one accumulator (256 columns; full: MMA commit; empty:
@@ -39,7 +42,7 @@ namespace dsv41 {
 
 constexpr int kMxStages = 4;
 constexpr int kMxRows = 256;     // weight rows a tile (N of the MMA)
-constexpr int kMxThreads = 192;
+constexpr int kMxThreads = 288;  // 9 warps: copies, MMA, 4 stagers, 2 idle, the second drainer
 constexpr int kMxMaxPicks = 32;
 constexpr int kMxKsMax = 1024;   // K slice bound (activation staging bytes a pick)
 
@@ -188,7 +191,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       mbar_init(b_free(i), 1);
     }
     mbar_init(d_full, 1);
-    mbar_init(d_empty, 4);
+    mbar_init(d_empty, 2);  // the two drain warps
     mbar_init(drain, 1);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -280,99 +283,101 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       mbar_wait(drain, 0, abort);
     }
   } else {
-    // ================= activation staging + accumulator drain (warps 2-5, 128 threads)
-    // (the 128 threads decide together -- softmax_all is the AND over named barrier 1 -- so none
-    // leaves while the others wait at a barrier)
-    const int et = tid - 64;
-    const int q = warp & 3;  // this warp's TMEM lanes: picks 32 q .. 32 q + 31
-    const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
     const int P = a.M * a.topk;
-    auto stage = [&](const MxWalk& sw, int bi) -> bool {
-      const int bb = bi & 1;
-      if (bi >= 2 && !softmax_all(mbar_wait(b_free(bb), ((bi >> 1) - 1) & 1, abort))) return false;
-      const int np = sw.np(), G = mx_groups(np);
-      const int k0 = sw.ks * a.ks_len;
-      int* pk = s_picks + bb * kMxMaxPicks;
-      uint8_t* sa = smem + L::kA + bb * L::kABytes;
-      uint8_t* sf = smem + L::kSfx + bb * L::kSfxBytes;
-      if (et < kMxMaxPicks) pk[et] = et < np ? a.picks[sw.p0 + sw.pb + et] : 0;
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      // A: [K step][group][8 chunks of 16 K][8 rows x 16 B]
-      const int kc_n = a.ks_len / 16;
-      for (int i = et; i < 8 * G * kc_n; i += 128) {
-        const int n = i / kc_n, kc = i % kc_n;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (n < np) {
-          const int row = a.x_by_pick ? pk[n] : pk[n] / a.topk;
-          v = ldg16(a.x + (size_t)row * a.K + k0 + 16 * kc);
+    // One drain warp's columns col0 .. col0 + 127 of every tile of the walk's current batch (picks
+    // in lanes 0..31, lane = pick slot): into registers, the accumulator released (d_empty counts
+    // both drain warps), then the uncoalesced stores of each pick's row of partials. The pick
+    // index comes from the routing plan in global memory (the stagers' shared copy may not be
+    // written yet when warp 8 starts a batch).
+    auto drain = [&](const MxWalk& dw, int& ti, int col0) -> bool {
+      const int np = dw.np();
+      const bool mine = lane < np;
+      float* orow = a.out + ((size_t)dw.ks * P + (mine ? a.picks[dw.p0 + dw.pb + lane] : 0)) * a.N;
+      for (int t = dw.tile_lo; t < dw.tile_hi; ++t, ++ti) {
+        if (!__all_sync(0xffffffffu, mbar_wait(d_full, ti & 1, abort))) return false;
+        tc_fence_after();
+        uint32_t v[128];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(t_d + col0 + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * c));
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(d_empty);
+        const int row0 = kMxRows * t + col0;
+        if (mine) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int r = row0 + 4 * j;
+            if (r + 3 < a.N)
+              *reinterpret_cast<float4*>(orow + r) = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                                                 __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+          }
         }
-        *reinterpret_cast<uint4*>(sa + ((kc >> 3) * G + (n >> 3)) * 1024 + (kc & 7) * 128 + (n & 7) * 16) = v;
       }
-      // scale atoms, one a K step: [lane n][16 B], bytes 0..3 = the codes of blocks 0..3
-      for (int i = et; i < ksteps * 32; i += 128) {
-        const int s = i / 32, n = i % 32;
-        uint32_t v = 0;
-        if (n < np) {
-          const int row = a.x_by_pick ? pk[n] : pk[n] / a.topk;
-          v = *reinterpret_cast<const uint32_t*>(a.xs + (size_t)row * (a.K / 32) + k0 / 32 + 4 * s);
-        }
-        *reinterpret_cast<uint4*>(sf + s * 512 + n * 16) = make_uint4(v, 0, 0, 0);
-      }
-      fence_async_smem();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (et == 0) mbar_arrive(b_ready(bb));
       return true;
     };
-    MxWalk sw = w;  // the staging walk runs up to two batches ahead of the drain walk
-    bool s_live = sw.start(a, nu, gridDim.x, blockIdx.x), ok = true;
-    int si = 0;
-    for (; ok && s_live && si < 2; ++si, s_live = sw.next(a)) ok = stage(sw, si);
-    int ti = 0;
-    bool live = ok && w.start(a, nu, gridDim.x, blockIdx.x);
-    for (int bi = 0; ok && live; live = w.next(a), ++bi) {
-      const int np = w.np();
-      const int* pk = s_picks + (bi & 1) * kMxMaxPicks;
-      const int n = 32 * q + lane;  // this thread's pick slot
-      const bool mine = n < np;
-      float* orow = a.out + ((size_t)w.ks * P + (mine ? pk[n] : 0)) * a.N;
-      for (int t = w.tile_lo; t < w.tile_hi; ++t, ++ti) {
-        if (!(ok = softmax_all(mbar_wait(d_full, ti & 1, abort)))) break;
-        tc_fence_after();
-        // two halves of 128 weight rows: the accumulator is free once the second is in registers
-        for (int h = 0; h < 2; ++h) {
-          uint32_t v[128];
-          if (32 * q < np) {
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-              tmem_ld32(t_d + lane_addr + 128 * h + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * c));
-            tmem_wait_ld();
+    if (warp < 6) {
+      // ================= activation staging (warps 2-5, 128 threads) and warp 4's half of the drain
+      // (the 128 threads decide together -- softmax_all is the AND over named barrier 1 -- so none
+      // leaves while the others wait at a barrier)
+      const int et = tid - 64;
+      auto stage = [&](const MxWalk& sw, int bi) -> bool {
+        const int bb = bi & 1;
+        if (bi >= 2 && !softmax_all(mbar_wait(b_free(bb), ((bi >> 1) - 1) & 1, abort))) return false;
+        const int np = sw.np(), G = mx_groups(np);
+        const int k0 = sw.ks * a.ks_len;
+        int* pk = s_picks + bb * kMxMaxPicks;
+        uint8_t* sa = smem + L::kA + bb * L::kABytes;
+        uint8_t* sf = smem + L::kSfx + bb * L::kSfxBytes;
+        if (et < kMxMaxPicks) pk[et] = et < np ? a.picks[sw.p0 + sw.pb + et] : 0;
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        // A: [K step][group][8 chunks of 16 K][8 rows x 16 B]
+        const int kc_n = a.ks_len / 16;
+        for (int i = et; i < 8 * G * kc_n; i += 128) {
+          const int n = i / kc_n, kc = i % kc_n;
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (n < np) {
+            const int row = a.x_by_pick ? pk[n] : pk[n] / a.topk;
+            v = ldg16(a.x + (size_t)row * a.K + k0 + 16 * kc);
           }
-          if (h == 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(d_empty);
+          *reinterpret_cast<uint4*>(sa + ((kc >> 3) * G + (n >> 3)) * 1024 + (kc & 7) * 128 + (n & 7) * 16) = v;
+        }
+        // scale atoms, one a K step: [lane n][16 B], bytes 0..3 = the codes of blocks 0..3
+        for (int i = et; i < ksteps * 32; i += 128) {
+          const int s = i / 32, n = i % 32;
+          uint32_t v = 0;
+          if (n < np) {
+            const int row = a.x_by_pick ? pk[n] : pk[n] / a.topk;
+            v = *reinterpret_cast<const uint32_t*>(a.xs + (size_t)row * (a.K / 32) + k0 / 32 + 4 * s);
           }
-          const int row0 = kMxRows * t + 128 * h;
-          if (mine) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int r = row0 + 4 * j;
-              if (r + 3 < a.N)
-                *reinterpret_cast<float4*>(orow + r) =
-                    make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
-                                __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
-            }
-          }
+          *reinterpret_cast<uint4*>(sf + s * 512 + n * 16) = make_uint4(v, 0, 0, 0);
+        }
+        fence_async_smem();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (et == 0) mbar_arrive(b_ready(bb));
+        return true;
+      };
+      MxWalk sw = w;  // the staging walk runs up to two batches ahead of the drain walk
+      bool s_live = sw.start(a, nu, gridDim.x, blockIdx.x), ok = true;
+      int si = 0;
+      for (; ok && s_live && si < 2; ++si, s_live = sw.next(a)) ok = stage(sw, si);
+      int ti = 0;
+      bool live = ok && w.start(a, nu, gridDim.x, blockIdx.x);
+      for (int bi = 0; ok && live; live = w.next(a), ++bi) {
+        if (warp == 4) ok = drain(w, ti, 0);
+        // the batch two ahead reuses this batch's activation and pick buffers (b_free)
+        ok = softmax_all(ok);
+        if (ok && s_live) {
+          ok = stage(sw, si);
+          ++si;
+          s_live = sw.next(a);
         }
       }
-      // the batch two ahead reuses this batch's buffers (its MMAs are done: its last tile was
-      // drained)
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (ok && s_live) {
-        ok = stage(sw, si);
-        ++si;
-        s_live = sw.next(a);
-      }
+    } else if (warp == 8) {
+      // ================= the drain's other half (columns 128..255)
+      int ti = 0;
+      bool ok = true;
+      for (bool live = w.start(a, nu, gridDim.x, blockIdx.x); ok && live; live = w.next(a)) ok = drain(w, ti, 128);
     }
   }
   // ---- teardown
