@@ -41,7 +41,9 @@ int dsv41_arch(void);
  * when M is below "dense_min_m" (its six stages separated by grid barriers), or its launch
  * sequence (default); "attn_bulk" 0/1 (DSV41_ATTN_BULK) the tcgen05 attention's producer
  * gathering each key tile's records into registers (default; "attn_pair" then chooses pair or
- * lone CTAs), or staging them in shared memory by bulk copies (lone CTAs). Takes effect at the
+ * lone CTAs), or staging them in shared memory by bulk copies (lone CTAs); "attn_wide" 1/0
+ * (DSV41_ATTN_WIDE) a row's 64 heads in one tcgen05 attention CTA (default when a rank holds 64
+ * heads of 512 + 64 dims), or the 32-head kernels above. Takes effect at the
  * next launch; DSV41_EINVAL for an unknown name or value. No counterpart in the reference (its variants are build keys). */
 int dsv41_set_option(const char* name, int64_t value);
 

@@ -16,6 +16,7 @@
 #include "../../../../include/dsv41_b200.h"
 #include "attention.cuh"
 #include "attn_tc.cuh"
+#include "attn_wide.cuh"
 #include "common.cuh"
 #include "epilogue.cuh"
 #include "front.cuh"
@@ -87,8 +88,9 @@ Option g_options[] = {
     {"attn_bulk", "DSV41_ATTN_BULK", 0, {0}, {false}},
     {"fused_allreduce", "DSV41_FUSED_AR", 1, {0}, {false}},
     {"k1_persistent", "DSV41_K1_PERSISTENT", 0, {0}, {false}},
+    {"attn_wide", "DSV41_ATTN_WIDE", 1, {0}, {false}},
 };
-enum { kOptAttnTc, kOptAttnPair, kOptDenseMinM, kOptPdl, kOptAttnBulk, kOptFusedAr, kOptK1Persistent };
+enum { kOptAttnTc, kOptAttnPair, kOptDenseMinM, kOptPdl, kOptAttnBulk, kOptFusedAr, kOptK1Persistent, kOptAttnWide };
 
 int64_t option(int i) {
   Option& o = g_options[i];
@@ -115,6 +117,10 @@ bool use_attn_pair() { return option(kOptAttnPair) == 1; }
 int dense_min_rows() { return (int)option(kOptDenseMinM); }
 bool use_pdl() { return option(kOptPdl) == 1; }
 bool use_attn_bulk() { return option(kOptAttnBulk) == 1; }
+// A row's 64 heads in one tcgen05 attention CTA (attn_wide_kernel: N = 64 MMAs, staged records,
+// one f16 p) (1, default), or the 32-head kernels above (0; DSV41_ATTN_WIDE=0). Measured at config
+// 2, M = 48: 243 us against the CTA pair's 392 us.
+bool use_attn_wide() { return option(kOptAttnWide) == 1; }
 // TP > 1: both all-reduces fused into the kernels that produce the partials (wo_b's epilogue, the
 // MoE combine) as LL peer stores (1, default), or the standalone exchange kernel after each (0;
 // DSV41_FUSED_AR=0).
@@ -533,7 +539,8 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   // attention split plan: the tcgen05 kernel takes every head of a row (one CTA an SM in
   // total), the mma.sync kernel 16-head tiles (two CTAs an SM)
   const bool tc = use_tc_attention() && (nope == 512 || nope == 448);
-  const int head_tiles = tc ? cdiv(heads, 32) : cdiv(heads, 16);
+  const bool wide = tc && nope == 512 && heads == kWdNH && use_attn_wide();
+  const int head_tiles = wide ? 1 : tc ? cdiv(heads, 32) : cdiv(heads, 16);
   const int units = M * head_tiles;
   int nchunks = cdiv(2 * sms, units);
   const int sub = tc ? kTcKeys : kSub;  // keys a sub-block
@@ -641,7 +648,9 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   at.scale_log2 = (float)(1.0 / sqrt((double)D) * 1.4426950408889634);
   at.part_o = part_o; at.part_ml = part_ml;
   mark(a->events, 0, st);
-  if (tc) {
+  if (wide) {
+    DSV41_TRY(launch(attn_wide_kernel<512>, dim3(M * nchunks), dim3(kWdThreads), WdSmem<576>::kBytes, st, at));
+  } else if (tc) {
     AttnTcArgs ta = {at, heads >= 32 ? 32 : std::max(16, cdiv(heads, 16) * 16), head_tiles};
     // the staged producer (lone CTAs), or a row's two head tiles sharing their key tiles as a
     // CTA pair, or lone gathering CTAs

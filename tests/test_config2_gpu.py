@@ -2,7 +2,8 @@
 GPU against the CPU oracle, stage by stage.
 
 Config 2 is hidden 4096, 64 heads of 512 + 64 dims (so the tcgen05 attention runs over the
-row's two 32-head tiles, ``attn_tc_kernel<512, ...>``), q_lora 1024, 8 wo_a
+row's 64 heads in one CTA, ``attn_wide_kernel<512>``, the default, and over its two 32-head
+tiles, ``attn_tc_kernel<512, ...>``), q_lora 1024, 8 wo_a
 groups of 1024, 256 routed experts top-8 with intermediate 2048 (the expert kernel's K slices
 and row groups) and a shared expert of 2048. Rows M = 1 (the CUDA-core GEMVs), 16 and 48 (the
 tcgen05 dense projections), at KV context 1536.
@@ -13,8 +14,10 @@ gates (pre, post, comb) within 1e-6; q cos 0.99999 / rel 5e-3; the attention out
 0.9998 (and rel 1e-3) against the exact oracle attention of the GPU's own q; wo_a rel 5e-3,
 wo_b rel 1e-3; the FFN seam's gates rel 1e-4; router logits, routing ids and weights
 bit-exact; the MoE partial cos 0.9999 / rel 1.5e-2. Each stage's oracle runs on the GPU's own
-inputs to that stage. The attention's three producers -- records gathered by a CTA pair (the
-default), staged by bulk copies, or gathered by lone CTAs -- give the same bits.
+inputs to that stage. The attention's three 32-head producers -- records gathered by a CTA pair,
+staged by bulk copies, or gathered by lone CTAs -- give the same bits; the 64-head CTAs (one f16
+p instead of a head and tail) meet the same oracle bounds, and every later stage runs on their
+output.
 Every check runs and the failures are reported together.
 """
 
@@ -75,6 +78,7 @@ def layer2():
     yield s, r, L, W
     ext.set_option("attn_pair", 1)
     ext.set_option("attn_bulk", 0)
+    ext.set_option("attn_wide", 1)
 
 
 @pytest.mark.parametrize("M", [1, 16, 48])
@@ -86,12 +90,13 @@ def test_config2_stages(layer2, M):
     cache0 = step["cache"].clone()
     ext.set_option("attn_bulk", 0)
     ext.set_option("attn_pair", 1)
+    ext.set_option("attn_wide", 0)
     b = r.k1(L, step, M)
     r.k2(L, step, M, b)
     torch.cuda.synchronize()
-    B = cpu(b)
-    # the same K2 with the other producers: records staged by bulk copies, then gathered by lone
-    # CTAs
+    pair = cpu(b)
+    # the same K2 with the other 32-head producers: records staged by bulk copies, then gathered
+    # by lone CTAs
     ext.set_option("attn_bulk", 1)
     r.k2(L, step, M, b)
     torch.cuda.synchronize()
@@ -102,6 +107,13 @@ def test_config2_stages(layer2, M):
     torch.cuda.synchronize()
     lone = cpu(b)
     ext.set_option("attn_pair", 1)
+    # the default at 64 heads, the one bench.py times: the 64-head CTAs (one f16 p); every stage
+    # below checks this run
+    ext.set_option("attn_wide", 1)
+    r.k2(L, step, M, b)
+    torch.cuda.synchronize()
+    B = cpu(b)
+    assert ext.lib().dsv41_device_error() == 0
     S = cpu(step)
     H, QL, D, nope = s.hidden, s.q_lora, s.head_dim, s.nope
     cs = W["cos_sin"][S["pos"]]
@@ -142,10 +154,14 @@ def test_config2_stages(layer2, M):
     xo = OL.attention(B["q"].float(), B["kt"], B["klen"], S["cache"], S["blk"], None, 1, W["sink"], cosv, sinv,
                       nope, s.rope, 8)
     gx = B["xo"].float()
-    c("attention cos >= 0.9998, rel < 1e-3", cos(gx, xo) >= 0.9998 and rel(gx, xo) < 1e-3, (cos(gx, xo), rel(gx, xo)))
+    c("attention (64-head CTAs) cos >= 0.9998, rel < 1e-3", cos(gx, xo) >= 0.9998 and rel(gx, xo) < 1e-3,
+      (cos(gx, xo), rel(gx, xo)))
+    px = pair["xo"].float()
+    c("attention (CTA pair) cos >= 0.9998, rel < 1e-3", cos(px, xo) >= 0.9998 and rel(px, xo) < 1e-3,
+      (cos(px, xo), rel(px, xo)))
     for name, other in (("staged", staged), ("lone", lone)):
-        c(f"pair == {name} CTAs", torch.equal(B["xo"], other["xo"]) and torch.equal(B["out"], other["out"]),
-          maxabs(B["xo"], other["xo"]))
+        c(f"pair == {name} CTAs", torch.equal(pair["xo"], other["xo"]) and torch.equal(pair["out"], other["out"]),
+          maxabs(pair["xo"], other["xo"]))
     # ---- wo_a -> X8B, wo_b
     _, x8b, x8bs = OL.wo_a(gx, W["woa"], W["woa_s"], s.groups_local, s.o_rank)
     wr = rel(N.mxfp8_dequant(B["x8b"], B["x8bs"]), N.mxfp8_dequant(x8b, x8bs))
