@@ -3,9 +3,11 @@
 //
 // CTA = (row, chunk of the row's keys), 16 warps:
 //   warps 0-7   softmax + epilogue: warp w owns TMEM lane quarter w % 4 and heads 32 (w / 4) ..
-//   warp  8     TMEM allocation and the MMA issue (one elected thread)
+//   warp  8     TMEM allocation and the QK issue (one elected thread)
 //   warp  9     copies: a tile's key-table entries -> runs of consecutive slots of one page -> one
-//               cp.async.bulk a run into the staging buffer (a tile's 48 raw records); the scale codes
+//               cp.async.bulk a run into the staging buffer (a tile's 48 raw records); the scale
+//               codes; and (lane 0) the PV issue: two issuing threads, because one thread's issue
+//               rate (~70 cycles an MMA of these shapes) set the period
 //   warps 10-15 conversion: staged FP8 records -> the f16 tile (two tiles in flight)
 // Per 48-key tile j (tile, S and P buffers j & 1):
 //   S^T[64 keys x 64 heads] = K_tile . Q^T   tcgen05.mma M=64 (keys; rows 48..63 read what follows
@@ -174,7 +176,8 @@ __global__ void __launch_bounds__(kWdThreads, 1) attn_wide_kernel(const AttnArgs
   auto b_scons = [&](int s) { return bar(8 + s); };   // softmax holds S[s] in registers
   auto b_pready = [&](int s) { return bar(10 + s); }; // softmax -> PV
   auto b_pvdone = [&](int s) { return bar(12 + s); }; // PV done: P[s] free, O complete to here
-  const uint32_t b_drain = bar(14);
+  const uint32_t b_drain = bar(14);   // the QK thread's MMAs complete
+  const uint32_t b_drain2 = bar(15);  // the PV thread's
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
   uint32_t* tmem_base = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   float* red = reinterpret_cast<float*>(smem + L::kRed);
@@ -214,6 +217,7 @@ __global__ void __launch_bounds__(kWdThreads, 1) attn_wide_kernel(const AttnArgs
     mbar_init(b_sfull, 1);
     mbar_init(b_sempty, kWdConv);
     mbar_init(b_drain, 1);
+    mbar_init(b_drain2, 1);
     *abort = 0;
   }
   if (tid < 64) {
@@ -235,11 +239,14 @@ __global__ void __launch_bounds__(kWdThreads, 1) attn_wide_kernel(const AttnArgs
   const uint32_t tm_s = tmem, tm_o = tmem + 128;
 
   if (warp == 9) {
-    // ================= copies (lane l: keys l and 32 + l of a tile)
-    // Per tile j: tile j + 1's records located (their code words loaded), tile j + 2's key-table
-    // entries loaded; then, once the converters are done with tile j - 1's records, tile j's
-    // codes and live keys published and its runs fetched: a key starts a run unless it continues
-    // the previous key's record (the next slot of the same page); a run's first lane copies it.
+    // ================= copies (lane l: keys l and 32 + l of a tile) and the PV issue (lane 0)
+    // One polling loop over two event streams. Copies: once the converters hold tile jc - 1's
+    // records in registers, tile jc's codes and live keys are published and its runs fetched (a
+    // key starts a run unless it continues the previous key's record, the next slot of the same
+    // page; a run's first lane copies it); then tile jc + 2 is located (its code words loaded) and
+    // tile jc + 3's key-table entries loaded, in flight while the loop polls. PVs: once softmax(jp)
+    // wrote P, PV(jp) -- its completion frees the tile for the conversion two tiles on.
+    const uint32_t id_pv = umma_idesc(128, kWdNH, 1, 1);
     const bool has_b = lane < kWdKeys - 32;
     auto kt_load = [&](int j, int i) {
       const int k = k0 + j * kWdKeys + i;
@@ -258,70 +265,141 @@ __global__ void __launch_bounds__(kWdThreads, 1) attn_wide_kernel(const AttnArgs
         c = *reinterpret_cast<const uint64_t*>(page + (size_t)blk * RB + (size_t)off * 8);
       }
     };
-    const uint8_t *pa = nullptr, *pb = nullptr;
-    uint64_t ca = 0, cb = 0;
-    int va = -1, vb = -1;
+    // PV(j): O += V^T P^T. A = V^T, MN-major, 128-byte swizzle: a 128-dim block = 2 chunks
+    // kChunkT apart (lbo), K step ks = key groups 2 ks, 2 ks + 1 (1 KB apart: sbo); B = P^T.
+    // K step outer, dim blocks inner: consecutive MMAs go to different accumulators
+    auto issue_pv = [&](int j) {
+      TC_TRACE(j, 3);
+      tc_fence_after();
+      const uint64_t da = umma_sdesc_sw128(s_tile0 + (j & 1) * L::kTileBytes, kChunkT, 1024);
+      const uint64_t db0 = umma_sdesc(s_p + (j & 1) * L::kPBytes, (kWdNH / 8) * 128, 128);
+      constexpr uint32_t db_step = (uint32_t)(2 * (kWdNH / 8) * 128) >> 4;
+#pragma unroll
+      for (int ks = 0; ks < kWdKeys / 16; ++ks)
+#pragma unroll
+        for (int b = 0; b < NBLK; ++b) {
+          const int d0 = 128 * b < D - 128 ? 128 * b : D - 128;
+          umma_f16(tm_o + 64 * b, da + (uint64_t)(((d0 / 64) * kChunkT + ks * 2048) >> 4),
+                   db0 + (uint64_t)(ks * db_step), id_pv, j > 0 || ks > 0);
+        }
+      umma_commit(b_free(j & 1));    // the tile is free
+      umma_commit(b_pvdone(j & 1));  // P[j & 1] free; O holds tiles 0 .. j
+      TC_TRACE(j, 9);
+    };
+    const uint8_t *pa = nullptr, *pb = nullptr, *na = nullptr, *nb = nullptr;
+    uint64_t ca = 0, cb = 0, nca = 0, ncb = 0;
+    int va = -1, vb = -1;  // key-table entries of the tile after the located ones
     if (nsub > 0) {
       locate(kt_load(0, lane), pa, ca);
       locate(kt_load(0, 32 + lane), pb, cb);
-      va = kt_load(1, lane);
-      vb = kt_load(1, 32 + lane);
+      const int v1a = kt_load(1, lane), v1b = kt_load(1, 32 + lane);
+      va = kt_load(2, lane);
+      vb = kt_load(2, 32 + lane);
+      locate(v1a, na, nca);
+      locate(v1b, nb, ncb);
     }
     const uint32_t stage = smem_u32(smem + L::kStage);
-    int issued = 0;  // tiles whose copies went out
-    for (int j = 0; j < nsub; ++j) {
-      const uint8_t *na = nullptr, *nb = nullptr;
-      uint64_t nca = 0, ncb = 0;
-      if (j + 1 < nsub) {
-        locate(va, na, nca);
-        locate(vb, nb, ncb);
-        va = kt_load(j + 2, lane);
-        vb = kt_load(j + 2, 32 + lane);
+    int jc = 0, jp = 0;  // next tile to copy, next tile to PV
+    uint32_t idle = 0;
+    uint64_t deadline = 0;
+    bool ok = true;
+    while (ok && (jc < nsub || jp < nsub)) {
+      bool progress = false;
+      if (jc < nsub) {
+        bool go = true;
+        if (jc >= 1) {
+          go = __shfl_sync(0xffffffffu, lane == 0 ? (int)mbar_test(b_sempty, (jc - 1) & 1) : 0, 0) != 0;
+          if (go) go = wd_warp_wait(b_sempty, (jc - 1) & 1, abort);  // (completes at once: each lane's acquire)
+        }
+        if (go) {
+          if (lane == 0) TC_TRACE(jc, 14);
+          meta_c[(jc & 1) * 64 + lane] = ca;
+          if (has_b) meta_c[(jc & 1) * 64 + 32 + lane] = cb;
+          const uint8_t* prev_a = reinterpret_cast<const uint8_t*>(
+              __shfl_up_sync(0xffffffffu, reinterpret_cast<unsigned long long>(pa), 1));
+          const uint8_t* last_a = reinterpret_cast<const uint8_t*>(
+              __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(pa), 31));
+          const uint8_t* prev_b = reinterpret_cast<const uint8_t*>(
+              __shfl_up_sync(0xffffffffu, reinterpret_cast<unsigned long long>(pb), 1));
+          if (lane == 0) {
+            prev_a = nullptr;
+            prev_b = last_a;
+          }
+          const bool start_a = pa != nullptr && !(prev_a != nullptr && pa == prev_a + RB);
+          const bool start_b = has_b && pb != nullptr && !(prev_b != nullptr && pb == prev_b + RB);
+          const uint32_t brk_a = __ballot_sync(0xffffffffu, start_a || pa == nullptr);
+          const uint32_t brk_b = __ballot_sync(0xffffffffu, !has_b || start_b || pb == nullptr);
+          const uint64_t brk = (uint64_t)brk_a | ((uint64_t)brk_b << 32);  // bits kWdKeys .. 63 set
+          const uint32_t va_mask = __ballot_sync(0xffffffffu, pa != nullptr);
+          const uint32_t vb_mask = __ballot_sync(0xffffffffu, has_b && pb != nullptr);
+          const uint32_t nvalid = __popc(va_mask) + __popc(vb_mask);
+          if (lane == 0) live_mask[jc & 1] = (uint64_t)va_mask | ((uint64_t)vb_mask << 32);
+          __syncwarp();
+          if (lane == 0) tc_expect_tx(b_sfull, nvalid * (uint32_t)RB);  // (0 bytes: the arrival completes it)
+          __syncwarp();
+          auto run_copy = [&](int i, const uint8_t* p) {
+            const uint64_t above = brk & ~((2ull << i) - 1);
+            const int len = __ffsll((long long)above) - 1 - i;
+            tc_bulk_load(stage + (uint32_t)(i * RB), p, (uint32_t)(len * RB), b_sfull);
+          };
+          if (start_a) run_copy(lane, pa);
+          if (start_b) run_copy(32 + lane, pb);
+          if (lane == 0) TC_TRACE(jc, 15);
+          ++jc;
+          pa = na;
+          pb = nb;
+          ca = nca;
+          cb = ncb;
+          na = nb = nullptr;
+          nca = ncb = 0;
+          if (jc + 1 < nsub) {  // tile jc + 1 located, tile jc + 2's entries loaded
+            locate(va, na, nca);
+            locate(vb, nb, ncb);
+            va = kt_load(jc + 2, lane);
+            vb = kt_load(jc + 2, 32 + lane);
+          }
+          progress = true;
+        }
       }
-      if (j >= 1 && !wd_warp_wait(b_sempty, (j - 1) & 1, abort)) break;
-      if (lane == 0) TC_TRACE(j, 14);
-      meta_c[(j & 1) * 64 + lane] = ca;
-      if (has_b) meta_c[(j & 1) * 64 + 32 + lane] = cb;
-      const uint8_t* prev_a = reinterpret_cast<const uint8_t*>(
-          __shfl_up_sync(0xffffffffu, reinterpret_cast<unsigned long long>(pa), 1));
-      const uint8_t* last_a = reinterpret_cast<const uint8_t*>(
-          __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(pa), 31));
-      const uint8_t* prev_b = reinterpret_cast<const uint8_t*>(
-          __shfl_up_sync(0xffffffffu, reinterpret_cast<unsigned long long>(pb), 1));
-      if (lane == 0) {
-        prev_a = nullptr;
-        prev_b = last_a;
+      if (jp < jc && jp < nsub) {
+        // (P(jp) exists only after tile jp was copied, converted and its QK ran)
+        const bool rdy = __shfl_sync(0xffffffffu, lane == 0 ? (int)mbar_test(b_pready(jp & 1), (jp >> 1) & 1) : 0, 0);
+        if (rdy) {
+          if (lane == 0) issue_pv(jp);
+          __syncwarp();
+          ++jp;
+          progress = true;
+        }
       }
-      const bool start_a = pa != nullptr && !(prev_a != nullptr && pa == prev_a + RB);
-      const bool start_b = has_b && pb != nullptr && !(prev_b != nullptr && pb == prev_b + RB);
-      const uint32_t brk_a = __ballot_sync(0xffffffffu, start_a || pa == nullptr);
-      const uint32_t brk_b = __ballot_sync(0xffffffffu, !has_b || start_b || pb == nullptr);
-      const uint64_t brk = (uint64_t)brk_a | ((uint64_t)brk_b << 32);  // bits kWdKeys .. 63 set
-      const uint32_t va_mask = __ballot_sync(0xffffffffu, pa != nullptr);
-      const uint32_t vb_mask = __ballot_sync(0xffffffffu, has_b && pb != nullptr);
-      const uint32_t nvalid = __popc(va_mask) + __popc(vb_mask);
-      if (lane == 0) live_mask[j & 1] = (uint64_t)va_mask | ((uint64_t)vb_mask << 32);
-      __syncwarp();
-      if (lane == 0) tc_expect_tx(b_sfull, nvalid * (uint32_t)RB);  // (0 bytes: the arrival completes it)
-      __syncwarp();
-      auto run_copy = [&](int i, const uint8_t* p) {
-        const uint64_t above = brk & ~((2ull << i) - 1);
-        const int len = __ffsll((long long)above) - 1 - i;
-        tc_bulk_load(stage + (uint32_t)(i * RB), p, (uint32_t)(len * RB), b_sfull);
-      };
-      if (start_a) run_copy(lane, pa);
-      if (start_b) run_copy(32 + lane, pb);
-      if (lane == 0) TC_TRACE(j, 15);
-      issued = j + 1;
-      pa = na;
-      pb = nb;
-      ca = nca;
-      cb = ncb;
+      if (progress) {
+        idle = 0;
+        deadline = 0;
+      } else if ((++idle & 255) == 0) {
+        // bounded: another role gave up, or nothing arrived for 2 s
+        if (*abort) {
+          ok = false;
+        } else {
+          const uint64_t now = wd_now();
+          if (deadline == 0) {
+            deadline = now + 2000000000ull;
+          } else if (now > deadline) {
+            *abort = 1;
+            atomicExch(&g_tc_error, 1);
+            ok = false;
+          }
+        }
+        ok = __all_sync(0xffffffffu, ok);
+      }
+    }
+    if (lane == 0) {
+      // every PV complete before the TMEM is freed (also after an abort)
+      umma_commit(b_drain2);
+      mbar_wait(b_drain2, 0, abort);
     }
     // no copy may still be landing when the CTA leaves (after an abort the converters stopped
     // consuming): wait, bounded, for the last issued tile's
-    if (issued > 0)
-      for (uint32_t it = 0; it < kTcWaitPolls && !mbar_try(b_sfull, (issued - 1) & 1); ++it) {
+    if (jc > 0)
+      for (uint32_t it = 0; it < kTcWaitPolls && !mbar_try(b_sfull, (jc - 1) & 1); ++it) {
       }
   } else if (warp >= 10) {
     // ================= conversion (warps 10-15): nope item f = (key f / 64, 8-dim unit f % 64),
@@ -385,12 +463,10 @@ __global__ void __launch_bounds__(kWdThreads, 1) attn_wide_kernel(const AttnArgs
       if (ctid == 0) TC_TRACE(j, 1);
     }
   } else if (warp == 8) {
-    // ================= MMA issue (one elected thread)
-    // QK(j) needs tile j and S[j & 1] consumed by softmax(j - 2); PV(j) needs P(j). QK(j + 1) goes
-    // out as soon as its inputs are ready, so it runs under softmax(j).
+    // ================= QK issue (one elected thread): QK(j + 1) goes out as soon as its inputs are
+    // ready, so it runs under softmax(j)
     if (lane == 0) {
       const uint32_t id_qk = umma_idesc(64, kWdNH, 0, 0);
-      const uint32_t id_pv = umma_idesc(128, kWdNH, 1, 1);
       auto issue_qk = [&](int j) {
         TC_TRACE(j, 10);
         const uint32_t dst = tm_s + 64 * (j & 1);
@@ -405,67 +481,16 @@ __global__ void __launch_bounds__(kWdThreads, 1) attn_wide_kernel(const AttnArgs
         umma_commit(b_sready(j & 1));
         TC_TRACE(j, 11);
       };
-      auto qk_ready = [&](int j) {
-        return mbar_test(b_full(j & 1), (j >> 1) & 1) && (j < 2 || mbar_test(b_scons(j & 1), ((j - 2) >> 1) & 1));
-      };
       auto wait_qk = [&](int j) {
         return mbar_wait(b_full(j & 1), (j >> 1) & 1, abort) &&
                (j < 2 || mbar_wait(b_scons(j & 1), ((j - 2) >> 1) & 1, abort));
       };
-      bool ok = true;
-      if (nsub > 0) ok = wait_qk(0);
-      if (ok && nsub > 0) {
+      // QK(j) once tile j is converted and S[j & 1] is free (softmax(j - 2) holds it in
+      // registers); the PVs are warp 9's
+      for (int j = 0; j < nsub; ++j) {
+        if (!wait_qk(j)) break;
         tc_fence_after();
-        issue_qk(0);
-      }
-      for (int j = 0; ok && j < nsub; ++j) {
-        const int s = j & 1;
-        const uint32_t p_ready = b_pready(s), p_par = (j >> 1) & 1;
-        bool qk_done = j + 1 >= nsub;
-        if (!qk_done && qk_ready(j + 1)) {
-          tc_fence_after();
-          issue_qk(j + 1);
-          qk_done = true;
-        }
-        if (!qk_done) {
-          // wait for whichever comes first: P(j) (then PV), or QK(j + 1)'s inputs
-          for (uint32_t it = 0; !qk_done && it < kTcWaitPolls; ++it) {
-            if (mbar_test(p_ready, p_par)) break;
-            if (qk_ready(j + 1)) {
-              tc_fence_after();
-              issue_qk(j + 1);
-              qk_done = true;
-            }
-          }
-        }
-        TC_TRACE(j, 2);
-        ok = mbar_wait(p_ready, p_par, abort);
-        if (!ok) break;
-        TC_TRACE(j, 3);
-        tc_fence_after();
-        // PV: O += V^T P^T. A = V^T, MN-major, 128-byte swizzle: a 128-dim block = 2 chunks
-        // kChunkT apart (lbo), K step ks = key groups 2 ks, 2 ks + 1 (1 KB apart: sbo); B = P^T
-        const uint64_t da = umma_sdesc_sw128(s_tile0 + (j & 1) * L::kTileBytes, kChunkT, 1024);
-        const uint64_t db0 = umma_sdesc(s_p + s * L::kPBytes, (kWdNH / 8) * 128, 128);
-        constexpr uint32_t db_step = (uint32_t)(2 * (kWdNH / 8) * 128) >> 4;
-        // K step outer, dim blocks inner: consecutive MMAs go to different accumulators
-#pragma unroll
-        for (int ks = 0; ks < kWdKeys / 16; ++ks)
-#pragma unroll
-          for (int b = 0; b < NBLK; ++b) {
-            const int d0 = 128 * b < D - 128 ? 128 * b : D - 128;
-            umma_f16(tm_o + 64 * b, da + (uint64_t)(((d0 / 64) * kChunkT + ks * 2048) >> 4),
-                     db0 + (uint64_t)(ks * db_step), id_pv, j > 0 || ks > 0);
-          }
-        umma_commit(b_free(j & 1));  // the tile is free
-        umma_commit(b_pvdone(s));    // P[s] free; O holds tiles 0 .. j
-        TC_TRACE(j, 9);
-        if (!qk_done) {
-          ok = wait_qk(j + 1);
-          if (!ok) break;
-          tc_fence_after();
-          issue_qk(j + 1);
-        }
+        issue_qk(j);
       }
       // every issued MMA complete before the TMEM is freed (also after an abort)
       umma_commit(b_drain);
@@ -576,37 +601,35 @@ __global__ void __launch_bounds__(kWdThreads, 1) attn_wide_kernel(const AttnArgs
 #pragma unroll
         for (int q = 0; q < 32; ++q) l_part[q] *= a_sm[hb + q];
       }
-      // p' = 2^(s - m + 7) into P^T[s] as one f16 (<= 2^15); this thread's partial sums of p'
-      uint32_t hi[16];
-#pragma unroll
-      for (int q = 0; q < 32; q += 4) {
-        const float4 m4 = *reinterpret_cast<const float4*>(m_sm + hb + q);
-        const float mq[4] = {m4.x, m4.y, m4.z, m4.w};
-        float pq[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          pq[i] = sv[q + i] == -INFINITY ? 0.f : ex2_approx(sv[q + i] - mq[i] + kWdShift);
-          l_part[q + i] += pq[i];
-        }
-        hi[q / 2] = cvt_f16x2(pq[0], pq[1]);
-        hi[q / 2 + 1] = cvt_f16x2(pq[2], pq[3]);
-      }
-      if (tid == 0) TC_TRACE(j, 12);
       // P^T[s] is free once PV(j - 2) is done
       if (j >= 2) {
         ok = wd_all(wd_warp_wait(b_pvdone(s), ((j - 2) >> 1) & 1, abort));
         if (!ok) break;
       }
       if (tid == 0) TC_TRACE(j, 13);
-      if (has_key) {
-        // P^T [key group][head group][8 keys][8 heads]: this half's head groups hb / 8 ..
-        uint8_t* pt = smem + L::kP + s * L::kPBytes;
-        const int row = (key >> 3) * (kWdNH / 8) + hb / 8;
+      // p' = 2^(s - m + 7) into P^T[s] as one f16 (<= 2^15), 8 heads (16 bytes) at a time; this
+      // thread's partial sums of p'. P^T [key group][head group][8 keys][8 heads]: this half's
+      // head groups hb / 8 ..
+      uint8_t* prow = smem + L::kP + s * L::kPBytes + ((key >> 3) * (kWdNH / 8) + hb / 8) * 128 + (key & 7) * 16;
 #pragma unroll
-        for (int hg = 0; hg < 4; ++hg)
-          *reinterpret_cast<uint4*>(pt + (row + hg) * 128 + (key & 7) * 16) =
-              make_uint4(hi[4 * hg], hi[4 * hg + 1], hi[4 * hg + 2], hi[4 * hg + 3]);
+      for (int g = 0; g < 4; ++g) {
+        uint32_t hw[4];
+#pragma unroll
+        for (int q = 8 * g; q < 8 * g + 8; q += 4) {
+          const float4 m4 = *reinterpret_cast<const float4*>(m_sm + hb + q);
+          const float mq[4] = {m4.x, m4.y, m4.z, m4.w};
+          float pq[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            pq[i] = sv[q + i] == -INFINITY ? 0.f : ex2_approx(sv[q + i] - mq[i] + kWdShift);
+            l_part[q + i] += pq[i];
+          }
+          hw[(q - 8 * g) / 2] = cvt_f16x2(pq[0], pq[1]);
+          hw[(q - 8 * g) / 2 + 1] = cvt_f16x2(pq[2], pq[3]);
+        }
+        if (has_key) *reinterpret_cast<uint4*>(prow + g * 128) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
       }
+      if (tid == 0) TC_TRACE(j, 12);
       fence_async_smem();
       tc_fence_before();
       __syncwarp();
