@@ -716,10 +716,13 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   DSV41_TRY(launch(seam_slice_kernel, dim3(H / kSliceCols), dim3(256), 0, st, s));
   DSV41_TRY(launch(seam_gate_norm_kernel, dim3(M), dim3(256), 0, st, s));
   // ---- router, routing, union
-  const int router_smem = 16 * H <= 200 * 1024 ? 16 * H : 0;
+  // rows a CTA: 4 once 8 would leave the SMs short of CTAs (M > 8)
+  const int rpc = M > 8 ? 4 : 8;
+  const int router_smem = 2 * rpc * H <= 200 * 1024 ? 2 * rpc * H : 0;
   RouterArgs ra = {M, E, H, normed, ptr<const __nv_bfloat16>(a->gate_w), logits, router_smem > 0};
   mark(a->events, 3, st);
-  DSV41_TRY(launch(router_kernel, dim3(cdiv(E, 8), cdiv(M, 8)), dim3(256), router_smem, st, ra));
+  DSV41_TRY(rpc == 4 ? launch(router_kernel<4>, dim3(cdiv(E, 8), cdiv(M, 4)), dim3(256), router_smem, st, ra)
+                     : launch(router_kernel<8>, dim3(cdiv(E, 8), cdiv(M, 8)), dim3(256), router_smem, st, ra));
   RouteArgs rt = {M, E, TK, (int)a->route_softmax, logits, ptr<const float>(a->bias),
                   ptr<int32_t>(a->ids), ptr<float>(a->wts)};
   PlanArgs pl = {M, E, TK, ptr<const int32_t>(a->ids), n_u, u_expert, u_off, picks};
@@ -839,7 +842,7 @@ int dsv41_index_query(const Dsv41IndexQueryArgs* a, void* stream) {
   // the head weights' dots: the router's exact fixed-order fp64 sums, heads as its experts
   const int smem = 16 * hidden <= 200 * 1024 ? 16 * hidden : 0;
   RouterArgs ra = {M, heads, hidden, ptr<const __nv_bfloat16>(a->x), ptr<const __nv_bfloat16>(a->wp), hw, smem > 0};
-  DSV41_TRY(launch(router_kernel, dim3(cdiv(heads, 8), cdiv(M, 8)), dim3(256), smem, st, ra));
+  DSV41_TRY(launch(router_kernel<8>, dim3(cdiv(heads, 8), cdiv(M, 8)), dim3(256), smem, st, ra));
   float scale;
   const uint32_t sb = (uint32_t)a->weight_scale_f32;
   memcpy(&scale, &sb, 4);

@@ -27,30 +27,35 @@ struct RouterArgs {
   const __nv_bfloat16* x;     // [M, K] normed
   const __nv_bfloat16* gate;  // [E, K]
   float* logits;              // [M, E]
-  int staged;                 // 1: the CTA's 8 rows of x go to shared memory (16 K bytes of it)
+  int staged;                 // 1: the CTA's rows of x go to shared memory (2 K bytes a row and 1024 K)
 };
 
-// grid (E / 8, ceil(M / 8)); warp w of CTA (ex, tg) = expert 8 ex + w, rows 8 tg .. 8 tg + 7.
-// A lane's weight loads go out 16 at a time (4096 K) before their sums; the CTA's 8 rows of x
-// are staged once in shared memory when they fit. The arithmetic is the contract's, unchanged:
-// per lane and row one fp64 chain over i, then j.
-constexpr int kRouterChunk = 16;  // 256-K iterations a batch of weight loads
-__global__ void __launch_bounds__(256) router_kernel(const RouterArgs a) {
+// grid (E / 8, ceil(M / RPC)); warp w of CTA (ex, tg) = expert 8 ex + w, rows RPC tg .. + RPC - 1
+// (RPC = 8, or 4 where a row group of 8 a CTA would leave the SMs short of CTAs: the sums are
+// chains of dependent fp64 FMAs, so the kernel wants warps in flight more than rows a warp). A
+// lane's weight loads go out ahead of their sums: all 16 batches of 256 K at once for 8 rows (the
+// latency-bound small-M case), 4 at a time, double-buffered, for 4 rows (fewer registers, so three
+// CTAs share an SM); the CTA's rows of x are staged once in shared memory when they fit. The
+// arithmetic is the contract's, unchanged: per lane and row one fp64 chain over i, then j.
+template <int RPC>
+__global__ void __launch_bounds__(256, RPC == 4 ? 3 : 1) router_kernel(const RouterArgs a) {
+  constexpr int kRouterChunk = RPC == 4 ? 4 : 16;  // 256-K iterations a batch of weight loads
   extern __shared__ __align__(16) uint8_t router_smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x * 8 + warp;
   const bool live = e < a.E;
   const int iters = a.K / 256;
   const __nv_bfloat16* w = a.gate + (size_t)(live ? e : 0) * a.K + 8 * lane;
-  uint4 wv[kRouterChunk];
-  auto load_chunk = [&](int i0) {
+  uint4 wv[kRouterChunk], wn[kRouterChunk];
+  auto load_chunk = [&](uint4 (&dst)[kRouterChunk], int i0) {
 #pragma unroll
     for (int i = 0; i < kRouterChunk; ++i)
-      wv[i] = (live && i0 + i < iters) ? ldg16(w + 256 * (i0 + i)) : make_uint4(0, 0, 0, 0);
+      dst[i] = (live && i0 + i < iters) ? ldg16(w + 256 * (i0 + i)) : make_uint4(0, 0, 0, 0);
   };
-  load_chunk(0);  // the gate weights wait on nothing: stream them before the dependency wait
+  load_chunk(wv, 0);  // the gate weights wait on nothing: stream them before the dependency wait
+  if (kRouterChunk < 16) load_chunk(wn, kRouterChunk);
   pdl_wait();
-  const int t0 = blockIdx.y * 8, nt = min(8, a.M - t0);
+  const int t0 = blockIdx.y * RPC, nt = min(RPC, a.M - t0);
   const __nv_bfloat16* xr = a.x + (size_t)t0 * a.K;
   if (a.staged) {
     __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(router_smem);
@@ -60,10 +65,11 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterArgs a) {
     xr = xs;
   }
   if (!live) return;
-  // the (up to) 8 rows' chains run side by side; each row's sum keeps the contract's order
-  double acc[8] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0};
+  // the rows' chains run side by side; each row's sum keeps the contract's order
+  double acc[RPC];
+#pragma unroll
+  for (int r = 0; r < RPC; ++r) acc[r] = 0.0;
   for (int i0 = 0; i0 < iters; i0 += kRouterChunk) {
-    if (i0 > 0) load_chunk(i0);
 #pragma unroll
     for (int i = 0; i < kRouterChunk; ++i) {
       if (i0 + i >= iters) break;
@@ -73,7 +79,7 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterArgs a) {
       for (int j = 0; j < 8; ++j)
         wd[j] = (double)__uint_as_float((j & 1) ? (ww[j >> 1] & 0xffff0000u) : (ww[j >> 1] << 16));
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
+      for (int r = 0; r < RPC; ++r) {
         if (r < nt) {
           const uint4 xv = *reinterpret_cast<const uint4*>(xr + (size_t)r * a.K + 8 * lane + 256 * (i0 + i));
           const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
@@ -85,9 +91,17 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterArgs a) {
         }
       }
     }
+    // the next batch (loaded a batch ahead when double-buffered); then the one after it
+    if (kRouterChunk < 16) {
+#pragma unroll
+      for (int i = 0; i < kRouterChunk; ++i) wv[i] = wn[i];
+      if (i0 + 2 * kRouterChunk < iters) load_chunk(wn, i0 + 2 * kRouterChunk);
+    } else if (i0 + kRouterChunk < iters) {
+      load_chunk(wv, i0 + kRouterChunk);
+    }
   }
 #pragma unroll
-  for (int r = 0; r < 8; ++r) {
+  for (int r = 0; r < RPC; ++r) {
     const double s = warp_sum_d(acc[r]);
     if (lane == 0 && r < nt) a.logits[(size_t)(t0 + r) * a.E + e] = (float)s;
   }
