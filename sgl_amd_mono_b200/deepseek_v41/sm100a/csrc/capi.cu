@@ -17,6 +17,7 @@
 #include "attention.cuh"
 #include "attn_tc.cuh"
 #include "attn_wide.cuh"
+#include "k2i_tc.cuh"
 #include "common.cuh"
 #include "epilogue.cuh"
 #include "front.cuh"
@@ -89,8 +90,12 @@ Option g_options[] = {
     {"fused_allreduce", "DSV41_FUSED_AR", 1, {0}, {false}},
     {"k1_persistent", "DSV41_K1_PERSISTENT", 0, {0}, {false}},
     {"attn_wide", "DSV41_ATTN_WIDE", 1, {0}, {false}},
+    {"k2i_tc", "DSV41_K2I_TC", 1, {0}, {false}},
 };
-enum { kOptAttnTc, kOptAttnPair, kOptDenseMinM, kOptPdl, kOptAttnBulk, kOptFusedAr, kOptK1Persistent, kOptAttnWide };
+enum {
+  kOptAttnTc, kOptAttnPair, kOptDenseMinM, kOptPdl, kOptAttnBulk, kOptFusedAr, kOptK1Persistent, kOptAttnWide,
+  kOptK2iTc
+};
 
 int64_t option(int i) {
   Option& o = g_options[i];
@@ -121,6 +126,9 @@ bool use_attn_bulk() { return option(kOptAttnBulk) == 1; }
 // one f16 p) (1, default), or the 32-head kernels above (0; DSV41_ATTN_WIDE=0). Measured at config
 // 2, M = 48: 243 us against the CTA pair's 392 us.
 bool use_attn_wide() { return option(kOptAttnWide) == 1; }
+// K2i's scorer on tcgen05 block-scaled MMAs (k2i_tc_kernel, 1, default) or on mma.sync with the fp64
+// chunk epilogue (k2i_score_kernel, 0; DSV41_K2I_TC=0). Both give the contract's bits.
+bool use_k2i_tc() { return option(kOptK2iTc) == 1; }
 // TP > 1: both all-reduces fused into the kernels that produce the partials (wo_b's epilogue, the
 // MoE combine) as LL peer stores (1, default), or the standalone exchange kernel after each (0;
 // DSV41_FUSED_AR=0).
@@ -878,8 +886,13 @@ int dsv41_k2i(const Dsv41K2iArgs* a, void* stream) {
   k.entry_rows = (int)a->entry_rows; k.owners = ptr<const int32_t>(a->owners);
   k.bounds = ptr<const int32_t>(a->bounds); k.logits = ptr<float>(a->logits); k.lstride = (int)a->lstride;
   k.reindex = (int)a->reindex; k.reindex_chunks = (int)a->reindex_chunks;
-  DSV41_TRY(launch(k2i_score_kernel, dim3((int)a->ctas), dim3(256), k2i_smem_bytes(k.heads),
-                   reinterpret_cast<cudaStream_t>(stream), k));
+  // the tensor-core scorer reads queries as 16-byte vectors and copies code bytes in bulk
+  if (use_k2i_tc() && a->q % 16 == 0 && a->kscale % 16 == 0)
+    DSV41_TRY(launch(k2i_tc_kernel, dim3((int)a->ctas), dim3(kKtThreads), KtSmem::kBytes,
+                     reinterpret_cast<cudaStream_t>(stream), k));
+  else
+    DSV41_TRY(launch(k2i_score_kernel, dim3((int)a->ctas), dim3(256), k2i_smem_bytes(k.heads),
+                     reinterpret_cast<cudaStream_t>(stream), k));
   return launch_status();
 }
 

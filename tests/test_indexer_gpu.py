@@ -105,6 +105,46 @@ def test_index_logits_bit_exact(heads, ctxs, per_req):
         assert torch.equal(lg[t, :n], want), t
 
 
+def quantized_case(ctxs, per_req, heads, seed, spread_keys=0):
+    """fp4_case's layouts with SGLang-like MXFP4 data: N(0, 1) keys and queries quantized per 32
+    dims (small code spreads: the tensor-core scorer's folded-scale tiles). ``spread_keys`` keys
+    get one chunk's code raised by 9, so their 128-key tiles take the per-chunk path."""
+    from sgl_amd_mono_b200.deepseek_v41 import quant
+    case = fp4_case(ctxs, per_req, heads, seed)
+    g = torch.Generator().manual_seed(seed + 1000)
+    pages = case["payload"].shape[0]
+    packed, codes = quant.quant_mxfp4(torch.randn(pages * 64, 128, generator=g))
+    case["payload"] = packed.view(pages, 64, 4, 16).permute(0, 2, 1, 3).contiguous().view(pages, 1, 4, 64, 16)
+    slot = torch.arange(64)
+    ks = torch.empty(pages, 1, 4, 64, dtype=torch.uint8)
+    ks[:, 0, :, (slot % 16) * 4 + slot // 16] = codes.view(pages, 64, 4).permute(0, 2, 1)
+    for _ in range(spread_keys):
+        p, s = int(torch.randint(0, pages, (1,), generator=g)), int(torch.randint(0, 64, (1,), generator=g))
+        ks[p, 0, 1, (s % 16) * 4 + s // 16] += 9
+    case["kscale"] = ks
+    rows = case["q"].shape[0]
+    qp, qc = quant.quant_mxfp4(torch.randn(rows * heads, 128, generator=g))
+    case["q"] = qp.view(rows, heads, 64).contiguous()
+    qs = torch.zeros(rows, 1, 4, 16, 4, dtype=torch.uint8)
+    h = torch.arange(heads)
+    qs[:, 0, :, h % 16, h // 16] = qc.view(rows, heads, 4).permute(0, 2, 1)
+    case["qscale"] = qs
+    return case
+
+
+@pytest.mark.parametrize("heads,ctxs,per_req,spread", [(64, [5000, 2100], 1, 0), (64, [3000, 700], 3, 0),
+                                                        (32, [4100, 1900], 2, 0), (64, [6000, 2500], 2, 12)])
+def test_index_logits_quantized_bit_exact(heads, ctxs, per_req, spread):
+    """Folded-scale tiles (and, with spread keys, per-chunk tiles among them) equal the contract."""
+    case = quantized_case(ctxs, per_req, heads, seed=heads + per_req + spread, spread_keys=spread)
+    lg = _logits_case(case, per_req, topk_plan=0)
+    for t in range(case["q"].shape[0]):
+        n = int(case["bounds"][t])
+        want = OI.index_logits(case["q"], case["qscale"], case["w"], case["payload"], case["kscale"],
+                               case["table"], t, torch.arange(n))
+        assert torch.equal(lg[t, :n], want), (t, (lg[t, :n] - want).abs().max().item())
+
+
 def test_topk_ties_and_pages():
     g = torch.Generator().manual_seed(5)
     rows, width, k = 6, 5000, 512
