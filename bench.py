@@ -525,7 +525,8 @@ def run_config3(args, runner, layers, world, stream, hbm_peak):
     """the indexer layer -- K2i over 16 rows' FP4 index keys of a 32768-token
     compressed context (64 index heads), the top-2048, then K1 + K2 with the SWA window (128
     keys) and the 2048 selected compressed keys. Timed as one CUDA graph (K2i's walk plan,
-    scoring and top-k, K1, K2), and K2i alone; two copies of the step's data alternate."""
+    scoring and top-k, K1, K2), and K2i alone; two copies of the step's data alternate. The
+    scorer is also timed alone over four copies of the index plane (``k2i_score_us``)."""
     from sgl_amd_mono_b200.deepseek_v41 import roofline, synth
     from sgl_amd_mono_b200.deepseek_v41.sm100a.indexer import K2iRunner
 
@@ -559,6 +560,22 @@ def run_config3(args, runner, layers, world, stream, hbm_peak):
 
     ms_sel = _graph_time(args, [lambda c=c: select(c) for c in copies], world, stream)
     ms_layer = _graph_time(args, [lambda i=i: layer(i) for i in range(2)], world, stream)
+    # K2i's scorer alone (each plane's walk plan computed beforehand in its own runner), over four
+    # copies of the index plane (4 x 35.7 MB, more than L2)
+    planes = [c[1] for c in copies] + [
+        synth.make_sparse(s, M, ctx, args.seed + 320 + i, dev, index_heads=heads) for i in range(2)]
+    scorers = []
+    for sp in planes:
+        kr = K2iRunner(dev, ctx, topk=topk)
+        kr.walk_plan(ratio=1, bounds=sp["bounds"], rows=M, per_req=1)
+        scorers.append((kr, sp))
+
+    def score(kr, sp):
+        kr.score(rows=M, per_req=1, ratio=1, query=(sp["q"], sp["qscale"], sp["w"]),
+                 plane=(sp["payload"], sp["kscale"]), page_table=sp["page_table"], bounds=sp["bounds"])
+
+    ms_score = _graph_time(args, [lambda kr=kr, sp=sp: score(kr, sp) for kr, sp in scorers], world, stream)
+    del planes[2:], scorers
     b = layer(0)
     torch.cuda.synchronize()
     union = int(torch.unique(b["ids"][:M]).numel())
@@ -571,6 +588,8 @@ def run_config3(args, runner, layers, world, stream, hbm_peak):
             "k2i_select_us": round(ms_sel * 1e3, 2),
             "k2i_index_GBs": round(index_bytes / (ms_sel * 1e-3) / 1e9, 1),
             "k2i_frac_hbm": round(index_bytes / (ms_sel * 1e-3) / 1e9 / hbm_peak, 4),
+            "k2i_score_us": round(ms_score * 1e3, 2),
+            "k2i_score_frac_hbm": round(index_bytes / (ms_score * 1e-3) / 1e9 / hbm_peak, 4),
             "algorithmic_MB": round(lb / 1e6, 1), "frac_hbm": round(lb / (ms_layer * 1e-3) / 1e9 / hbm_peak, 4),
             "union": union}
 
