@@ -18,6 +18,7 @@
 #include "attn_tc.cuh"
 #include "attn_wide.cuh"
 #include "k2i_tc.cuh"
+#include "topk_cl.cuh"
 #include "common.cuh"
 #include "epilogue.cuh"
 #include "front.cuh"
@@ -91,10 +92,11 @@ Option g_options[] = {
     {"k1_persistent", "DSV41_K1_PERSISTENT", 0, {0}, {false}},
     {"attn_wide", "DSV41_ATTN_WIDE", 1, {0}, {false}},
     {"k2i_tc", "DSV41_K2I_TC", 1, {0}, {false}},
+    {"topk_cluster", "DSV41_TOPK_CLUSTER", 1, {0}, {false}},
 };
 enum {
   kOptAttnTc, kOptAttnPair, kOptDenseMinM, kOptPdl, kOptAttnBulk, kOptFusedAr, kOptK1Persistent, kOptAttnWide,
-  kOptK2iTc
+  kOptK2iTc, kOptTopkCluster
 };
 
 int64_t option(int i) {
@@ -129,6 +131,9 @@ bool use_attn_wide() { return option(kOptAttnWide) == 1; }
 // K2i's scorer on tcgen05 block-scaled MMAs (k2i_tc_kernel, 1, default) or on mma.sync with the fp64
 // chunk epilogue (k2i_score_kernel, 0; DSV41_K2I_TC=0). Both give the contract's bits.
 bool use_k2i_tc() { return option(kOptK2iTc) == 1; }
+// Top-k rows of at least kTopkClMinCands candidates over a cluster of 8 CTAs each
+// (topk_cluster_kernel, 1, default) or one CTA a row (topk_kernel, 0; DSV41_TOPK_CLUSTER=0).
+bool use_topk_cluster() { return option(kOptTopkCluster) == 1; }
 // TP > 1: both all-reduces fused into the kernels that produce the partials (wo_b's epilogue, the
 // MoE combine) as LL peer stores (1, default), or the standalone exchange kernel after each (0;
 // DSV41_FUSED_AR=0).
@@ -902,7 +907,18 @@ int dsv41_topk(const Dsv41TopkArgs* a, void* stream) {
     return DSV41_EINVAL;
   // a row has at most vstride values, hence at most ceil(vstride / group) candidates (rounded up
   // to a multiple of 4: the kernel reads the staged keys four at a time)
-  const int cap = (std::min<int>(40960, ((int)a->vstride + (int)a->group - 1) / (int)a->group) + 3) / 4 * 4;
+  const int cands = ((int)a->vstride + (int)a->group - 1) / (int)a->group;
+  if (use_topk_cluster() && cands >= kTopkClMinCands) {
+    // a CTA stages its eighth of a row (rows past 8 x 8192 candidates read theirs from global memory)
+    const int cap_cl = std::min(8192, (cands + kTopkCl - 1) / kTopkCl + 127) / 128 * 128;
+    TopkArgs t = {(int)a->rows, (int)a->k, ptr<const float>(a->vals), (int)a->vstride, ptr<const int32_t>(a->n),
+                  (int)a->group, ptr<int32_t>(a->out), ptr<int32_t>(a->page_out), ptr<const int32_t>(a->table),
+                  (int)a->table_stride, (int)a->page, ptr<const int32_t>(a->owners), cap_cl};
+    DSV41_TRY(launch(topk_cluster_kernel, dim3((int)a->rows * kTopkCl), dim3(kTopkClThreads),
+                     cap_cl * 4 + kTopkBins * 4, reinterpret_cast<cudaStream_t>(stream), t, kTopkCl));
+    return launch_status();
+  }
+  const int cap = (std::min<int>(40960, cands) + 3) / 4 * 4;
   TopkArgs t = {(int)a->rows, (int)a->k, ptr<const float>(a->vals), (int)a->vstride, ptr<const int32_t>(a->n),
                 (int)a->group, ptr<int32_t>(a->out), ptr<int32_t>(a->page_out), ptr<const int32_t>(a->table),
                 (int)a->table_stride, (int)a->page, ptr<const int32_t>(a->owners), cap};
