@@ -33,7 +33,7 @@ struct WalkPlanArgs {
 // index_plan.py:42-82 restated: pieces of <= 6 adjacent rows of one owner; a piece needs
 // ceil(max bound / 128) chunks when a row's bound exceeds topk; each piece gets
 // ceil(need / width) tasks sharing its chunks evenly at the smallest width whose task count
-// fits the CTAs. One thread (rows <= 48).
+// fits the CTAs. One warp plans (rows <= 64) with ballots and scans.
 __global__ void walk_plan_kernel(const WalkPlanArgs a) {
   __shared__ int s_owner[64], s_bound[64];
   __shared__ int s_lead[64], s_span[64], s_need[64], s_k[64], s_first[65], s_pieces;
@@ -45,51 +45,95 @@ __global__ void walk_plan_kernel(const WalkPlanArgs a) {
   }
   for (int i = threadIdx.x; i < a.ctas * 4; i += blockDim.x) a.plan[i] = 0;
   __syncthreads();
-  if (threadIdx.x == 0) {  // one thread plans (rows <= 48); the block writes the tasks
-    int lead[64], span[64], need[64];
-    int np = 0, run_first = 0;
-    for (int t = 0; t < a.rows; ++t) {
-      const bool start = t == 0 || s_owner[t] != s_owner[t - 1];
-      if (start) run_first = t;
-      if (start || (t - run_first) % kWalkRows == 0) lead[np++] = t;
-    }
-    int pieces = 0;
-    for (int i = 0; i < np; ++i) {
-      const int l = lead[i], e = i + 1 < np ? lead[i + 1] : a.rows;
-      int nd = 0;
-      for (int t = l; t < e; ++t) {
+  if (threadIdx.x < 32) {  // one warp plans (rows <= 64: lane l holds rows l and l + 32); the block writes the tasks
+    const int lane = threadIdx.x;
+    const uint32_t full = 0xffffffffu;
+    auto below = [](int t) { return t >= 63 ? ~0ull : ((2ull << t) - 1); };  // bits 0 .. t
+    // a run of one owner starts a piece, and so does every kWalkRows-th row of the run
+    auto starts = [&](int t) { return t < a.rows && (t == 0 || s_owner[t] != s_owner[t - 1]); };
+    const uint64_t smask = (uint64_t)__ballot_sync(full, starts(lane)) | ((uint64_t)__ballot_sync(full, starts(lane + 32)) << 32);
+    auto leads = [&](int t) {
+      if (t >= a.rows) return false;
+      const int run_first = 63 - __clzll((long long)(smask & below(t)));
+      return (t - run_first) % kWalkRows == 0;
+    };
+    const uint64_t lmask = (uint64_t)__ballot_sync(full, leads(lane)) | ((uint64_t)__ballot_sync(full, leads(lane + 32)) << 32);
+    const int np = __popcll((long long)lmask);
+    s_k[lane] = 0;  // (scratch: each piece's need, before the pieces without one are dropped)
+    s_k[lane + 32] = 0;
+    __syncwarp();
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int t = lane + 32 * h;
+      if (t < a.rows) {
+        const int pc = __popcll((long long)(lmask & below(t))) - 1;
         const int b = s_bound[t];
-        if (b > a.topk) nd = max(nd, (b + kIdxChunk - 1) / kIdxChunk);
-      }
-      if (nd > 0) {
-        lead[pieces] = l;
-        span[pieces] = e - l;
-        need[pieces] = nd;
-        ++pieces;
+        if (b > a.topk) atomicMax(&s_k[pc], (b + kIdxChunk - 1) / kIdxChunk);
+        if ((lmask >> t) & 1) s_first[pc] = t;  // (scratch: the piece's first row)
       }
     }
+    __syncwarp();
+    // keep the pieces that need chunks, in order
+    int pl[2], ps[2], pn[2];
+    bool keep[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int pc = lane + 32 * h;
+      keep[h] = pc < np && s_k[pc] > 0;
+      pl[h] = pc < np ? s_first[pc] : 0;
+      ps[h] = pc < np ? (pc + 1 < np ? s_first[pc + 1] : a.rows) - pl[h] : 0;
+      pn[h] = pc < np ? s_k[pc] : 0;
+    }
+    const uint64_t kmask = (uint64_t)__ballot_sync(full, keep[0]) | ((uint64_t)__ballot_sync(full, keep[1]) << 32);
+    const int pieces = __popcll((long long)kmask);
+    __syncwarp();
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int pc = lane + 32 * h;
+      if (keep[h]) {
+        const int i = __popcll((long long)(kmask & ((1ull << pc) - 1)));
+        s_lead[i] = pl[h];
+        s_span[i] = ps[h];
+        s_need[i] = pn[h];
+      }
+    }
+    __syncwarp();
     if (pieces == 0 || pieces >= a.ctas) {
-      s_pieces = 0;
+      if (lane == 0) s_pieces = 0;
     } else {
-      long total = 0;
-      for (int i = 0; i < pieces; ++i) total += need[i];
+      // the smallest width (chunks a task) whose task count fits the CTAs, from the total's share
+      const int n0 = lane < pieces ? s_need[lane] : 0, n1 = lane + 32 < pieces ? s_need[lane + 32] : 0;
+      const long total = __reduce_add_sync(full, n0 + n1);
       int width = (int)max((total + a.ctas - 1) / a.ctas, 1L);
       for (;; ++width) {
-        long tasks = 0;
-        for (int i = 0; i < pieces; ++i) tasks += (need[i] + width - 1) / width;
+        const int tasks = __reduce_add_sync(full, (n0 + width - 1) / width + (n1 + width - 1) / width);
         if (tasks <= a.ctas) break;
       }
-      int r = 0;
-      for (int i = 0; i < pieces; ++i) {
-        s_lead[i] = lead[i];
-        s_span[i] = span[i];
-        s_need[i] = need[i];
-        s_first[i] = r;
-        s_k[i] = (need[i] + width - 1) / width;
-        r += s_k[i];
+      // tasks a piece and their first index (exclusive scan over pieces 0 .. 31, then 32 ..)
+      const int k0 = (n0 + width - 1) / width, k1 = (n1 + width - 1) / width;
+      int c0 = k0, c1 = k1;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int o0 = __shfl_up_sync(full, c0, d), o1 = __shfl_up_sync(full, c1, d);
+        if (lane >= d) {
+          c0 += o0;
+          c1 += o1;
+        }
       }
-      s_first[pieces] = r;
-      s_pieces = pieces;
+      const int tot0 = __shfl_sync(full, c0, 31);
+      if (lane < pieces) {
+        s_k[lane] = k0;
+        s_first[lane] = c0 - k0;
+      }
+      if (lane + 32 < pieces) {
+        s_k[lane + 32] = k1;
+        s_first[lane + 32] = tot0 + c1 - k1;
+      }
+      const int tot1 = __shfl_sync(full, c1, 31);
+      if (lane == 0) {
+        s_first[pieces] = tot0 + tot1;
+        s_pieces = pieces;
+      }
     }
   }
   __syncthreads();
