@@ -43,7 +43,11 @@ int dsv41_arch(void);
  * gathering each key tile's records into registers (default; "attn_pair" then chooses pair or
  * lone CTAs), or staging them in shared memory by bulk copies (lone CTAs); "attn_wide" 1/0
  * (DSV41_ATTN_WIDE) a row's 64 heads in one tcgen05 attention CTA (default when a rank holds 64
- * heads of 512 + 64 dims), or the 32-head kernels above. Takes effect at the
+ * heads of 512 + 64 dims), or the 32-head kernels above; "k2i_tc" 1/0 (DSV41_K2I_TC) K2i's scorer
+ * on tcgen05 block-scaled MMAs (default; needs q and kscale 16-byte aligned) or on mma.sync with
+ * the fp64 chunk epilogue, the same logits either way; "topk_cluster" 1/0 (DSV41_TOPK_CLUSTER)
+ * dsv41_topk rows of at least 2048 candidates over an 8-CTA cluster each (default) or one CTA a
+ * row, the same selection either way. Takes effect at the
  * next launch; DSV41_EINVAL for an unknown name or value. No counterpart in the reference (its variants are build keys). */
 int dsv41_set_option(const char* name, int64_t value);
 
