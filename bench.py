@@ -264,7 +264,7 @@ def run_ours(args, world, rank, local):
     from sgl_amd_mono_b200.deepseek_v41 import roofline, synth
     from sgl_amd_mono_b200.deepseek_v41.shapes import CONFIG2
     from sgl_amd_mono_b200.deepseek_v41.sm100a import abi
-    from sgl_amd_mono_b200.deepseek_v41.sm100a.runner import MonoRunner
+    from sgl_amd_mono_b200.deepseek_v41.sm100a.runner import MonoRunner, peer_cap
 
     from sgl_amd_mono_b200.common.peer import PeerBuffer
 
@@ -280,7 +280,7 @@ def run_ours(args, world, rank, local):
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
     sweep = sorted({int(x) for x in args.sweep.split(",") if x} | {args.rows})
-    peers = PeerBuffer(max(sweep) * shape.hidden, None, rank, world, dev) if tp > 1 else None
+    peers = PeerBuffer(peer_cap(shape, max(sweep)), None, rank, world, dev) if tp > 1 else None
     runner = MonoRunner(shape, dev, rank=rank, peers=peers)
     # every rank draws the same full layer and keeps its shard
     positions = max(args.ctx, 32768) + 8  # config 5's verify rows sit at positions up to 32767

@@ -153,8 +153,11 @@ typedef struct {
   int64_t gate_w, bias, w13, w13_codes, w2, w2_codes, sgu, sgu_codes, sw2, sw2_codes;
   /* outputs (xo, x8b, x8bs, attn_part, attn, logits: optional inspection copies) */
   int64_t out, ids, wts, xo, x8b, x8bs, attn_part, attn, logits, moe_part;
-  /* tensor parallelism */
-  int64_t peers, peer_cap, deadline_ns, phase, inject;
+  /* tensor parallelism (sink_all: the sinks of every rank's heads in rank order, float [tp * heads],
+   * or 0; with it, phase 0, the in-kernel exchanges, M >= tp and peer_cap >= ceil(M / tp) * heads *
+   * (nope + rope), each rank runs the attention of its ceil(M / tp) rows for all heads -- the rows'
+   * queries and outputs exchanged through the peer region -- instead of its heads for all rows) */
+  int64_t peers, peer_cap, deadline_ns, phase, inject, sink_all;
   /* optional host array of DSV41_K2_STAGES + 1 cudaEvent_t recorded at stage boundaries
    * (attention, wo_a + wo_b, all-reduce + FFN seam, router + routing, shared expert,
    * routed experts, combine + all-reduce); 0 = none */

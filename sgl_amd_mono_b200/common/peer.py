@@ -28,6 +28,8 @@ MAX_TP = 8
 GUARD_WORDS = 8
 W_SEQ, W_DONE, W_DEADLINE, W_PEER, W_FAULT = 0, 1, 3, 4, 5
 SITES = {1: "attention all-reduce", 2: "MoE all-reduce"}
+# every exchange a wait can give up in (the fault-injection hook takes SITES only)
+WAIT_SITES = {**SITES, 3: "row attention's query exchange", 4: "row attention's output exchange"}
 MIN_DEADLINE_S = 0.05
 
 
@@ -85,7 +87,7 @@ def guard_message(words: list[int]) -> Optional[str]:
     """The failure the guard words record, or None."""
     parts = []
     if words[W_DEADLINE]:
-        parts.append(f"a wait at the {SITES.get(words[W_DEADLINE], words[W_DEADLINE])} ran past its deadline")
+        parts.append(f"a wait at the {WAIT_SITES.get(words[W_DEADLINE], words[W_DEADLINE])} ran past its deadline")
     if words[W_PEER]:
         parts.append("a wait saw another rank's failure flag")
     if words[W_FAULT]:

@@ -120,7 +120,7 @@ def _build(model, hf_config, ctx) -> _Draft:
 
     from ..common.peer import PeerBuffer
     from .shapes import LayerShape
-    from .sm100a.runner import MonoRunner
+    from .sm100a.runner import MonoRunner, peer_cap
 
     p = get_parallel()
     s0 = model.stages[0]
@@ -131,7 +131,7 @@ def _build(model, hf_config, ctx) -> _Draft:
         experts=hf_config.dspark_n_routed_experts, topk=hf_config.dspark_num_experts_per_tok,
         inter=hf_config.moe_intermediate_size, shared_inter=hf_config.moe_intermediate_size, tp=p.tp_size)
     device = s0.input_layernorm.weight.device
-    peers = (PeerBuffer(target.MAX_ROWS * shape.hidden, p.tp_group.cpu_group, p.tp_rank, p.tp_size, device)
+    peers = (PeerBuffer(peer_cap(shape, target.MAX_ROWS), p.tp_group.cpu_group, p.tp_rank, p.tp_size, device)
              if p.tp_size > 1 else None)
     runner = MonoRunner(shape, device, ctx.copies, rank=p.tp_rank, peers=peers, group=p.tp_group.cpu_group,
                         deadline_s=ctx.deadline_s)

@@ -34,7 +34,7 @@ K2Args = struct("Dsv41K2Args", [
     "res_out", "post_out", "comb_out", "pre_out", "normed",
     "gate_w", "bias", "w13", "w13_codes", "w2", "w2_codes", "sgu", "sgu_codes", "sw2", "sw2_codes",
     "out", "ids", "wts", "xo", "x8b", "x8bs", "attn_part", "attn", "logits", "moe_part",
-    "peers", "peer_cap", "deadline_ns", "phase", "inject", "events",
+    "peers", "peer_cap", "deadline_ns", "phase", "inject", "sink_all", "events",
     "scratch", "scratch_bytes",
 ])
 K2_STAGES = ("attention", "wo_a+wo_b", "reduce+ffn seam", "router", "shared expert", "routed experts",

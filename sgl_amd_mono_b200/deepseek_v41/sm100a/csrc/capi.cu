@@ -93,10 +93,11 @@ Option g_options[] = {
     {"attn_wide", "DSV41_ATTN_WIDE", 1, {0}, {false}},
     {"k2i_tc", "DSV41_K2I_TC", 1, {0}, {false}},
     {"topk_cluster", "DSV41_TOPK_CLUSTER", 1, {0}, {false}},
+    {"row_attn", "DSV41_ROW_ATTN", 1, {0}, {false}},
 };
 enum {
   kOptAttnTc, kOptAttnPair, kOptDenseMinM, kOptPdl, kOptAttnBulk, kOptFusedAr, kOptK1Persistent, kOptAttnWide,
-  kOptK2iTc, kOptTopkCluster
+  kOptK2iTc, kOptTopkCluster, kOptRowAttn
 };
 
 int64_t option(int i) {
@@ -134,6 +135,10 @@ bool use_k2i_tc() { return option(kOptK2iTc) == 1; }
 // Top-k rows of at least kTopkClMinCands candidates over a cluster of 8 CTAs each
 // (topk_cluster_kernel, 1, default) or one CTA a row (topk_kernel, 0; DSV41_TOPK_CLUSTER=0).
 bool use_topk_cluster() { return option(kOptTopkCluster) == 1; }
+// TP > 1: each rank attends its share of the rows for all heads, the rows' queries and outputs
+// exchanged in-kernel (1, default, when the caller passes every head's sinks), or its own heads for
+// every row over the replicated KV cache (0; DSV41_ROW_ATTN=0).
+bool use_row_attn() { return option(kOptRowAttn) == 1; }
 // TP > 1: both all-reduces fused into the kernels that produce the partials (wo_b's epilogue, the
 // MoE combine) as LL peer stores (1, default), or the standalone exchange kernel after each (0;
 // DSV41_FUSED_AR=0).
@@ -549,12 +554,18 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   const int P = M * TK, keys = (int)a->keys_ld;
   const int sms = sm_count();
   Carver c{go ? ptr<uint8_t>(a->scratch) : nullptr};
+  // row-parallel attention (TP > 1): this rank's rows [row0, row0 + Mr) for all Ha heads
+  const int tpn = (int)a->tp, mr = cdiv(M, tpn);
+  const bool rowattn = tpn > 1 && a->phase == 0 && a->sink_all != 0 && use_row_attn() && use_fused_allreduce() &&
+                       M >= tpn && (int64_t)mr * heads * D <= a->peer_cap;
+  const int Ma = rowattn ? mr : M, Ha = rowattn ? heads * tpn : heads;
+  const int row0 = rowattn ? (int)a->rank * mr : 0, Mr = rowattn ? std::min(M, row0 + mr) - row0 : M;
   // attention split plan: the tcgen05 kernel takes every head of a row (one CTA an SM in
   // total), the mma.sync kernel 16-head tiles (two CTAs an SM)
   const bool tc = use_tc_attention() && (nope == 512 || nope == 448);
-  const bool wide = tc && nope == 512 && heads == kWdNH && use_attn_wide();
-  const int head_tiles = wide ? 1 : tc ? cdiv(heads, 32) : cdiv(heads, 16);
-  const int units = M * head_tiles;
+  const bool wide = tc && nope == 512 && Ha == kWdNH && use_attn_wide();
+  const int head_tiles = wide ? 1 : tc ? cdiv(Ha, 32) : cdiv(Ha, 16);
+  const int units = Ma * head_tiles;
   int nchunks = cdiv(2 * sms, units);
   const int sub = tc ? kTcKeys : kSub;  // keys a sub-block
   if (tc) {
@@ -569,9 +580,12 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   nchunks = std::max(1, std::min(nchunks, cdiv(keys, sub)));
   const int chunk_keys = cdiv(cdiv(keys, nchunks), sub) * sub;
   nchunks = cdiv(keys, chunk_keys);
-  auto* part_o = c.take<float>((int64_t)M * nchunks * heads * D);
-  auto* part_ml = c.take<float>((int64_t)M * nchunks * heads * 2);
+  auto* part_o = c.take<float>((int64_t)Ma * nchunks * Ha * D);
+  auto* part_ml = c.take<float>((int64_t)Ma * nchunks * Ha * 2);
   auto* xo = a->xo ? ptr<__nv_bfloat16>(a->xo) : c.take<__nv_bfloat16>((int64_t)M * heads * D);
+  // row-parallel attention: this rank's rows' queries and outputs for every head
+  auto* q_all = rowattn ? c.take<__nv_bfloat16>((int64_t)Ma * Ha * D) : nullptr;
+  auto* xo_rows = rowattn ? c.take<__nv_bfloat16>((int64_t)Ma * Ha * D) : nullptr;
   const int gk = heads / G * D;  // wo_a's K a group
   GemvArgs ga = gemv_plan(ptr<const uint8_t>(a->woa), ptr<const uint8_t>(a->woa_codes), xo, nullptr,
                           M, G * O, gk, heads * D, O, sms);
@@ -652,24 +666,31 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
   const int xgrid = std::min(grid_for((int64_t)M * H / 8, 256), 4 * sms);
   if (phase != 2) {
   // ---- attention
+  mark(a->events, 0, st);
+  const int a2a_grid = std::min(grid_for((int64_t)mr * heads * D / 8, 256), 4 * sms);
+  if (rowattn) {
+    // the rows' queries of every rank's heads (exchange site 3)
+    A2AArgs qa = {0, M, mr, heads, D, ptr<const __nv_bfloat16>(a->q), q_all};
+    DSV41_TRY(launch2(ll_a2a_kernel, dim3(a2a_grid), dim3(256), 0, st, exchange(3, nullptr), qa));
+  }
   AttnArgs at = {};
-  at.M = M; at.heads = heads; at.D = D; at.nope = nope; at.rope = rope; at.keys_ld = keys;
+  at.M = Mr; at.heads = Ha; at.D = D; at.nope = nope; at.rope = rope; at.keys_ld = keys;
   at.nchunks = nchunks; at.chunk_keys = chunk_keys; at.head_tiles = head_tiles;
-  at.q = ptr<const __nv_bfloat16>(a->q); at.kt = ptr<const int32_t>(a->kt); at.klen = ptr<const int32_t>(a->klen);
+  at.q = rowattn ? q_all : ptr<const __nv_bfloat16>(a->q);
+  at.kt = ptr<const int32_t>(a->kt) + (int64_t)row0 * keys; at.klen = ptr<const int32_t>(a->klen) + row0;
   at.swa = ptr<const uint8_t>(a->swa); at.swa_stride = a->swa_stride; at.swa_blk = (int)a->swa_blk;
   at.comp = ptr<const uint8_t>(a->comp); at.comp_stride = a->comp_stride; at.comp_blk = (int)(a->comp_blk ? a->comp_blk : 1);
   at.scale_log2 = (float)(1.0 / sqrt((double)D) * 1.4426950408889634);
   at.part_o = part_o; at.part_ml = part_ml;
-  mark(a->events, 0, st);
   if (wide) {
-    DSV41_TRY(launch(attn_wide_kernel<512>, dim3(M * nchunks), dim3(kWdThreads), WdSmem<576>::kBytes, st, at));
+    DSV41_TRY(launch(attn_wide_kernel<512>, dim3(Mr * nchunks), dim3(kWdThreads), WdSmem<576>::kBytes, st, at));
   } else if (tc) {
-    AttnTcArgs ta = {at, heads >= 32 ? 32 : std::max(16, cdiv(heads, 16) * 16), head_tiles};
+    AttnTcArgs ta = {at, Ha >= 32 ? 32 : std::max(16, cdiv(Ha, 16) * 16), head_tiles};
     // the staged producer (lone CTAs), or a row's two head tiles sharing their key tiles as a
     // CTA pair, or lone gathering CTAs
     const bool bulk = use_attn_bulk();
     const bool pair = !bulk && head_tiles == 2 && use_attn_pair();
-    const dim3 grid(M * nchunks * head_tiles), block(kTcThreads);
+    const dim3 grid(Mr * nchunks * head_tiles), block(kTcThreads);
     using S576 = TcSmem<576, kTcBulkStages, kTcStaging>;
     using S512 = TcSmem<512, kTcBulkStages, kTcStaging>;
     if (nope == 512)
@@ -681,16 +702,23 @@ int k2_run(const Dsv41K2Args* a, cudaStream_t st, bool go, int64_t* need) {
                 : pair ? launch(attn_tc_kernel<448, true>, grid, block, TcSmem<512>::kBytes, st, ta, 2)
                        : launch(attn_tc_kernel<448, false>, grid, block, TcSmem<512>::kBytes, st, ta));
   } else {
-    DSV41_TRY(launch(attn_split_kernel, dim3(M * nchunks * head_tiles), dim3(256), attn_smem_bytes(D), st, at));
+    DSV41_TRY(launch(attn_split_kernel, dim3(Mr * nchunks * head_tiles), dim3(256), attn_smem_bytes(D), st, at));
   }
   CombineArgs cb = {};
-  cb.M = M; cb.heads = heads; cb.D = D; cb.nope = nope; cb.rope = rope; cb.nchunks = nchunks;
-  cb.part_o = part_o; cb.part_ml = part_ml; cb.sink = ptr<const float>(a->sink);
-  cb.cos_sin = ptr<const float>(a->cos_sin); cb.pos = ptr<const int64_t>(a->pos); cb.xo = xo;
+  cb.M = Mr; cb.heads = Ha; cb.D = D; cb.nope = nope; cb.rope = rope; cb.nchunks = nchunks;
+  cb.part_o = part_o; cb.part_ml = part_ml;
+  cb.sink = ptr<const float>(rowattn ? a->sink_all : a->sink);
+  cb.cos_sin = ptr<const float>(a->cos_sin); cb.pos = ptr<const int64_t>(a->pos) + row0;
+  cb.xo = rowattn ? xo_rows : xo;
   cb.rope_rows = a->rope_rows;
-  DSV41_TRY(nchunks > 16 && M * heads <= sms
-                ? launch(attn_combine_kernel<32>, dim3(M * heads), dim3(kCombineThreads), nchunks * 8, st, cb)
-                : launch(attn_combine_kernel<16>, dim3(M * heads), dim3(kCombineThreads), nchunks * 8, st, cb));
+  DSV41_TRY(nchunks > 16 && Mr * Ha <= sms
+                ? launch(attn_combine_kernel<32>, dim3(Mr * Ha), dim3(kCombineThreads), nchunks * 8, st, cb)
+                : launch(attn_combine_kernel<16>, dim3(Mr * Ha), dim3(kCombineThreads), nchunks * 8, st, cb));
+  if (rowattn) {
+    // every row's output for this rank's heads (exchange site 4)
+    A2AArgs oa = {1, M, mr, heads, D, xo_rows, xo};
+    DSV41_TRY(launch2(ll_a2a_kernel, dim3(a2a_grid), dim3(256), 0, st, exchange(4, nullptr), oa));
+  }
   // ---- wo_a -> X8B -> wo_b -> partial -> reduce
   mark(a->events, 1, st);
   DSV41_TRY(gemv_go(ga, st));

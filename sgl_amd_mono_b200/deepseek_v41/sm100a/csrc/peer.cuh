@@ -315,6 +315,101 @@ __global__ void __launch_bounds__(256) allreduce_ll_kernel(const PeerLL x, const
   pdl_launch();
 }
 
+// ------------------------------------------------------------------ row-parallel attention's exchanges
+// With rows split over the ranks (rank r owns rows [r mr, min(M, (r + 1) mr))), every rank runs the
+// attention of its rows for all heads. Two all-to-alls of bf16 blocks (one row's hl x D values of
+// one rank's hl heads) over the LL slots carry what it needs:
+//   mode 0 (queries): rank s sends peer p, for each of p's rows i, src[p mr + i][0 .. hl)[D] (its
+//     heads' queries); p stores it at dst[i][s hl .. (s + 1) hl)[D] (all heads, rank-major);
+//   mode 1 (outputs): rank s sends peer p, for each of its own rows i, src[i][p hl .. (p + 1) hl)[D];
+//     p stores it at dst[s mr + i][0 .. hl)[D] (every row, its own heads).
+// Block i from rank s is slot [e & 1][s] of the receiver at 8-value group i hl D / 8. Each thread
+// pushes all its groups before it waits for any. Every rank must own at least one row (M >= tp):
+// then every exchange waits on every rank, which keeps the slot parity reuse safe.
+struct A2AArgs {
+  int mode, M, mr, hl, D;
+  const __nv_bfloat16* src;
+  __nv_bfloat16* dst;
+};
+
+// Rank src's group i8 of this exchange from this rank's region, once its epoch is e (the waits and
+// failure handling of ll_reduce).
+__device__ inline bool ll_fetch(const PeerLL& x, uint32_t e, int src, int64_t i8, uint32_t (&o)[4]) {
+  const int par = (int)(e & 1u);
+  const int64_t me = x.peers[x.rank];
+  const uint64_t* p = ll_slot(me, par, x.tp, src, x.cap) + 4 * i8;
+  uint64_t v[4];
+  uint64_t t0 = 0;
+  for (uint32_t it = 1;; ++it) {
+    ld_ll2(p, v[0], v[1]);
+    ld_ll2(p + 2, v[2], v[3]);
+    if ((uint32_t)(v[0] >> 32) == e && (uint32_t)(v[1] >> 32) == e && (uint32_t)(v[2] >> 32) == e &&
+        (uint32_t)(v[3] >> 32) == e)
+      break;
+    if ((it & 63) != 0) continue;
+    bool failed = false;
+    for (int q = 0; q < x.tp; ++q)
+      if (q != x.rank) failed |= ld_acquire_sys(peer_words(me + kFailOff) + q) != 0;
+    if (failed) {
+      atomicExch(peer_words(me) + kErrPeer, 1u);
+      return false;
+    }
+    if (ld_acquire_sys(peer_words(me + kFailOff) + x.rank) != 0) return false;
+    const uint64_t now = global_ns();
+    if (t0 == 0) {
+      t0 = now;
+    } else if (now - t0 > (uint64_t)x.deadline_ns || it == 0xffffffc0u) {
+      atomicCAS(peer_words(me) + kErrDeadline, 0u, (uint32_t)x.site);
+      for (int q = 0; q < x.tp; ++q) st_release_sys(peer_words(x.peers[q] + kFailOff) + x.rank, 1u);
+      return false;
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) o[q] = (uint32_t)v[q];
+  return true;
+}
+
+__global__ void __launch_bounds__(256) ll_a2a_kernel(const PeerLL x, const A2AArgs a) {
+  pdl_wait();
+  int fail = 0;
+  const uint32_t e = ll_begin(x, &fail);
+  const int par = (int)(e & 1u);
+  const int G = a.hl * a.D / 8;  // 8-value groups a block
+  auto rows_of = [&](int r) { return max(0, min(a.M, (r + 1) * a.mr) - r * a.mr); };
+  const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, nthr = (int64_t)gridDim.x * blockDim.x;
+  const int hall = x.tp * a.hl;
+  if (!fail) {
+    for (int p = 0; p < x.tp; ++p) {
+      const int64_t total = (int64_t)(a.mode == 0 ? rows_of(p) : rows_of(x.rank)) * G;
+      uint64_t* slot = ll_slot(x.peers[p], par, x.tp, x.rank, x.cap);
+      for (int64_t q = t0; q < total; q += nthr) {
+        const int i = (int)(q / G), g = (int)(q % G);
+        const __nv_bfloat16* s = a.mode == 0 ? a.src + ((size_t)(p * a.mr + i) * a.hl) * a.D + 8 * g
+                                             : a.src + ((size_t)i * hall + p * a.hl) * a.D + 8 * g;
+        const uint4 v = *reinterpret_cast<const uint4*>(s);
+        st_ll2(slot + 4 * q, v.x, v.y, e);
+        st_ll2(slot + 4 * q + 2, v.z, v.w, e);
+      }
+    }
+    for (int s = 0; s < x.tp && !fail; ++s) {
+      const int64_t total = (int64_t)(a.mode == 0 ? rows_of(x.rank) : rows_of(s)) * G;
+      for (int64_t q = t0; q < total; q += nthr) {
+        const int i = (int)(q / G), g = (int)(q % G);
+        uint32_t o[4];
+        if (!ll_fetch(x, e, s, q, o)) {
+          fail = 1;
+          break;
+        }
+        __nv_bfloat16* d = a.mode == 0 ? a.dst + ((size_t)i * hall + s * a.hl) * a.D + 8 * g
+                                       : a.dst + ((size_t)(s * a.mr + i) * a.hl) * a.D + 8 * g;
+        *reinterpret_cast<uint4*>(d) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+  ll_end(x, e);
+  pdl_launch();
+}
+
 // out = bf16(sum over ranks in rank order of parts[r]), fp32 accumulation: the reduction step
 // of the NCCL variant (an all-gather of the partials, then this), bit-identical to the
 // in-kernel exchange.

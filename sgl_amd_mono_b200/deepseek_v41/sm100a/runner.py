@@ -56,6 +56,13 @@ class Layer:
         return self.r[k] if k in self.r else self.w[k]
 
 
+def peer_cap(shape: LayerShape, rows: int) -> int:
+    """bf16 elements a PeerBuffer slot needs for launches of up to ``rows`` rows: the all-reduces'
+    rows x hidden, and the row-parallel attention's exchanges (ceil(rows / tp) rows x this rank's
+    heads x head_dim)."""
+    return max(rows * shape.hidden, -(-rows // max(shape.tp, 1)) * shape.heads_local * shape.head_dim)
+
+
 class MonoRunner:
     MAX_ROWS = 48
 
@@ -112,6 +119,17 @@ class MonoRunner:
             ext.call("dsv41_relayout_mxfp4", a, _stream())
             r[name], r[name + "_codes"] = dst, dcodes
             self.copies[("mxfp4 tensor-core tile relayout", tag, name)] = (dst, dcodes)
+        if s.tp > 1 and self.allreduce == "peer":
+            # every rank's head sinks in rank order, for the row-parallel attention (each rank
+            # attends its rows for all heads); a collective over the ranks, once a bound layer
+            if dist.is_initialized() and dist.get_world_size(self.group) == s.tp:
+                src = w["sink"].contiguous()
+                if dist.get_backend(self.group) == "gloo":
+                    src = src.cpu()
+                parts = [torch.empty_like(src) for _ in range(s.tp)]
+                dist.all_gather(parts, src, group=self.group)
+                r["sink_all"] = torch.cat(parts).to(d)
+                self.copies[("every rank's attention sinks", tag, "sink_all")] = (r["sink_all"],)
         return Layer(w, r)
 
     # ------------------------------------------------------------ buffers
@@ -215,7 +233,8 @@ class MonoRunner:
             keys_ld=b["kt"].shape[1],
             q=_p(b["q"]), kt=_p(b["kt"]), klen=_p(b["klen"]), swa=_p(step["cache"]),
             swa_stride=step["page_stride"], swa_blk=step["blk"], comp=_p(comp), comp_stride=comp_stride,
-            comp_blk=comp_blk, sink=_p(w["sink"]), cos_sin=_p(w["cos_sin"]), pos=_p(step["pos"]),
+            comp_blk=comp_blk, sink=_p(w["sink"]), sink_all=_p(L.r.get("sink_all")),
+            cos_sin=_p(w["cos_sin"]), pos=_p(step["pos"]),
             rope_rows=w["cos_sin"].shape[0],
             woa=_p(w["woa"]), woa_codes=_p(w["woa_s"]), wob=_p(w["wob"]), wob_codes=_p(w["wob_s"]),
             res_in=_p(b["res1"]), post_in=_p(b["post_a"]), comb_in=_p(b["comb_a"]), pre_in=_p(b["pre_a"]),

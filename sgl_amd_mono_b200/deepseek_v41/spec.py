@@ -441,7 +441,7 @@ def _build(model, hf_config, ctx) -> _Built:
     from ..common.peer import PeerBuffer
     from .shapes import LayerShape
     from .sm100a.indexer import K2iRunner
-    from .sm100a.runner import MonoRunner
+    from .sm100a.runner import MonoRunner, peer_cap
 
     p = get_parallel()
     layers0 = model.model.layers
@@ -456,7 +456,7 @@ def _build(model, hf_config, ctx) -> _Built:
         tp=p.tp_size)
     device = layers0[covered[0]].input_layernorm.weight.device
     # the peer handshake is collective: every rank gets here (attach agreed first)
-    peers = (PeerBuffer(MAX_ROWS * shape.hidden, p.tp_group.cpu_group, p.tp_rank, p.tp_size, device)
+    peers = (PeerBuffer(peer_cap(shape, MAX_ROWS), p.tp_group.cpu_group, p.tp_rank, p.tp_size, device)
              if p.tp_size > 1 else None)
     runner = MonoRunner(shape, device, ctx.copies, rank=p.tp_rank, peers=peers, group=p.tp_group.cpu_group,
                         deadline_s=ctx.deadline_s)

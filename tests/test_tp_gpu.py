@@ -234,18 +234,23 @@ def _tp_worker(rank, world, port, q, inject):
     from sgl_amd_mono_b200.common.peer import DeviceGuardError, PeerBuffer
     from sgl_amd_mono_b200.deepseek_v41 import synth
     from sgl_amd_mono_b200.deepseek_v41.shapes import LayerShape
-    from sgl_amd_mono_b200.deepseek_v41.sm100a.runner import MonoRunner
+    from sgl_amd_mono_b200.deepseek_v41.sm100a.runner import MonoRunner, peer_cap
     s = LayerShape(**SMALL_TP).sharded(world)
-    peers = PeerBuffer(M_ROWS * s.hidden, None, rank, world, dev)
+    peers = PeerBuffer(peer_cap(s, M_ROWS), None, rank, world, dev)
     # drawn on the CPU (the oracle's generator), then moved
     w = {k: (v.to(dev) if torch.is_tensor(v) else v)
          for k, v in synth.make_layer(s, 31, "cpu", positions=CTX + 8, rank=rank).items()}
     S = {k: (v.to(dev) if torch.is_tensor(v) else v) for k, v in synth.make_step(s, M_ROWS, CTX, 32, "cpu").items()}
+    from sgl_amd_mono_b200.common import ext
     res = {"error": None}
-    for mode in ("peer", "nccl"):
+    # peer: row-parallel attention (each rank attends its rows for all heads); peer_heads: each rank
+    # its heads for every row; nccl: the same split as peer_heads, the all-reduces through NCCL
+    for mode in ("peer", "peer_heads", "nccl"):
         dist.barrier()
         try:
-            rn = MonoRunner(s, dev, rank=rank, peers=peers, allreduce=mode, deadline_s=0.5 if inject else 5.0)
+            ext.set_option("row_attn", 0 if mode == "peer_heads" else 1)
+            rn = MonoRunner(s, dev, rank=rank, peers=peers, allreduce="nccl" if mode == "nccl" else "peer",
+                            deadline_s=0.5 if inject else 5.0)
             L = rn.bind(w)
             step = dict(S, cache=S["cache"].clone())
             torch.cuda.synchronize()
@@ -301,10 +306,16 @@ def test_k2_tp2_in_kernel_allreduce_two_gpus():
     assert not any(g["error"] for g in got), [g["error"] for g in got]
     r0, r1 = got[0], got[1]
     for k in ("out", "attn", "ids"):
-        assert np.array_equal(r0["peer"][k], r0["nccl"][k]), k  # both variants: the same bits
-        assert np.array_equal(r0["peer"][k], r1["peer"][k]), k  # every rank: the same result
-    parts = [torch.from_numpy(r["peer"]["attn_part"]).to(torch.bfloat16) for r in got]
-    assert np.array_equal(OL.all_reduce(parts).float().numpy(), r0["peer"]["attn"])
+        assert np.array_equal(r0["peer_heads"][k], r0["nccl"][k]), k  # both exchanges: the same bits
+        for mode in ("peer", "peer_heads"):
+            assert np.array_equal(r0[mode][k], r1[mode][k]), (mode, k)  # every rank: the same result
+    for mode in ("peer", "peer_heads"):
+        parts = [torch.from_numpy(r[mode]["attn_part"]).to(torch.bfloat16) for r in got]
+        assert np.array_equal(OL.all_reduce(parts).float().numpy(), r0[mode]["attn"]), mode
+    # the row split attends with other kernels / chunkings than the head split: close, same routing
+    assert np.array_equal(r0["peer"]["ids"], r0["peer_heads"]["ids"])
+    a, b = r0["peer"]["attn"], r0["peer_heads"]["attn"]
+    assert np.linalg.norm(a - b) / np.linalg.norm(b) < 1e-2
     # the oracle over both ranks' shards
     s = LayerShape(**SMALL_TP).sharded(2)
     ws = [synth.make_layer(s, 31, "cpu", positions=CTX + 8, rank=r) for r in range(2)]
