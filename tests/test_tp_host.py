@@ -159,6 +159,34 @@ def test_guard_messages():
     assert "MoE all-reduce" in m and "failure flag" in m and "fault-injection" in m
 
 
+def test_guard_messages_name_the_row_attention_exchanges():
+    w = [0] * 8
+    w[P.W_DEADLINE] = 3
+    assert "query exchange" in P.guard_message(w)
+    w[P.W_DEADLINE] = 4
+    assert "output exchange" in P.guard_message(w)
+
+
+
+def test_fault_injection_takes_the_all_reduce_sites_only(monkeypatch):
+    monkeypatch.setenv("SGLANG_AMD_MONO_FAULT_INJECT", "0:3")
+    with pytest.raises(ValueError):
+        P.fault_injection(0)
+
+
+def test_peer_cap_covers_both_exchange_kinds():
+    """A slot holds rows x hidden (the all-reduces) and ceil(rows / tp) x local heads x head_dim
+    (the row-parallel attention's all-to-alls); K2 falls back to the head split when it cannot."""
+    from sgl_amd_mono_b200.deepseek_v41.shapes import CONFIG2
+    from sgl_amd_mono_b200.deepseek_v41.sm100a.runner import peer_cap
+    for tp in (2, 4, 8):
+        s = CONFIG2.sharded(tp)
+        for rows in (1, 4, 7, 16, 48):
+            c = peer_cap(s, rows)
+            assert c >= rows * s.hidden
+            assert c >= -(-rows // tp) * s.heads_local * s.head_dim
+
+
 def test_runner_refuses_tp_without_peers():
     from sgl_amd_mono_b200.deepseek_v41.shapes import CONFIG2
     from sgl_amd_mono_b200.deepseek_v41.sm100a.runner import MonoRunner
