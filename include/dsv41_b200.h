@@ -47,7 +47,9 @@ int dsv41_arch(void);
  * on tcgen05 block-scaled MMAs (default; needs q and kscale 16-byte aligned) or on mma.sync with
  * the fp64 chunk epilogue, the same logits either way; "topk_cluster" 1/0 (DSV41_TOPK_CLUSTER)
  * dsv41_topk rows of at least 2048 candidates over an 8-CTA cluster each (default) or one CTA a
- * row, the same selection either way. Takes effect at the
+ * row, the same selection either way; "row_attn" 1/0 (DSV41_ROW_ATTN) at TP > 1 each rank attends
+ * ceil(M / tp) rows for all heads (default; needs sink_all, M >= tp and the peer capacity) or its
+ * own heads for every row. Takes effect at the
  * next launch; DSV41_EINVAL for an unknown name or value. No counterpart in the reference (its variants are build keys). */
 int dsv41_set_option(const char* name, int64_t value);
 
